@@ -1,0 +1,161 @@
+/*
+ * lmoe.h - C ABI of liblmoe.so, the sm_100a routed-MoE kernels that replace
+ * Locali's kernel module and MLX gather_qmm on the expert hot path.
+ *
+ * Every entry point takes raw device pointers, plain sizes, a caller-owned
+ * workspace and a cudaStream_t (passed as void*), enqueues its kernels on that
+ * stream and returns an int status (LMOE_OK = 0, negative on error).  None of
+ * them allocates device memory or synchronises the host; all of them are safe
+ * to enqueue while a stream is being captured into a CUDA graph, once the
+ * workspace has been initialised by lmoe_workspace_init().
+ *
+ * Arena layout (unchanged from the reference, arena.py:150-160 and
+ * dsv4_index.py:111-124): per projection, three stacked arrays indexed by
+ * arena slot -- weight uint32 [n_slots, rows, cols*bits/32] (codes LSB-first,
+ * dsv4_kernels.py:135-150), scales and biases [n_slots, rows, cols/group] in
+ * the activation dtype.  Slot 0 is reserved as all zeros (arena.py:123-126).
+ *
+ * Error convention follows native/locali_core.c (-1 bad argument, -3 bad
+ * key): see the LMOE_E* codes below.
+ */
+#ifndef LMOE_H
+#define LMOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LMOE_ABI_VERSION 1
+
+/* status codes */
+#define LMOE_OK 0
+#define LMOE_EINVAL (-1)        /* null pointer or inconsistent sizes            */
+#define LMOE_EUNSUPPORTED (-2)  /* geometry / bits / group size not compiled     */
+#define LMOE_EINDEX (-3)        /* expert id or arena slot out of range (device) */
+#define LMOE_ECUDA (-4)         /* CUDA launch or runtime error                  */
+#define LMOE_EWORKSPACE (-5)    /* workspace too small                           */
+
+/* activation / scale dtype */
+#define LMOE_BF16 0
+#define LMOE_F16 1
+
+/* router scoring functions (arena.py:502 is sigmoid; the V4 gate also uses
+ * sqrtsoftplus, tests/test_dsv4_engine_small.py:59) */
+#define LMOE_SCORE_SIGMOID 0
+#define LMOE_SCORE_SOFTMAX 1
+#define LMOE_SCORE_SQRTSOFTPLUS 2
+
+/* SwiGLU rounding: FUSED = one rounding of silu_f32(gate)*up
+ * (dsv4_kernels.py:165-170, dsv4_arena.py:228-232); STOCK = MLX
+ * nn.silu(gate)*up op by op in the activation dtype (dsv4_arena.py:234). */
+#define LMOE_SWIGLU_FUSED 0
+#define LMOE_SWIGLU_STOCK 1
+
+/* One quantized projection for all arena slots. */
+typedef struct lmoe_qproj {
+    const uint32_t *weight; /* [n_slots, rows, cols*bits/32] */
+    const void *scales;     /* [n_slots, rows, cols/group_size] */
+    const void *biases;     /* [n_slots, rows, cols/group_size] */
+    int32_t bits;           /* 2, 4 or 8 */
+    int32_t group_size;     /* 64 or 128 (32 for 4- and 8-bit) */
+} lmoe_qproj;
+
+/* The routed experts of one tier: SwitchGLU gate/up [inter, hidden] and
+ * down [hidden, inter] (dsv4_arena.py:168-235). */
+typedef struct lmoe_experts {
+    int32_t n_slots;
+    int32_t hidden;
+    int32_t inter;
+    int32_t dtype; /* LMOE_BF16 or LMOE_F16 */
+    lmoe_qproj gate;
+    lmoe_qproj up;
+    lmoe_qproj down;
+} lmoe_experts;
+
+/* V4 router (arena.py:501-506 + routed scaling). weight bf16 [E, hidden]. */
+typedef struct lmoe_router {
+    const void *weight;
+    const float *bias; /* [E] selection-only bias, or NULL */
+    int32_t n_experts;
+    int32_t top_k;
+    int32_t scoring;
+    int32_t norm_topk;
+    float routed_scaling;
+} lmoe_router;
+
+typedef struct lmoe_layer {
+    lmoe_router router;
+    lmoe_experts experts;
+    const int32_t *expert_slot; /* [E] device: arena slot of each expert */
+    float swiglu_limit;         /* <= 0 disables the clamp */
+    int32_t swiglu_mode;        /* LMOE_SWIGLU_* */
+} lmoe_layer;
+
+/* ABI version and error text. */
+int lmoe_version(void);
+const char *lmoe_strerror(int status);
+
+/* Bytes of workspace needed for up to max_tokens tokens of this layer. */
+size_t lmoe_workspace_size(const lmoe_layer *layer, int32_t max_tokens);
+
+/* Zero a fresh workspace (once; kernels leave it reusable afterwards). */
+int lmoe_workspace_init(void *workspace, size_t bytes, void *stream);
+
+/* Device error flag raised by kernels (bad expert id / slot); reading it
+ * synchronises the stream, then clears the flag.  Returns LMOE_OK or
+ * LMOE_EINDEX. */
+int lmoe_workspace_status(void *workspace, void *stream);
+
+/* Router only: replaces the V4 MoEGate call at dsv4_arena.py:165-166
+ * (arena.py:501-506).  x [T, hidden] activations; idx [T, top_k] int32
+ * (ordered by biased score, ties to the lower id); w [T, top_k] fp32
+ * combine weights (already multiplied by routed_scaling). */
+int lmoe_route(const lmoe_layer *layer, const void *x, int32_t tokens,
+               int32_t *idx, float *w, void *workspace, size_t ws_bytes,
+               void *stream);
+
+/* Whole routed-MoE layer: ArenaMoE.__call__ single-tier path
+ * (arena.py:508-547, _apply :569-624, V4 _gather dsv4_arena.py:168-235):
+ * router -> dispatch -> fused gate/up + clamped SwiGLU -> down + weighted
+ * combine.  out [T, hidden] in the activation dtype.  idx/w may be NULL;
+ * when given they receive the routing. */
+int lmoe_moe_layer(const lmoe_layer *layer, const void *x, int32_t tokens,
+                   void *out, int32_t *idx, float *w, void *workspace,
+                   size_t ws_bytes, void *stream);
+
+/* Same layer with routing supplied by the caller (an external gate, as
+ * V4ArenaMoE.route returns it): idx [T, top_k] expert ids, w [T, top_k]
+ * fp32 weights (arena.py:512-546). */
+int lmoe_moe_routed(const lmoe_layer *layer, const void *x, int32_t tokens,
+                    const int32_t *idx, const float *w, void *out,
+                    void *workspace, size_t ws_bytes, void *stream);
+
+/* Fused gate/up products + clamped SwiGLU over arena slots: replaces
+ * fused_affine2_swiglu (dsv4_kernels.py:246-300) for 2/4/8-bit and any batch.
+ * x [T, hidden]; slots [T, top_k] uint32 arena slots (gather_qmm
+ * rhs_indices); h [T*top_k, inter] activations (route r = t*top_k + j). */
+int lmoe_gateup_swiglu(const lmoe_experts *experts, const void *x,
+                       int32_t tokens, int32_t top_k, const uint32_t *slots,
+                       float limit, int32_t swiglu_mode, void *h,
+                       void *workspace, size_t ws_bytes, void *stream);
+
+/* mx.gather_qmm(x, w, s, b, rhs_indices=slots, transpose=True) for one
+ * projection (dsv4_arena.py:198-221, arena.py:676-681).  x [routes, cols]
+ * (one input row per route); slots [routes]; y [routes, rows]. */
+int lmoe_gather_qmm(const lmoe_qproj *proj, int32_t n_slots, int32_t rows,
+                    int32_t cols, int32_t dtype, const void *x,
+                    int32_t routes, const uint32_t *slots, void *y,
+                    void *workspace, size_t ws_bytes, void *stream);
+
+/* Workspace bytes for lmoe_gateup_swiglu / lmoe_gather_qmm calls. */
+size_t lmoe_workspace_size_routes(int32_t max_routes, int32_t hidden,
+                                  int32_t inter, int32_t n_slots);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LMOE_H */

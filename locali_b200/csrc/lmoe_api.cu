@@ -1,0 +1,450 @@
+// C ABI of liblmoe.so (declared in include/lmoe.h).  Host-side validation,
+// workspace layout and kernel sequencing; no allocation, no host sync.
+#include <cstring>
+
+#include "../../include/lmoe.h"
+#include "lmoe_kernels.cuh"
+
+using namespace lmoe;
+
+namespace {
+
+bool gemv_ok(int bits, int gs) {
+    return (bits == 2 && (gs == 64 || gs == 128)) ||
+           ((bits == 4 || bits == 8) && (gs == 32 || gs == 64 || gs == 128));
+}
+
+size_t al(size_t v) { return (v + 255) & ~size_t(255); }
+
+struct Layout {
+    size_t status = 0, partial = 0, idx = 0, w = 0, sorted = 0, counts = 0, roff = 0,
+           nchunks = 0, chunks = 0, xpanel = 0, xsum = 0, hpanel = 0, hsum = 0, yw = 0,
+           cnt = 0, total = 0;
+    int max_chunks = 0;
+};
+
+int max_chunks_for(int buckets, int R) {
+    const int distinct = buckets < R ? buckets : R;
+    return distinct + R / kChunkTok + 1;
+}
+
+// Layout shared by all entry points.  x_rows: rows of the input panel;
+// R: routes; K: input width; I: intermediate width (0 if unused);
+// H_out: output width of the combine (0 if unused); T: tokens.
+Layout make_layout(int T, int R, int K, int I, int H_out, int buckets, int E_router,
+                   int ksplit, int x_rows) {
+    Layout L;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        const size_t o = off;
+        off += al(bytes);
+        return o;
+    };
+    L.status = take(256);
+    L.partial = take((size_t)ksplit * T * E_router * 4);
+    L.idx = take((size_t)R * 4);
+    L.w = take((size_t)R * 4);
+    L.sorted = take((size_t)R * 4);
+    L.counts = take((size_t)(buckets + 1) * 4);
+    L.roff = take((size_t)(buckets + 1) * 4);
+    L.nchunks = take(16);
+    L.max_chunks = max_chunks_for(buckets, R);
+    L.chunks = take((size_t)L.max_chunks * sizeof(Chunk));
+    L.xpanel = take((size_t)x_rows * K * 2);
+    L.xsum = take((size_t)x_rows * (K / 16) * 4);
+    L.hpanel = take((size_t)R * I * 2);
+    L.hsum = take((size_t)R * (I / 16) * 4);
+    L.yw = take((size_t)R * H_out * 2);
+    L.cnt = take((size_t)T * (H_out / 16) * 4);
+    L.total = off;
+    return L;
+}
+
+Layout layer_layout(const lmoe_layer *l, int T) {
+    const int H = l->experts.hidden, I = l->experts.inter;
+    const int R = T * l->router.top_k;
+    return make_layout(T, R, H, I, H, l->router.n_experts + 1, l->router.n_experts, H / kRouterKS, T);
+}
+
+template <typename P>
+P *at(void *ws, size_t off) {
+    return reinterpret_cast<P *>(static_cast<uint8_t *>(ws) + off);
+}
+
+QView view(const lmoe_qproj &p, int n_slots, int rows, int cols) {
+    QView v;
+    v.w = p.weight;
+    v.s = static_cast<const uint16_t *>(p.scales);
+    v.b = static_cast<const uint16_t *>(p.biases);
+    v.words_per_row = cols * p.bits / 32;
+    v.groups_per_row = cols / p.group_size;
+    v.w_slot_stride = (int64_t)rows * v.words_per_row;
+    v.sb_slot_stride = (int64_t)rows * v.groups_per_row;
+    v.rows = rows;
+    v.cols = cols;
+    (void)n_slots;
+    return v;
+}
+
+int check_proj(const lmoe_qproj &p, int rows, int cols) {
+    if (!p.weight || !p.scales || !p.biases) return LMOE_EINVAL;
+    if (!gemv_ok(p.bits, p.group_size)) return LMOE_EUNSUPPORTED;
+    if (rows % 16 != 0 || cols % p.group_size != 0) return LMOE_EUNSUPPORTED;
+    return LMOE_OK;
+}
+
+int check_experts(const lmoe_experts *e) {
+    if (!e) return LMOE_EINVAL;
+    if (e->n_slots < 1 || e->hidden <= 0 || e->inter <= 0) return LMOE_EINVAL;
+    if (e->dtype != LMOE_BF16 && e->dtype != LMOE_F16) return LMOE_EUNSUPPORTED;
+    int rc;
+    if ((rc = check_proj(e->gate, e->inter, e->hidden))) return rc;
+    if ((rc = check_proj(e->up, e->inter, e->hidden))) return rc;
+    if ((rc = check_proj(e->down, e->hidden, e->inter))) return rc;
+    if (e->gate.bits != e->up.bits || e->gate.group_size != e->up.group_size) return LMOE_EUNSUPPORTED;
+    return LMOE_OK;
+}
+
+int check_layer(const lmoe_layer *l) {
+    if (!l) return LMOE_EINVAL;
+    int rc = check_experts(&l->experts);
+    if (rc) return rc;
+    const lmoe_router &r = l->router;
+    if (r.n_experts < 1 || r.top_k < 1 || r.top_k > 16 || r.top_k > r.n_experts) return LMOE_EINVAL;
+    if (r.n_experts > 32 * kRouterMaxEPL) return LMOE_EUNSUPPORTED;
+    if (r.scoring < 0 || r.scoring > 2) return LMOE_EUNSUPPORTED;
+    if (l->swiglu_mode != LMOE_SWIGLU_FUSED && l->swiglu_mode != LMOE_SWIGLU_STOCK) return LMOE_EUNSUPPORTED;
+    if (!l->expert_slot) return LMOE_EINVAL;
+    return LMOE_OK;
+}
+
+int cuda_rc(cudaError_t e) {
+    if (e == cudaSuccess) return LMOE_OK;
+    if (e == cudaErrorInvalidValue) return LMOE_EUNSUPPORTED;
+    return LMOE_ECUDA;
+}
+
+// Runs dispatch for R routes into buckets [0, n_experts) (+ zero bucket).
+int run_dispatch(const Layout &L, void *ws, const int32_t *idx, int R, int n_experts,
+                 const int32_t *expert_slot, int n_slots, cudaStream_t st) {
+    DispatchIn din;
+    din.idx = idx;
+    din.R = R;
+    din.n_experts = n_experts;
+    din.expert_slot = expert_slot;
+    din.n_slots = n_slots;
+    DispatchOut dout;
+    dout.sorted_routes = at<int32_t>(ws, L.sorted);
+    dout.chunks = at<Chunk>(ws, L.chunks);
+    dout.n_chunks = at<int32_t>(ws, L.nchunks);
+    dout.counts = at<int32_t>(ws, L.counts);
+    dout.route_off = at<int32_t>(ws, L.roff);
+    int32_t *err = at<int32_t>(ws, L.status);
+    if (R <= kDispatchSmallMaxRoutes && n_experts + 1 <= kDispatchSmallMaxBuckets)
+        return cuda_rc(launch_dispatch_small(din, dout, err, st));
+    return cuda_rc(launch_dispatch_large(din, dout, err, st));
+}
+
+GemvArgs gemv_base(const Layout &L, void *ws, int n_slots, int ntok_max) {
+    GemvArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.chunks = at<Chunk>(ws, L.chunks);
+    a.n_chunks = at<int32_t>(ws, L.nchunks);
+    a.sorted_routes = at<int32_t>(ws, L.sorted);
+    a.n_slots = n_slots;
+    a.ntok_max = ntok_max;
+    a.err = at<int32_t>(ws, L.status);
+    return a;
+}
+
+// gate/up + SwiGLU then down + combine over an already dispatched layer.
+int run_experts(const lmoe_layer *l, const Layout &L, void *ws, int T, const float *route_w,
+                void *out, cudaStream_t st) {
+    const lmoe_experts &ex = l->experts;
+    const int H = ex.hidden, I = ex.inter, k = l->router.top_k;
+    const int ntok_max = T < kChunkTok ? T : kChunkTok;
+    GemvArgs gu = gemv_base(L, ws, ex.n_slots, ntok_max);
+    gu.q0 = view(ex.gate, ex.n_slots, I, H);
+    gu.q1 = view(ex.up, ex.n_slots, I, H);
+    gu.panel = at<uint16_t>(ws, L.xpanel);
+    gu.sum16 = at<float>(ws, L.xsum);
+    gu.route_div = k;
+    gu.out = at<uint16_t>(ws, L.hpanel);
+    gu.out_sum16 = at<float>(ws, L.hsum);
+    gu.out_panel = 1;
+    gu.out_bits = ex.down.bits;
+    gu.out_gs = ex.down.group_size;
+    gu.limit = l->swiglu_limit;
+    gu.swiglu_mode = l->swiglu_mode;
+    int rc = cuda_rc(launch_gemv(MODE_GATEUP, ex.dtype == LMOE_F16, ex.gate.bits, ex.gate.group_size,
+                                 gu, L.max_chunks, st));
+    if (rc) return rc;
+    GemvArgs dn = gemv_base(L, ws, ex.n_slots, ntok_max);
+    dn.q0 = view(ex.down, ex.n_slots, H, I);
+    dn.panel = at<uint16_t>(ws, L.hpanel);
+    dn.sum16 = at<float>(ws, L.hsum);
+    dn.route_div = 1;
+    dn.out = at<uint16_t>(ws, L.yw);
+    dn.route_w = route_w;
+    dn.top_k = k;
+    dn.counters = at<uint32_t>(ws, L.cnt);
+    dn.combined = static_cast<uint16_t *>(out);
+    return cuda_rc(launch_gemv(MODE_DOWN, ex.dtype == LMOE_F16, ex.down.bits, ex.down.group_size, dn,
+                               L.max_chunks, st));
+}
+
+}  // namespace
+
+extern "C" {
+
+int lmoe_version(void) { return LMOE_ABI_VERSION; }
+
+const char *lmoe_strerror(int status) {
+    switch (status) {
+        case LMOE_OK: return "ok";
+        case LMOE_EINVAL: return "invalid argument";
+        case LMOE_EUNSUPPORTED: return "unsupported geometry, bit width or group size";
+        case LMOE_EINDEX: return "expert id or arena slot out of range";
+        case LMOE_ECUDA: return "CUDA error";
+        case LMOE_EWORKSPACE: return "workspace too small";
+        default: return "unknown status";
+    }
+}
+
+size_t lmoe_workspace_size(const lmoe_layer *layer, int32_t max_tokens) {
+    if (check_layer(layer) || max_tokens < 0) return 0;
+    const int T = max_tokens > 0 ? max_tokens : 1;
+    return layer_layout(layer, T).total;
+}
+
+size_t lmoe_workspace_size_routes(int32_t max_routes, int32_t hidden, int32_t inter, int32_t n_slots) {
+    if (max_routes < 0 || hidden <= 0 || n_slots < 1) return 0;
+    const int R = max_routes > 0 ? max_routes : 1;
+    const int K = hidden > inter ? hidden : inter;
+    return make_layout(R, R, K, 0, 0, n_slots + 1, 1, 1, R).total;
+}
+
+int lmoe_workspace_init(void *workspace, size_t bytes, void *stream) {
+    if (!workspace || bytes == 0) return LMOE_EINVAL;
+    return cuda_rc(cudaMemsetAsync(workspace, 0, bytes, static_cast<cudaStream_t>(stream)));
+}
+
+int lmoe_workspace_status(void *workspace, void *stream) {
+    if (!workspace) return LMOE_EINVAL;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int32_t host = 0;
+    cudaError_t e = cudaMemcpyAsync(&host, workspace, sizeof(int32_t), cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return LMOE_ECUDA;
+    if (host != 0) {
+        e = cudaMemsetAsync(workspace, 0, sizeof(int32_t), st);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+        if (e != cudaSuccess) return LMOE_ECUDA;
+        return host;
+    }
+    return LMOE_OK;
+}
+
+static int route_impl(const lmoe_layer *l, const Layout &L, const void *x, int T, int32_t *idx_user,
+                      float *w_user, void *ws, bool fused_dispatch, bool panel, cudaStream_t st) {
+    const int H = l->experts.hidden;
+    const int k = l->router.top_k;
+    const int R = T * k;
+    const int ksplit = H / kRouterKS;
+    RouterArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.x = static_cast<const uint16_t *>(x);
+    a.T = T;
+    a.H = H;
+    a.wg = static_cast<const uint16_t *>(l->router.weight);
+    a.bias = l->router.bias;
+    a.E = l->router.n_experts;
+    a.top_k = k;
+    a.scoring = l->router.scoring;
+    a.norm_topk = l->router.norm_topk;
+    a.scaling = l->router.routed_scaling;
+    a.partial = at<float>(ws, L.partial);
+    if (panel) {
+        a.xpanel = at<uint16_t>(ws, L.xpanel);
+        a.xsum16 = at<float>(ws, L.xsum);
+        a.pbits = l->experts.gate.bits;
+        a.pgs = l->experts.gate.group_size;
+    }
+    a.act_f16 = l->experts.dtype == LMOE_F16;
+    a.counter = at<uint32_t>(ws, L.status) + 1;
+    a.idx_ws = at<int32_t>(ws, L.idx);
+    a.w_ws = at<float>(ws, L.w);
+    a.idx_user = idx_user;
+    a.w_user = w_user;
+    a.err = at<int32_t>(ws, L.status);
+    a.din.idx = a.idx_ws;
+    a.din.R = R;
+    a.din.n_experts = a.E;
+    a.din.expert_slot = l->expert_slot;
+    a.din.n_slots = l->experts.n_slots;
+    a.dout.sorted_routes = at<int32_t>(ws, L.sorted);
+    a.dout.chunks = at<Chunk>(ws, L.chunks);
+    a.dout.n_chunks = at<int32_t>(ws, L.nchunks);
+    a.dout.counts = at<int32_t>(ws, L.counts);
+    a.dout.route_off = at<int32_t>(ws, L.roff);
+    const bool small = fused_dispatch && T <= 64 && R <= kDispatchSmallMaxRoutes &&
+                       a.E + 1 <= kDispatchSmallMaxBuckets;
+    a.finish = small ? 1 : 0;
+    int rc = cuda_rc(launch_router(a, ksplit, st));
+    if (rc) return rc;
+    if (small) return LMOE_OK;
+    TopkArgs tk;
+    tk.partial = a.partial;
+    tk.ksplit = ksplit;
+    tk.T = T;
+    tk.E = a.E;
+    tk.top_k = k;
+    tk.scoring = a.scoring;
+    tk.norm_topk = a.norm_topk;
+    tk.scaling = a.scaling;
+    tk.bias = a.bias;
+    tk.idx_ws = a.idx_ws;
+    tk.w_ws = a.w_ws;
+    tk.idx_user = idx_user;
+    tk.w_user = w_user;
+    rc = cuda_rc(launch_topk(tk, st));
+    if (rc || !fused_dispatch) return rc;
+    return run_dispatch(L, ws, a.idx_ws, R, a.E, l->expert_slot, l->experts.n_slots, st);
+}
+
+int lmoe_route(const lmoe_layer *layer, const void *x, int32_t tokens, int32_t *idx, float *w,
+               void *workspace, size_t ws_bytes, void *stream) {
+    int rc = check_layer(layer);
+    if (rc) return rc;
+    if (tokens < 0 || (tokens > 0 && (!x || !idx || !w || !workspace))) return LMOE_EINVAL;
+    if (tokens == 0) return LMOE_OK;
+    if (layer->experts.hidden % kRouterKS) return LMOE_EUNSUPPORTED;
+    const Layout L = layer_layout(layer, tokens);
+    if (ws_bytes < L.total) return LMOE_EWORKSPACE;
+    return route_impl(layer, L, x, tokens, idx, w, workspace, false, false,
+                      static_cast<cudaStream_t>(stream));
+}
+
+int lmoe_moe_layer(const lmoe_layer *layer, const void *x, int32_t tokens, void *out, int32_t *idx,
+                   float *w, void *workspace, size_t ws_bytes, void *stream) {
+    int rc = check_layer(layer);
+    if (rc) return rc;
+    if (tokens < 0 || (tokens > 0 && (!x || !out || !workspace))) return LMOE_EINVAL;
+    if (tokens == 0) return LMOE_OK;
+    if (layer->experts.hidden % kRouterKS) return LMOE_EUNSUPPORTED;
+    const Layout L = layer_layout(layer, tokens);
+    if (ws_bytes < L.total) return LMOE_EWORKSPACE;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    rc = route_impl(layer, L, x, tokens, idx, w, workspace, true, true, st);
+    if (rc) return rc;
+    return run_experts(layer, L, workspace, tokens, at<float>(workspace, L.w), out, st);
+}
+
+int lmoe_moe_routed(const lmoe_layer *layer, const void *x, int32_t tokens, const int32_t *idx,
+                    const float *w, void *out, void *workspace, size_t ws_bytes, void *stream) {
+    int rc = check_layer(layer);
+    if (rc) return rc;
+    if (tokens < 0 || (tokens > 0 && (!x || !idx || !w || !out || !workspace))) return LMOE_EINVAL;
+    if (tokens == 0) return LMOE_OK;
+    const Layout L = layer_layout(layer, tokens);
+    if (ws_bytes < L.total) return LMOE_EWORKSPACE;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const lmoe_experts &ex = layer->experts;
+    PanelArgs pa;
+    pa.x = static_cast<const uint16_t *>(x);
+    pa.rows = tokens;
+    pa.K = ex.hidden;
+    pa.panel = at<uint16_t>(workspace, L.xpanel);
+    pa.sum16 = at<float>(workspace, L.xsum);
+    pa.bits = ex.gate.bits;
+    pa.gs = ex.gate.group_size;
+    pa.act_f16 = ex.dtype == LMOE_F16;
+    rc = cuda_rc(launch_panel(pa, st));
+    if (rc) return rc;
+    const int R = tokens * layer->router.top_k;
+    rc = run_dispatch(L, workspace, idx, R, layer->router.n_experts, layer->expert_slot, ex.n_slots, st);
+    if (rc) return rc;
+    return run_experts(layer, L, workspace, tokens, w, out, st);
+}
+
+int lmoe_gateup_swiglu(const lmoe_experts *experts, const void *x, int32_t tokens, int32_t top_k,
+                       const uint32_t *slots, float limit, int32_t swiglu_mode, void *h,
+                       void *workspace, size_t ws_bytes, void *stream) {
+    int rc = check_experts(experts);
+    if (rc) return rc;
+    if (tokens < 0 || top_k < 1) return LMOE_EINVAL;
+    if (tokens > 0 && (!x || !slots || !h || !workspace)) return LMOE_EINVAL;
+    if (swiglu_mode != LMOE_SWIGLU_FUSED && swiglu_mode != LMOE_SWIGLU_STOCK) return LMOE_EUNSUPPORTED;
+    if (tokens == 0) return LMOE_OK;
+    const int R = tokens * top_k;
+    const int H = experts->hidden, I = experts->inter;
+    const int K = H > I ? H : I;
+    const Layout L = make_layout(R, R, K, 0, 0, experts->n_slots + 1, 1, 1, R);
+    if (ws_bytes < L.total) return LMOE_EWORKSPACE;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    PanelArgs pa;
+    pa.x = static_cast<const uint16_t *>(x);
+    pa.rows = tokens;
+    pa.K = H;
+    pa.panel = at<uint16_t>(workspace, L.xpanel);
+    pa.sum16 = at<float>(workspace, L.xsum);
+    pa.bits = experts->gate.bits;
+    pa.gs = experts->gate.group_size;
+    pa.act_f16 = experts->dtype == LMOE_F16;
+    rc = cuda_rc(launch_panel(pa, st));
+    if (rc) return rc;
+    rc = run_dispatch(L, workspace, reinterpret_cast<const int32_t *>(slots), R, experts->n_slots,
+                      nullptr, experts->n_slots, st);
+    if (rc) return rc;
+    const int ntok_max = tokens < kChunkTok ? tokens : kChunkTok;
+    GemvArgs gu = gemv_base(L, workspace, experts->n_slots, ntok_max);
+    gu.q0 = view(experts->gate, experts->n_slots, I, H);
+    gu.q1 = view(experts->up, experts->n_slots, I, H);
+    gu.panel = pa.panel;
+    gu.sum16 = pa.sum16;
+    gu.route_div = top_k;
+    gu.out = static_cast<uint16_t *>(h);
+    gu.out_panel = 0;
+    gu.limit = limit;
+    gu.swiglu_mode = swiglu_mode;
+    return cuda_rc(launch_gemv(MODE_GATEUP, pa.act_f16, experts->gate.bits, experts->gate.group_size,
+                               gu, L.max_chunks, st));
+}
+
+int lmoe_gather_qmm(const lmoe_qproj *proj, int32_t n_slots, int32_t rows, int32_t cols, int32_t dtype,
+                    const void *x, int32_t routes, const uint32_t *slots, void *y, void *workspace,
+                    size_t ws_bytes, void *stream) {
+    if (!proj || n_slots < 1 || rows <= 0 || cols <= 0 || routes < 0) return LMOE_EINVAL;
+    if (dtype != LMOE_BF16 && dtype != LMOE_F16) return LMOE_EUNSUPPORTED;
+    int rc = check_proj(*proj, rows, cols);
+    if (rc) return rc;
+    if (routes == 0) return LMOE_OK;
+    if (!x || !slots || !y || !workspace) return LMOE_EINVAL;
+    const Layout L = make_layout(routes, routes, cols, 0, 0, n_slots + 1, 1, 1, routes);
+    if (ws_bytes < L.total) return LMOE_EWORKSPACE;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    PanelArgs pa;
+    pa.x = static_cast<const uint16_t *>(x);
+    pa.rows = routes;
+    pa.K = cols;
+    pa.panel = at<uint16_t>(workspace, L.xpanel);
+    pa.sum16 = at<float>(workspace, L.xsum);
+    pa.bits = proj->bits;
+    pa.gs = proj->group_size;
+    pa.act_f16 = dtype == LMOE_F16;
+    rc = cuda_rc(launch_panel(pa, st));
+    if (rc) return rc;
+    rc = run_dispatch(L, workspace, reinterpret_cast<const int32_t *>(slots), routes, n_slots, nullptr,
+                      n_slots, st);
+    if (rc) return rc;
+    const int ntok_max = routes < kChunkTok ? routes : kChunkTok;
+    GemvArgs q = gemv_base(L, workspace, n_slots, ntok_max);
+    q.q0 = view(*proj, n_slots, rows, cols);
+    q.panel = pa.panel;
+    q.sum16 = pa.sum16;
+    q.route_div = 1;
+    q.out = static_cast<uint16_t *>(y);
+    return cuda_rc(launch_gemv(MODE_QMM, pa.act_f16, proj->bits, proj->group_size, q, L.max_chunks, st));
+}
+
+}  // extern "C"

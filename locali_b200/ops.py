@@ -1,0 +1,273 @@
+"""Tensor-level wrappers over the C ABI (torch CUDA tensors in, out).
+
+These are thin: they build the plain-pointer descriptors of include/lmoe.h
+from torch tensors, own a device workspace, and enqueue the kernels on the
+current CUDA stream.  No host synchronisation happens unless asked for
+(:meth:`Workspace.check`).
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from ._lib import check, lmoe
+
+_ACT = {torch.bfloat16: _lib.LMOE_BF16, torch.float16: _lib.LMOE_F16}
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _need_cuda(*ts: torch.Tensor) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("locali_b200 kernels need CUDA tensors (no CPU fallback)")
+
+
+@dataclass
+class QProjArrays:
+    """One projection of all arena slots (MLX SwitchGLU layout).
+
+    weight int32/uint32 [n_slots, rows, cols*bits/32]; scales/biases
+    [n_slots, rows, cols/group_size] in the activation dtype.
+    """
+
+    weight: torch.Tensor
+    scales: torch.Tensor
+    biases: torch.Tensor
+    bits: int
+    group_size: int
+
+    @property
+    def rows(self) -> int:
+        return int(self.weight.shape[-2])
+
+    @property
+    def cols(self) -> int:
+        return int(self.scales.shape[-1]) * self.group_size
+
+    @staticmethod
+    def infer(weight: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, cols: int) -> "QProjArrays":
+        """Infer bits = packed*32/cols and group = cols/groups (dsv4_engine.py:162-171)."""
+        packed = int(weight.shape[-1])
+        groups = int(scales.shape[-1])
+        if (packed * 32) % cols or cols % groups:
+            raise ValueError(f"cannot infer affine quantization: weight {tuple(weight.shape)}, "
+                             f"scales {tuple(scales.shape)}, cols {cols}")
+        return QProjArrays(weight, scales, biases, packed * 32 // cols, cols // groups)
+
+    def ctype(self) -> _lib.QProj:
+        for t in (self.weight, self.scales, self.biases):
+            if not t.is_contiguous():
+                raise ValueError("arena arrays must be contiguous")
+        return _lib.QProj(self.weight.data_ptr(), self.scales.data_ptr(), self.biases.data_ptr(),
+                          int(self.bits), int(self.group_size))
+
+
+@dataclass
+class ExpertArrays:
+    gate: QProjArrays
+    up: QProjArrays
+    down: QProjArrays
+
+    @property
+    def n_slots(self) -> int:
+        return int(self.gate.weight.shape[0])
+
+    @property
+    def hidden(self) -> int:
+        return self.gate.cols
+
+    @property
+    def inter(self) -> int:
+        return self.gate.rows
+
+    @property
+    def dtype(self) -> torch.dtype:
+        return self.gate.scales.dtype
+
+    def ctype(self) -> _lib.Experts:
+        if self.dtype not in _ACT:
+            raise ValueError(f"unsupported scale dtype {self.dtype}")
+        return _lib.Experts(self.n_slots, self.hidden, self.inter, _ACT[self.dtype],
+                            self.gate.ctype(), self.up.ctype(), self.down.ctype())
+
+
+@dataclass
+class RouterArrays:
+    weight: torch.Tensor            # [E, H] bf16
+    bias: torch.Tensor | None       # [E] fp32 selection-only bias
+    top_k: int
+    scoring: str = "sigmoid"
+    routed_scaling: float = 1.0
+    norm_topk: bool = True
+
+    @property
+    def n_experts(self) -> int:
+        return int(self.weight.shape[0])
+
+    def ctype(self) -> _lib.Router:
+        if self.weight.dtype != torch.bfloat16:
+            raise ValueError("router weight must be bf16")
+        if self.bias is not None and self.bias.dtype != torch.float32:
+            raise ValueError("router bias must be fp32")
+        return _lib.Router(self.weight.data_ptr(), _ptr(self.bias), self.n_experts, int(self.top_k),
+                           _lib.SCORING[self.scoring], int(bool(self.norm_topk)), float(self.routed_scaling))
+
+
+class Workspace:
+    """Caller-owned device scratch for the kernels; zeroed once when (re)sized.
+
+    Kernels leave it reusable (their combine counters return to zero), so a
+    workspace may be used by any number of calls on one stream.  Calls that
+    overlap on different streams need different workspaces.
+    """
+
+    def __init__(self, device: torch.device | str | int | None = None):
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        self.buf: torch.Tensor | None = None
+
+    @property
+    def nbytes(self) -> int:
+        return 0 if self.buf is None else self.buf.numel()
+
+    def ensure(self, nbytes: int) -> "Workspace":
+        if nbytes <= 0:
+            raise _lib.LmoeError(_lib.LMOE_EINVAL, "workspace size")
+        if self.buf is None or self.buf.numel() < nbytes:
+            self.buf = torch.empty(int(nbytes), dtype=torch.uint8, device=self.device)
+            check(lmoe().lmoe_workspace_init(self.buf.data_ptr(), self.buf.numel(), _stream()), "workspace init")
+        return self
+
+    def ptr(self) -> int:
+        return self.buf.data_ptr()
+
+    def check(self) -> None:
+        """Synchronise and raise if a kernel flagged a bad expert id or slot."""
+        if self.buf is not None:
+            check(lmoe().lmoe_workspace_status(self.buf.data_ptr(), _stream()), "kernel status")
+
+
+class MoEKernel:
+    """One routed-MoE layer bound to its arena arrays and router.
+
+    ``expert_slot`` (int32 [E] on the device) maps expert ids to arena slots,
+    so routing, dispatch and the expert products all stay on the GPU.
+    """
+
+    def __init__(self, router: RouterArrays, experts: ExpertArrays, expert_slot: torch.Tensor,
+                 swiglu_limit: float = 10.0, swiglu_mode: str = "fused"):
+        _need_cuda(router.weight, experts.gate.weight, expert_slot)
+        if expert_slot.dtype != torch.int32 or not expert_slot.is_contiguous():
+            raise ValueError("expert_slot must be contiguous int32")
+        self.router, self.experts, self.expert_slot = router, experts, expert_slot
+        self.swiglu_limit, self.swiglu_mode = float(swiglu_limit), swiglu_mode
+        self.desc = _lib.Layer(router.ctype(), experts.ctype(), expert_slot.data_ptr(),
+                               self.swiglu_limit, _lib.SWIGLU_MODE[swiglu_mode])
+        self.act_dtype = experts.dtype
+        self.ws = Workspace(expert_slot.device)
+
+    def workspace_bytes(self, tokens: int) -> int:
+        n = lmoe().lmoe_workspace_size(ctypes.byref(self.desc), int(tokens))
+        if n == 0:
+            raise _lib.LmoeError(_lib.LMOE_EUNSUPPORTED, "layer descriptor")
+        return int(n)
+
+    def _x(self, x: torch.Tensor) -> torch.Tensor:
+        _need_cuda(x)
+        if x.dtype != self.act_dtype:
+            x = x.to(self.act_dtype)
+        return x.reshape(-1, x.shape[-1]).contiguous()
+
+    def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None, idx: torch.Tensor | None = None,
+                 w: torch.Tensor | None = None) -> torch.Tensor:
+        flat = self._x(x)
+        T = flat.shape[0]
+        if out is None:
+            out = torch.empty_like(flat)
+        self.ws.ensure(self.workspace_bytes(T))
+        check(lmoe().lmoe_moe_layer(ctypes.byref(self.desc), flat.data_ptr(), T, out.data_ptr(), _ptr(idx),
+                                    _ptr(w), self.ws.ptr(), self.ws.nbytes, _stream()), "lmoe_moe_layer")
+        return out.reshape(x.shape)
+
+    def route(self, x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        flat = self._x(x)
+        T = flat.shape[0]
+        k = self.router.top_k
+        idx = torch.empty((T, k), dtype=torch.int32, device=flat.device)
+        w = torch.empty((T, k), dtype=torch.float32, device=flat.device)
+        self.ws.ensure(self.workspace_bytes(T))
+        check(lmoe().lmoe_route(ctypes.byref(self.desc), flat.data_ptr(), T, idx.data_ptr(), w.data_ptr(),
+                                self.ws.ptr(), self.ws.nbytes, _stream()), "lmoe_route")
+        return idx, w
+
+    def routed(self, x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+        flat = self._x(x)
+        T = flat.shape[0]
+        idx = idx.reshape(T, -1).to(torch.int32).contiguous()
+        w = w.reshape(T, -1).to(torch.float32).contiguous()
+        if idx.shape[1] != self.router.top_k:
+            raise ValueError("routing width must equal top_k")
+        if out is None:
+            out = torch.empty_like(flat)
+        self.ws.ensure(self.workspace_bytes(T))
+        check(lmoe().lmoe_moe_routed(ctypes.byref(self.desc), flat.data_ptr(), T, idx.data_ptr(), w.data_ptr(),
+                                     out.data_ptr(), self.ws.ptr(), self.ws.nbytes, _stream()), "lmoe_moe_routed")
+        return out.reshape(x.shape)
+
+
+_route_ws: dict[int, Workspace] = {}
+
+
+def _routes_ws(device: torch.device, routes: int, hidden: int, inter: int, n_slots: int) -> Workspace:
+    key = device.index if device.index is not None else torch.cuda.current_device()
+    ws = _route_ws.get(key)
+    if ws is None:
+        ws = _route_ws[key] = Workspace(torch.device("cuda", key))
+    n = lmoe().lmoe_workspace_size_routes(int(routes), int(hidden), int(inter), int(n_slots))
+    return ws.ensure(int(n))
+
+
+def gateup_swiglu(x: torch.Tensor, slots: torch.Tensor, experts: ExpertArrays, limit: float,
+                  mode: str = "fused") -> torch.Tensor:
+    """Fused gate/up + clamped SwiGLU for [T, k] routes -> [T*k, inter]."""
+    _need_cuda(x, slots)
+    T = x.shape[0]
+    slots = slots.reshape(T, -1).to(torch.int32).contiguous()
+    k = slots.shape[1]
+    x = x.reshape(T, -1).to(experts.dtype).contiguous()
+    h = torch.empty((T * k, experts.inter), dtype=experts.dtype, device=x.device)
+    ws = _routes_ws(x.device, T * k, experts.hidden, experts.inter, experts.n_slots)
+    desc = experts.ctype()
+    check(lmoe().lmoe_gateup_swiglu(ctypes.byref(desc), x.data_ptr(), T, k, slots.data_ptr(), float(limit),
+                                    _lib.SWIGLU_MODE[mode], h.data_ptr(), ws.ptr(), ws.nbytes, _stream()),
+          "lmoe_gateup_swiglu")
+    return h
+
+
+def gather_qmm(x: torch.Tensor, slots: torch.Tensor, proj: QProjArrays) -> torch.Tensor:
+    """``mx.gather_qmm(x, w, s, b, rhs_indices=slots, transpose=True)`` with one
+    input row per route: x [R, cols], slots [R] -> [R, rows]."""
+    _need_cuda(x, slots)
+    R = x.shape[0]
+    slots = slots.reshape(-1).to(torch.int32).contiguous()
+    if slots.numel() != R:
+        raise ValueError("one slot per input row")
+    x = x.reshape(R, -1).to(proj.scales.dtype).contiguous()
+    y = torch.empty((R, proj.rows), dtype=proj.scales.dtype, device=x.device)
+    ws = _routes_ws(x.device, R, proj.cols, proj.rows, int(proj.weight.shape[0]))
+    desc = proj.ctype()
+    check(lmoe().lmoe_gather_qmm(ctypes.byref(desc), int(proj.weight.shape[0]), proj.rows, proj.cols,
+                                 _ACT[proj.scales.dtype], x.data_ptr(), R, slots.data_ptr(), y.data_ptr(),
+                                 ws.ptr(), ws.nbytes, _stream()), "lmoe_gather_qmm")
+    return y

@@ -1,0 +1,85 @@
+"""The C-ABI libraries load and export every symbol their headers declare;
+host-side validation works without a GPU (no kernel is launched here)."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from locali_b200 import _lib
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _declared(header: Path) -> list[str]:
+    text = header.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    names = re.findall(r"^[A-Za-z_][\w \*]*?\b(lmoe_\w+|locali_cache_\w+)\s*\(", text, flags=re.M)
+    return sorted(set(names))
+
+
+def test_headers_declare_entry_points():
+    lm = _declared(ROOT / "include" / "lmoe.h")
+    assert "lmoe_moe_layer" in lm and "lmoe_gateup_swiglu" in lm and "lmoe_route" in lm
+    core = _declared(ROOT / "include" / "locali_core.h")
+    assert set(core) == set(_lib.CORE_SYMBOLS)
+
+
+@pytest.mark.parametrize("header,lib", [("lmoe.h", "liblmoe.so"), ("locali_core.h", "liblocali_core.so")])
+def test_library_exports_every_declared_symbol(built, header, lib):
+    dll = ctypes.CDLL(str(ROOT / "locali_b200" / lib))
+    for name in _declared(ROOT / "include" / header):
+        assert hasattr(dll, name), f"{lib} does not export {name}"
+
+
+def _layer(bits=2, gs=64, hidden=1024, inter=512, E=16, k=6):
+    fake = 256  # non-null dummy pointers: nothing is dereferenced on the host
+    q = lambda b: _lib.QProj(fake, fake, fake, b, gs)  # noqa: E731
+    ex = _lib.Experts(E + 1, hidden, inter, _lib.LMOE_BF16, q(bits), q(bits), q(bits))
+    r = _lib.Router(fake, None, E, k, 0, 1, 1.0)
+    return _lib.Layer(r, ex, fake, 10.0, 0)
+
+
+def test_workspace_size_and_validation(built):
+    lib = _lib.lmoe()
+    L = _layer()
+    n1 = lib.lmoe_workspace_size(ctypes.byref(L), 1)
+    n64 = lib.lmoe_workspace_size(ctypes.byref(L), 64)
+    assert 0 < n1 < n64
+    # unsupported bit width / group size
+    assert lib.lmoe_workspace_size(ctypes.byref(_layer(bits=3)), 1) == 0
+    assert lib.lmoe_workspace_size(ctypes.byref(_layer(bits=2, gs=32)), 1) == 0
+    # top_k > n_experts
+    assert lib.lmoe_workspace_size(ctypes.byref(_layer(E=4, k=6)), 1) == 0
+    # zero tokens is a successful no-op; null pointers with tokens are rejected
+    assert lib.lmoe_moe_layer(ctypes.byref(L), None, 0, None, None, None, None, 0, None) == _lib.LMOE_OK
+    assert lib.lmoe_moe_layer(ctypes.byref(L), None, 4, None, None, None, None, 0, None) == _lib.LMOE_EINVAL
+    assert lib.lmoe_moe_layer(None, None, 4, None, None, None, None, 0, None) == _lib.LMOE_EINVAL
+    # too small a workspace is reported before any launch
+    rc = lib.lmoe_moe_layer(ctypes.byref(L), 256, 4, 256, None, None, 256, 16, None)
+    assert rc == _lib.LMOE_EWORKSPACE
+    bad = _layer()
+    bad.swiglu_mode = 7
+    assert lib.lmoe_moe_layer(ctypes.byref(bad), 256, 4, 256, None, None, 256, 1 << 30, None) == \
+        _lib.LMOE_EUNSUPPORTED
+
+
+def test_strerror_and_version(built):
+    lib = _lib.lmoe()
+    assert lib.lmoe_version() == 1
+    assert lib.lmoe_strerror(_lib.LMOE_EINDEX).decode().startswith("expert id")
+    assert lib.lmoe_workspace_size_routes(8, 512, 256, 5) > 0
+
+
+def test_product_path_fails_loudly_without_cuda(built):
+    import torch
+
+    from locali_b200 import ops
+
+    x = torch.zeros((1, 512), dtype=torch.bfloat16)
+    slots = torch.zeros((1, 1), dtype=torch.int32)
+    q = ops.QProjArrays(torch.zeros((2, 64, 32), dtype=torch.int32), torch.zeros((2, 64, 8), dtype=torch.bfloat16),
+                        torch.zeros((2, 64, 8), dtype=torch.bfloat16), 2, 64)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.gather_qmm(x, slots, q)
