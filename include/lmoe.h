@@ -110,12 +110,17 @@ int lmoe_workspace_init(void *workspace, size_t bytes, void *stream);
 int lmoe_workspace_status(void *workspace, void *stream);
 
 /* Router only: replaces the V4 MoEGate call at dsv4_arena.py:165-166
- * (arena.py:501-506).  x [T, hidden] activations; idx [T, top_k] int32
- * (ordered by biased score, ties to the lower id); w [T, top_k] fp32
- * combine weights (already multiplied by routed_scaling). */
-int lmoe_route(const lmoe_layer *layer, const void *x, int32_t tokens,
-               int32_t *idx, float *w, void *workspace, size_t ws_bytes,
-               void *stream);
+ * (arena.py:501-506).  x [T, hidden] activations of `dtype`; idx [T, top_k]
+ * int32 (ordered by biased score, ties to the lower id); w [T, top_k] fp32
+ * combine weights (already multiplied by routed_scaling).  hidden must be a
+ * multiple of 256. */
+int lmoe_route(const lmoe_router *router, int32_t hidden, int32_t dtype,
+               const void *x, int32_t tokens, int32_t *idx, float *w,
+               void *workspace, size_t ws_bytes, void *stream);
+
+/* Workspace bytes for lmoe_route with up to max_tokens tokens. */
+size_t lmoe_workspace_size_route(const lmoe_router *router, int32_t hidden,
+                                 int32_t max_tokens);
 
 /* Whole routed-MoE layer: ArenaMoE.__call__ single-tier path
  * (arena.py:508-547, _apply :569-624, V4 _gather dsv4_arena.py:168-235):
@@ -125,6 +130,15 @@ int lmoe_route(const lmoe_layer *layer, const void *x, int32_t tokens,
 int lmoe_moe_layer(const lmoe_layer *layer, const void *x, int32_t tokens,
                    void *out, int32_t *idx, float *w, void *workspace,
                    size_t ws_bytes, void *stream);
+
+/* lmoe_moe_layer that also records two caller-owned CUDA events
+ * (cudaEvent_t, either may be NULL) on the stream: ev_routed after the
+ * routing/dispatch kernel, ev_gateup after the gate/up kernel.  Lets a
+ * caller time each kernel of the layer with events on its launching stream. */
+int lmoe_moe_layer_staged(const lmoe_layer *layer, const void *x, int32_t tokens,
+                          void *out, int32_t *idx, float *w, void *workspace,
+                          size_t ws_bytes, void *stream, void *ev_routed,
+                          void *ev_gateup);
 
 /* Same layer with routing supplied by the caller (an external gate, as
  * V4ArenaMoE.route returns it): idx [T, top_k] expert ids, w [T, top_k]

@@ -86,10 +86,13 @@ _SIGS = {
                                    ctypes.c_size_t),
     "lmoe_workspace_init": ([_VP, ctypes.c_size_t, _VP], ctypes.c_int),
     "lmoe_workspace_status": ([_VP, _VP], ctypes.c_int),
-    "lmoe_route": ([ctypes.POINTER(Layer), _VP, ctypes.c_int32, _VP, _VP, _VP, ctypes.c_size_t, _VP],
-                   ctypes.c_int),
+    "lmoe_route": ([ctypes.POINTER(Router), ctypes.c_int32, ctypes.c_int32, _VP, ctypes.c_int32, _VP, _VP, _VP,
+                    ctypes.c_size_t, _VP], ctypes.c_int),
+    "lmoe_workspace_size_route": ([ctypes.POINTER(Router), ctypes.c_int32, ctypes.c_int32], ctypes.c_size_t),
     "lmoe_moe_layer": ([ctypes.POINTER(Layer), _VP, ctypes.c_int32, _VP, _VP, _VP, _VP, ctypes.c_size_t,
                         _VP], ctypes.c_int),
+    "lmoe_moe_layer_staged": ([ctypes.POINTER(Layer), _VP, ctypes.c_int32, _VP, _VP, _VP, _VP, ctypes.c_size_t,
+                               _VP, _VP, _VP], ctypes.c_int),
     "lmoe_moe_routed": ([ctypes.POINTER(Layer), _VP, ctypes.c_int32, _VP, _VP, _VP, _VP, ctypes.c_size_t,
                          _VP], ctypes.c_int),
     "lmoe_gateup_swiglu": ([ctypes.POINTER(Experts), _VP, ctypes.c_int32, ctypes.c_int32, _VP, ctypes.c_float,

@@ -159,7 +159,7 @@ GemvArgs gemv_base(const Layout &L, void *ws, int n_slots, int ntok_max) {
 
 // gate/up + SwiGLU then down + combine over an already dispatched layer.
 int run_experts(const lmoe_layer *l, const Layout &L, void *ws, int T, const float *route_w,
-                void *out, cudaStream_t st) {
+                void *out, cudaStream_t st, cudaEvent_t ev_gateup = nullptr) {
     const lmoe_experts &ex = l->experts;
     const int H = ex.hidden, I = ex.inter, k = l->router.top_k;
     const int ntok_max = T < kChunkTok ? T : kChunkTok;
@@ -179,6 +179,7 @@ int run_experts(const lmoe_layer *l, const Layout &L, void *ws, int T, const flo
     int rc = cuda_rc(launch_gemv(MODE_GATEUP, ex.dtype == LMOE_F16, ex.gate.bits, ex.gate.group_size,
                                  gu, L.max_chunks, st));
     if (rc) return rc;
+    if (ev_gateup && cudaEventRecord(ev_gateup, st) != cudaSuccess) return LMOE_ECUDA;
     GemvArgs dn = gemv_base(L, ws, ex.n_slots, ntok_max);
     dn.q0 = view(ex.down, ex.n_slots, H, I);
     dn.panel = at<uint16_t>(ws, L.hpanel);
@@ -245,10 +246,11 @@ int lmoe_workspace_status(void *workspace, void *stream) {
     return LMOE_OK;
 }
 
-static int route_impl(const lmoe_layer *l, const Layout &L, const void *x, int T, int32_t *idx_user,
-                      float *w_user, void *ws, bool fused_dispatch, bool panel, cudaStream_t st) {
-    const int H = l->experts.hidden;
-    const int k = l->router.top_k;
+// Router (+ top-k, + dispatch when `l` is given).  In the decode regime the
+// router kernel's last block runs top-k (and dispatch) itself: one launch.
+static int route_impl(const lmoe_router &r, int H, int dtype, const lmoe_layer *l, const Layout &L, const void *x,
+                      int T, int32_t *idx_user, float *w_user, void *ws, cudaStream_t st) {
+    const int k = r.top_k;
     const int R = T * k;
     const int ksplit = H / kRouterKS;
     RouterArgs a;
@@ -256,21 +258,21 @@ static int route_impl(const lmoe_layer *l, const Layout &L, const void *x, int T
     a.x = static_cast<const uint16_t *>(x);
     a.T = T;
     a.H = H;
-    a.wg = static_cast<const uint16_t *>(l->router.weight);
-    a.bias = l->router.bias;
-    a.E = l->router.n_experts;
+    a.wg = static_cast<const uint16_t *>(r.weight);
+    a.bias = r.bias;
+    a.E = r.n_experts;
     a.top_k = k;
-    a.scoring = l->router.scoring;
-    a.norm_topk = l->router.norm_topk;
-    a.scaling = l->router.routed_scaling;
+    a.scoring = r.scoring;
+    a.norm_topk = r.norm_topk;
+    a.scaling = r.routed_scaling;
     a.partial = at<float>(ws, L.partial);
-    if (panel) {
+    if (l) {
         a.xpanel = at<uint16_t>(ws, L.xpanel);
         a.xsum16 = at<float>(ws, L.xsum);
         a.pbits = l->experts.gate.bits;
         a.pgs = l->experts.gate.group_size;
     }
-    a.act_f16 = l->experts.dtype == LMOE_F16;
+    a.act_f16 = dtype == LMOE_F16;
     a.counter = at<uint32_t>(ws, L.status) + 1;
     a.idx_ws = at<int32_t>(ws, L.idx);
     a.w_ws = at<float>(ws, L.w);
@@ -280,53 +282,74 @@ static int route_impl(const lmoe_layer *l, const Layout &L, const void *x, int T
     a.din.idx = a.idx_ws;
     a.din.R = R;
     a.din.n_experts = a.E;
-    a.din.expert_slot = l->expert_slot;
-    a.din.n_slots = l->experts.n_slots;
+    a.din.expert_slot = l ? l->expert_slot : nullptr;
+    a.din.n_slots = l ? l->experts.n_slots : 0;
     a.dout.sorted_routes = at<int32_t>(ws, L.sorted);
     a.dout.chunks = at<Chunk>(ws, L.chunks);
     a.dout.n_chunks = at<int32_t>(ws, L.nchunks);
     a.dout.counts = at<int32_t>(ws, L.counts);
     a.dout.route_off = at<int32_t>(ws, L.roff);
-    const bool small = fused_dispatch && T <= 64 && R <= kDispatchSmallMaxRoutes &&
-                       a.E + 1 <= kDispatchSmallMaxBuckets;
-    a.finish = small ? 1 : 0;
+    const bool small_topk = T <= 64;
+    const bool small_disp = l && R <= kDispatchSmallMaxRoutes && a.E + 1 <= kDispatchSmallMaxBuckets;
+    a.finish = small_topk ? 1 : 0;
+    a.do_dispatch = (small_topk && small_disp) ? 1 : 0;
     int rc = cuda_rc(launch_router(a, ksplit, st));
     if (rc) return rc;
-    if (small) return LMOE_OK;
-    TopkArgs tk;
-    tk.partial = a.partial;
-    tk.ksplit = ksplit;
-    tk.T = T;
-    tk.E = a.E;
-    tk.top_k = k;
-    tk.scoring = a.scoring;
-    tk.norm_topk = a.norm_topk;
-    tk.scaling = a.scaling;
-    tk.bias = a.bias;
-    tk.idx_ws = a.idx_ws;
-    tk.w_ws = a.w_ws;
-    tk.idx_user = idx_user;
-    tk.w_user = w_user;
-    rc = cuda_rc(launch_topk(tk, st));
-    if (rc || !fused_dispatch) return rc;
+    if (!small_topk) {
+        TopkArgs tk;
+        tk.partial = a.partial;
+        tk.ksplit = ksplit;
+        tk.T = T;
+        tk.E = a.E;
+        tk.top_k = k;
+        tk.scoring = a.scoring;
+        tk.norm_topk = a.norm_topk;
+        tk.scaling = a.scaling;
+        tk.bias = a.bias;
+        tk.idx_ws = a.idx_ws;
+        tk.w_ws = a.w_ws;
+        tk.idx_user = idx_user;
+        tk.w_user = w_user;
+        rc = cuda_rc(launch_topk(tk, st));
+        if (rc) return rc;
+    }
+    if (!l || a.do_dispatch) return LMOE_OK;
     return run_dispatch(L, ws, a.idx_ws, R, a.E, l->expert_slot, l->experts.n_slots, st);
 }
 
-int lmoe_route(const lmoe_layer *layer, const void *x, int32_t tokens, int32_t *idx, float *w,
-               void *workspace, size_t ws_bytes, void *stream) {
-    int rc = check_layer(layer);
+int check_router(const lmoe_router *r, int hidden) {
+    if (!r || !r->weight || hidden <= 0) return LMOE_EINVAL;
+    if (r->n_experts < 1 || r->top_k < 1 || r->top_k > 16 || r->top_k > r->n_experts) return LMOE_EINVAL;
+    if (r->n_experts > 32 * kRouterMaxEPL) return LMOE_EUNSUPPORTED;
+    if (r->scoring < 0 || r->scoring > 2) return LMOE_EUNSUPPORTED;
+    if (hidden % kRouterKS) return LMOE_EUNSUPPORTED;
+    return LMOE_OK;
+}
+
+size_t lmoe_workspace_size_route(const lmoe_router *router, int32_t hidden, int32_t max_tokens) {
+    if (check_router(router, hidden) || max_tokens < 0) return 0;
+    const int T = max_tokens > 0 ? max_tokens : 1;
+    return make_layout(T, T * router->top_k, 0, 0, 0, router->n_experts + 1, router->n_experts,
+                       hidden / kRouterKS, 0).total;
+}
+
+int lmoe_route(const lmoe_router *router, int32_t hidden, int32_t dtype, const void *x, int32_t tokens,
+               int32_t *idx, float *w, void *workspace, size_t ws_bytes, void *stream) {
+    int rc = check_router(router, hidden);
     if (rc) return rc;
+    if (dtype != LMOE_BF16 && dtype != LMOE_F16) return LMOE_EUNSUPPORTED;
     if (tokens < 0 || (tokens > 0 && (!x || !idx || !w || !workspace))) return LMOE_EINVAL;
     if (tokens == 0) return LMOE_OK;
-    if (layer->experts.hidden % kRouterKS) return LMOE_EUNSUPPORTED;
-    const Layout L = layer_layout(layer, tokens);
+    const Layout L = make_layout(tokens, tokens * router->top_k, 0, 0, 0, router->n_experts + 1,
+                                 router->n_experts, hidden / kRouterKS, 0);
     if (ws_bytes < L.total) return LMOE_EWORKSPACE;
-    return route_impl(layer, L, x, tokens, idx, w, workspace, false, false,
+    return route_impl(*router, hidden, dtype, nullptr, L, x, tokens, idx, w, workspace,
                       static_cast<cudaStream_t>(stream));
 }
 
-int lmoe_moe_layer(const lmoe_layer *layer, const void *x, int32_t tokens, void *out, int32_t *idx,
-                   float *w, void *workspace, size_t ws_bytes, void *stream) {
+int lmoe_moe_layer_staged(const lmoe_layer *layer, const void *x, int32_t tokens, void *out, int32_t *idx,
+                          float *w, void *workspace, size_t ws_bytes, void *stream, void *ev_routed,
+                          void *ev_gateup) {
     int rc = check_layer(layer);
     if (rc) return rc;
     if (tokens < 0 || (tokens > 0 && (!x || !out || !workspace))) return LMOE_EINVAL;
@@ -335,9 +358,17 @@ int lmoe_moe_layer(const lmoe_layer *layer, const void *x, int32_t tokens, void 
     const Layout L = layer_layout(layer, tokens);
     if (ws_bytes < L.total) return LMOE_EWORKSPACE;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    rc = route_impl(layer, L, x, tokens, idx, w, workspace, true, true, st);
+    rc = route_impl(layer->router, layer->experts.hidden, layer->experts.dtype, layer, L, x, tokens, idx, w,
+                    workspace, st);
     if (rc) return rc;
-    return run_experts(layer, L, workspace, tokens, at<float>(workspace, L.w), out, st);
+    if (ev_routed && cudaEventRecord(static_cast<cudaEvent_t>(ev_routed), st) != cudaSuccess) return LMOE_ECUDA;
+    return run_experts(layer, L, workspace, tokens, at<float>(workspace, L.w), out, st,
+                       static_cast<cudaEvent_t>(ev_gateup));
+}
+
+int lmoe_moe_layer(const lmoe_layer *layer, const void *x, int32_t tokens, void *out, int32_t *idx,
+                   float *w, void *workspace, size_t ws_bytes, void *stream) {
+    return lmoe_moe_layer_staged(layer, x, tokens, out, idx, w, workspace, ws_bytes, stream, nullptr, nullptr);
 }
 
 int lmoe_moe_routed(const lmoe_layer *layer, const void *x, int32_t tokens, const int32_t *idx,
@@ -370,8 +401,15 @@ int lmoe_moe_routed(const lmoe_layer *layer, const void *x, int32_t tokens, cons
 int lmoe_gateup_swiglu(const lmoe_experts *experts, const void *x, int32_t tokens, int32_t top_k,
                        const uint32_t *slots, float limit, int32_t swiglu_mode, void *h,
                        void *workspace, size_t ws_bytes, void *stream) {
-    int rc = check_experts(experts);
+    // only gate and up are read here; the down projection is not validated
+    if (!experts) return LMOE_EINVAL;
+    if (experts->n_slots < 1 || experts->hidden <= 0 || experts->inter <= 0) return LMOE_EINVAL;
+    if (experts->dtype != LMOE_BF16 && experts->dtype != LMOE_F16) return LMOE_EUNSUPPORTED;
+    int rc = check_proj(experts->gate, experts->inter, experts->hidden);
+    if (!rc) rc = check_proj(experts->up, experts->inter, experts->hidden);
     if (rc) return rc;
+    if (experts->gate.bits != experts->up.bits || experts->gate.group_size != experts->up.group_size)
+        return LMOE_EUNSUPPORTED;
     if (tokens < 0 || top_k < 1) return LMOE_EINVAL;
     if (tokens > 0 && (!x || !slots || !h || !workspace)) return LMOE_EINVAL;
     if (swiglu_mode != LMOE_SWIGLU_FUSED && swiglu_mode != LMOE_SWIGLU_STOCK) return LMOE_EUNSUPPORTED;

@@ -439,6 +439,7 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
     for (int tok = warp; tok < a.T; tok += 8)
         topk_token(a.partial, gridDim.y, a.T, a.E, tok, a.bias, a.scoring, a.top_k, a.norm_topk,
                    a.scaling, a.idx_ws, a.w_ws, a.idx_user, a.w_user);
+    if (!a.do_dispatch) return;
     __threadfence();
     __syncthreads();
     dispatch_block(a.din, a.dout, a.err, s_disp);
@@ -857,9 +858,19 @@ static cudaError_t launch_gemv_t(const GemvArgs &a, int max_chunks, cudaStream_t
         if (e != cudaSuccess) return e;
         configured = smem;
     }
+    // occupancy depends only on (warps, smem); remember the last answer
+    static int cached_nw = -1, cached_per_sm = 0;
+    static size_t cached_smem = 0;
     int per_sm = 0;
-    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, nw * 32, smem);
-    if (e != cudaSuccess) return e;
+    if (cached_nw == nw && cached_smem == smem) {
+        per_sm = cached_per_sm;
+    } else {
+        cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, nw * 32, smem);
+        if (e != cudaSuccess) return e;
+        cached_nw = nw;
+        cached_smem = smem;
+        cached_per_sm = per_sm;
+    }
     if (per_sm < 1) return cudaErrorInvalidConfiguration;
     const long units_max = (long)max_chunks * (a.q0.rows / 16);
     long grid = (long)per_sm * num_sms();

@@ -39,6 +39,7 @@ struct RouterArgs {
     int32_t act_f16;
     // finisher (decode regime): last CTA runs top-k + dispatch
     int32_t finish;
+    int32_t do_dispatch;
     uint32_t *counter;
     int32_t *idx_ws;  // [T*k]
     float *w_ws;      // [T*k]

@@ -27,6 +27,15 @@ def _stream() -> int:
     return torch.cuda.current_stream().cuda_stream
 
 
+def _event(ev: torch.cuda.Event | None) -> int | None:
+    """Raw cudaEvent_t of a torch event (created on first use)."""
+    if ev is None:
+        return None
+    if ev.cuda_event == 0:
+        ev.record()  # forces creation of the underlying event
+    return ev.cuda_event
+
+
 def _need_cuda(*ts: torch.Tensor) -> None:
     for t in ts:
         if t is not None and not t.is_cuda:
@@ -199,16 +208,20 @@ class MoEKernel:
                                     _ptr(w), self.ws.ptr(), self.ws.nbytes, _stream()), "lmoe_moe_layer")
         return out.reshape(x.shape)
 
-    def route(self, x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    def staged(self, x: torch.Tensor, out: torch.Tensor, ev_routed: torch.cuda.Event,
+               ev_gateup: torch.cuda.Event, idx: torch.Tensor | None = None) -> torch.Tensor:
+        """The layer with CUDA events recorded after routing and after gate/up
+        (for per-kernel timing on the launching stream)."""
         flat = self._x(x)
         T = flat.shape[0]
-        k = self.router.top_k
-        idx = torch.empty((T, k), dtype=torch.int32, device=flat.device)
-        w = torch.empty((T, k), dtype=torch.float32, device=flat.device)
         self.ws.ensure(self.workspace_bytes(T))
-        check(lmoe().lmoe_route(ctypes.byref(self.desc), flat.data_ptr(), T, idx.data_ptr(), w.data_ptr(),
-                                self.ws.ptr(), self.ws.nbytes, _stream()), "lmoe_route")
-        return idx, w
+        check(lmoe().lmoe_moe_layer_staged(ctypes.byref(self.desc), flat.data_ptr(), T, out.data_ptr(), _ptr(idx),
+                                           None, self.ws.ptr(), self.ws.nbytes, _stream(), _event(ev_routed),
+                                           _event(ev_gateup)), "lmoe_moe_layer_staged")
+        return out
+
+    def route(self, x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        return route(self._x(x), self.router, self.ws)
 
     def routed(self, x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor,
                out: torch.Tensor | None = None) -> torch.Tensor:
@@ -224,6 +237,26 @@ class MoEKernel:
         check(lmoe().lmoe_moe_routed(ctypes.byref(self.desc), flat.data_ptr(), T, idx.data_ptr(), w.data_ptr(),
                                      out.data_ptr(), self.ws.ptr(), self.ws.nbytes, _stream()), "lmoe_moe_routed")
         return out.reshape(x.shape)
+
+
+def route(x: torch.Tensor, router: RouterArrays, ws: Workspace | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Router kernel only: x [T, hidden] -> (idx int32 [T, k], w fp32 [T, k])."""
+    _need_cuda(x, router.weight)
+    if x.dtype not in _ACT:
+        raise ValueError(f"unsupported activation dtype {x.dtype}")
+    flat = x.reshape(-1, x.shape[-1]).contiguous()
+    T, H = flat.shape
+    k = router.top_k
+    idx = torch.empty((T, k), dtype=torch.int32, device=flat.device)
+    w = torch.empty((T, k), dtype=torch.float32, device=flat.device)
+    desc = router.ctype()
+    n = lmoe().lmoe_workspace_size_route(ctypes.byref(desc), H, T)
+    if n == 0:
+        raise _lib.LmoeError(_lib.LMOE_EUNSUPPORTED, "router descriptor")
+    ws = (ws or Workspace(flat.device)).ensure(int(n))
+    check(lmoe().lmoe_route(ctypes.byref(desc), H, _ACT[flat.dtype], flat.data_ptr(), T, idx.data_ptr(),
+                            w.data_ptr(), ws.ptr(), ws.nbytes, _stream()), "lmoe_route")
+    return idx, w
 
 
 _route_ws: dict[int, Workspace] = {}
