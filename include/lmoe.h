@@ -140,6 +140,28 @@ int lmoe_moe_layer_staged(const lmoe_layer *layer, const void *x, int32_t tokens
                           size_t ws_bytes, void *stream, void *ev_routed,
                           void *ev_gateup);
 
+/* Allocation-free lmoe_moe_layer.  No counterpart in the reference: it exists
+ * for callers that cannot allocate device memory for a workspace (a serving
+ * loop whose device memory belongs to another allocator, a runtime that
+ * forbids allocation on its request path, a binding without a device
+ * allocator).  Scratch lives in a static device array of
+ * LMOE_STATIC_WORKSPACE_BYTES (8 MiB), held by every GPU that loads the
+ * library until the process exits; layers whose workspace would exceed it
+ * (lmoe_workspace_size > 8 MiB, about 80 decode tokens at DeepSeek-V4-Flash
+ * shapes) are rejected with LMOE_EWORKSPACE before anything is enqueued.  The
+ * first call on a device looks up the array's device address with that
+ * device current; make that first call before any stream capture.  The call
+ * allocates nothing (no cudaMalloc/cudaFree), zeroes the array's counters on
+ * the stream, then runs the same kernels as lmoe_moe_layer.  All calls on a
+ * device share the one array and it keeps the last call's contents, so calls
+ * that overlap on the GPU (different streams, or concurrent host threads
+ * without ordering) race and corrupt each other's results. */
+#define LMOE_STATIC_WORKSPACE_BYTES (8u << 20)
+int lmoe_moe_layer_static(const lmoe_layer *layer, const void *x,
+                          int32_t tokens, void *out, int32_t *idx, float *w,
+                          void *stream);
+size_t lmoe_static_workspace_bytes(void);
+
 /* Same layer with routing supplied by the caller (an external gate, as
  * V4ArenaMoE.route returns it): idx [T, top_k] expert ids, w [T, top_k]
  * fp32 weights (arena.py:512-546). */

@@ -1,6 +1,7 @@
 // C ABI of liblmoe.so (declared in include/lmoe.h).  Host-side validation,
 // workspace layout and kernel sequencing; no allocation, no host sync.
 #include <cstring>
+#include <mutex>
 
 #include "../../include/lmoe.h"
 #include "lmoe_kernels.cuh"
@@ -369,6 +370,67 @@ int lmoe_moe_layer_staged(const lmoe_layer *layer, const void *x, int32_t tokens
 int lmoe_moe_layer(const lmoe_layer *layer, const void *x, int32_t tokens, void *out, int32_t *idx,
                    float *w, void *workspace, size_t ws_bytes, void *stream) {
     return lmoe_moe_layer_staged(layer, x, tokens, out, idx, w, workspace, ws_bytes, stream, nullptr, nullptr);
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------ allocation-free layer
+// Some callers cannot allocate device memory for a workspace: a serving loop
+// whose device memory is owned by another allocator, a host runtime that
+// forbids allocation on its request path, or a foreign-language binding with
+// no device allocator at all.  lmoe_moe_layer_static serves them by keeping
+// its scratch in this file-scope device array, which every GPU that loads
+// the library holds until the process exits.
+static __device__ __align__(256) uint8_t g_lmoe_static_ws[LMOE_STATIC_WORKSPACE_BYTES];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_static_mu;
+void *g_static_ptr[kMaxDevices] = {};
+
+// Device address of the static scratch on the current device.  In host code
+// the array's name is only a host-side stand-in, so the address is looked up
+// once per device with that device current.
+int static_workspace(void **out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return LMOE_ECUDA;
+    if (dev < 0 || dev >= kMaxDevices) return LMOE_EUNSUPPORTED;
+    std::lock_guard<std::mutex> lock(g_static_mu);
+    if (!g_static_ptr[dev]) {
+        void *p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_lmoe_static_ws) != cudaSuccess || !p) return LMOE_ECUDA;
+        g_static_ptr[dev] = p;
+    }
+    *out = g_static_ptr[dev];
+    return LMOE_OK;
+}
+}  // namespace
+
+extern "C" {
+
+size_t lmoe_static_workspace_bytes(void) { return LMOE_STATIC_WORKSPACE_BYTES; }
+
+int lmoe_moe_layer_static(const lmoe_layer *layer, const void *x, int32_t tokens, void *out, int32_t *idx,
+                          float *w, void *stream) {
+    int rc = check_layer(layer);
+    if (rc) return rc;
+    if (tokens < 0 || (tokens > 0 && (!x || !out))) return LMOE_EINVAL;
+    if (tokens == 0) return LMOE_OK;
+    if (layer->experts.hidden % kRouterKS) return LMOE_EUNSUPPORTED;
+    const Layout L = layer_layout(layer, tokens);
+    if (L.total > LMOE_STATIC_WORKSPACE_BYTES) return LMOE_EWORKSPACE;
+    void *ws = nullptr;
+    rc = static_workspace(&ws);
+    if (rc) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // The array keeps whatever the previous call left in it: zero the words
+    // that must start at zero (error flag, router block counter, combine
+    // counters) before this call's kernels run.
+    const size_t cnt_bytes = (size_t)tokens * (layer->experts.hidden / 16) * sizeof(uint32_t);
+    if (cudaMemsetAsync(at<uint8_t>(ws, L.status), 0, 256, st) != cudaSuccess ||
+        cudaMemsetAsync(at<uint8_t>(ws, L.cnt), 0, cnt_bytes, st) != cudaSuccess)
+        return LMOE_ECUDA;
+    return lmoe_moe_layer(layer, x, tokens, out, idx, w, ws, LMOE_STATIC_WORKSPACE_BYTES, stream);
 }
 
 int lmoe_moe_routed(const lmoe_layer *layer, const void *x, int32_t tokens, const int32_t *idx,

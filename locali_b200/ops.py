@@ -208,6 +208,20 @@ class MoEKernel:
                                     _ptr(w), self.ws.ptr(), self.ws.nbytes, _stream()), "lmoe_moe_layer")
         return out.reshape(x.shape)
 
+    def call_static(self, x: torch.Tensor, out: torch.Tensor | None = None, idx: torch.Tensor | None = None,
+                    w: torch.Tensor | None = None) -> torch.Tensor:
+        """The layer through ``lmoe_moe_layer_static``: no workspace is
+        allocated; the library's fixed 8 MiB device scratch is used instead
+        (for callers that cannot allocate device memory).  Calls that overlap
+        on the GPU share that scratch and must not run concurrently."""
+        flat = self._x(x)
+        T = flat.shape[0]
+        if out is None:
+            out = torch.empty_like(flat)
+        check(lmoe().lmoe_moe_layer_static(ctypes.byref(self.desc), flat.data_ptr(), T, out.data_ptr(), _ptr(idx),
+                                           _ptr(w), _stream()), "lmoe_moe_layer_static")
+        return out.reshape(x.shape)
+
     def staged(self, x: torch.Tensor, out: torch.Tensor, ev_routed: torch.cuda.Event,
                ev_gateup: torch.cuda.Event, idx: torch.Tensor | None = None) -> torch.Tensor:
         """The layer with CUDA events recorded after routing and after gate/up
