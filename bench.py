@@ -58,11 +58,15 @@ def parse():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--config", default="c1")
     p.add_argument("--tokens", type=int, default=None)
+    p.add_argument("--experts", type=int, default=None,
+                   help="override the expert count (small cases for profiler captures)")
     p.add_argument("--layers", type=int, default=0, help="distinct layers cycled (0 = auto)")
     p.add_argument("--e2e-steps", type=int, default=200)
     p.add_argument("--kernel-steps", type=int, default=200)
     p.add_argument("--cpu-sample", type=int, default=2, help="tokens timed for the CPU baseline")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--layout", choices=["tiled", "rowmajor"], default="tiled",
+                   help="expert weights in HBM: pre-tiled (one bulk copy per 16-row tile) or the row-major arrays")
     return p.parse_args()
 
 
@@ -218,10 +222,18 @@ def run_ours(args):
 
     from locali_b200 import ops, synth
 
-    cfg = synth.config(args.config) if args.tokens is None else synth.config(args.config, tokens=args.tokens)
+    over = {}
+    if args.tokens is not None:
+        over["tokens"] = args.tokens
+    if args.experts is not None:
+        over["n_experts"] = args.experts
+    cfg = synth.config(args.config, **over)
     T = cfg.tokens
     n_layers = args.layers or 16
     layers = [synth.make_layer(cfg, seed=1000 * rank + i, device=dev) for i in range(n_layers)]
+    if args.layout == "tiled":
+        for l in layers:
+            l.experts.pack_tiles()
     kerns = [ops.MoEKernel(l.router, l.experts, l.expert_slot, cfg.swiglu_limit) for l in layers]
     K, W = args.steps, args.warmup
     g = torch.Generator(device=dev).manual_seed(77 + rank)
@@ -296,7 +308,7 @@ def run_ours(args):
 
     # ---- e2e through the public module API with host buffers
     e2e = None
-    if rank == 0 or world > 1:
+    if args.e2e_steps > 0:
         e2e = run_e2e(args, cfg, layers, n_layers, dev)
 
     if rank != 0:
@@ -323,6 +335,7 @@ def run_ours(args):
             "layers_cycled": n_layers,
             "l2": f"{n_layers} distinct layers cycled; >{4 * 126} MB of expert bytes touched between reuses",
             "weights": f"{cfg.bits_gate}-bit affine g{cfg.group_size} (uint32 codes, bf16 scales/biases)",
+            "layout": args.layout,
         },
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": traffic, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",

@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define LMOE_ABI_VERSION 1
+#define LMOE_ABI_VERSION 2
 
 /* status codes */
 #define LMOE_OK 0
@@ -61,6 +61,12 @@ typedef struct lmoe_qproj {
     const void *biases;     /* [n_slots, rows, cols/group_size] */
     int32_t bits;           /* 2, 4 or 8 */
     int32_t group_size;     /* 64 or 128 (32 for 4- and 8-bit) */
+    /* Optional pre-tiled copy of all slots (lmoe_tile_pack), 16-byte aligned,
+     * lmoe_tile_bytes() per slot; NULL = stream the row-major arrays above.
+     * When set, the expert GEMVs read only this copy (weight/scales/biases
+     * may then be NULL).  No counterpart in the reference: its arena keeps the
+     * row-major MLX arrays only. */
+    const void *tiles;
 } lmoe_qproj;
 
 /* The routed experts of one tier: SwitchGLU gate/up [inter, hidden] and
@@ -97,6 +103,12 @@ typedef struct lmoe_layer {
 /* ABI version and error text. */
 int lmoe_version(void);
 const char *lmoe_strerror(int status);
+
+/* Profiling aid (not part of the reference interface): while buf is non-NULL,
+ * every gate/up expert kernel launched by lmoe_moe_layer* records
+ * %globaltimer stamps into buf[block][unit][8] (units_per_block units per
+ * block; device memory owned by the caller).  Pass NULL to stop. */
+void lmoe_profile_trace(uint64_t *buf, int32_t units_per_block);
 
 /* Bytes of workspace needed for up to max_tokens tokens of this layer. */
 size_t lmoe_workspace_size(const lmoe_layer *layer, int32_t max_tokens);
@@ -189,6 +201,22 @@ int lmoe_gather_qmm(const lmoe_qproj *proj, int32_t n_slots, int32_t rows,
 /* Workspace bytes for lmoe_gateup_swiglu / lmoe_gather_qmm calls. */
 size_t lmoe_workspace_size_routes(int32_t max_routes, int32_t hidden,
                                   int32_t inter, int32_t n_slots);
+
+/* Pre-tiled weight format (no counterpart in the reference, whose arena
+ * holds row-major MLX arrays, arena.py:96-150).  A projection [rows, cols]
+ * of one slot becomes rows/16 tiles of lmoe_tile_bytes()/(rows/16) bytes:
+ * the 16 rows' codes, scales and biases contiguous and pre-swizzled, so the
+ * decode GEMV moves each tile with one bulk copy.  Returns bytes per slot,
+ * 0 when the geometry has no tile layout. */
+size_t lmoe_tile_bytes(int32_t rows, int32_t cols, int32_t bits,
+                       int32_t group_size);
+
+/* Pack slots [slot_begin, slot_begin + slot_count) of the row-major
+ * projection src (weight/scales/biases, 16-byte aligned) into tiles (slot 0
+ * at tiles, lmoe_tile_bytes() per slot).  Asynchronous on stream. */
+int lmoe_tile_pack(const lmoe_qproj *src, int32_t n_slots, int32_t rows,
+                   int32_t cols, int32_t slot_begin, int32_t slot_count,
+                   void *tiles, void *stream);
 
 #ifdef __cplusplus
 }

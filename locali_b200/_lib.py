@@ -34,6 +34,7 @@ class QProj(ctypes.Structure):
         ("biases", ctypes.c_void_p),
         ("bits", ctypes.c_int32),
         ("group_size", ctypes.c_int32),
+        ("tiles", ctypes.c_void_p),
     ]
 
 
@@ -101,6 +102,9 @@ _SIGS = {
                             ctypes.c_int32, _VP, _VP, ctypes.c_size_t, _VP], ctypes.c_int),
     "lmoe_gather_qmm": ([ctypes.POINTER(QProj), ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                          _VP, ctypes.c_int32, _VP, _VP, _VP, ctypes.c_size_t, _VP], ctypes.c_int),
+    "lmoe_tile_bytes": ([ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32], ctypes.c_size_t),
+    "lmoe_tile_pack": ([ctypes.POINTER(QProj), ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                        ctypes.c_int32, _VP, _VP], ctypes.c_int),
 }
 
 CORE_SYMBOLS = [
@@ -131,7 +135,7 @@ def lmoe() -> ctypes.CDLL:
             fn = getattr(lib, name)
             fn.argtypes = args
             fn.restype = res
-        if lib.lmoe_version() != 1:
+        if lib.lmoe_version() != 2:
             raise RuntimeError("liblmoe.so ABI version mismatch; rebuild it")
         _lmoe = lib
     return _lmoe

@@ -17,6 +17,10 @@ bool gemv_ok(int bits, int gs) {
 
 size_t al(size_t v) { return (v + 255) & ~size_t(255); }
 
+// profiling timeline of the gate/up kernel (lmoe_profile_trace)
+uint64_t *g_trace = nullptr;
+int32_t g_trace_units = 0;
+
 struct Layout {
     size_t status = 0, partial = 0, idx = 0, w = 0, sorted = 0, counts = 0, roff = 0,
            nchunks = 0, chunks = 0, xpanel = 0, xsum = 0, hpanel = 0, hsum = 0, yw = 0,
@@ -26,7 +30,7 @@ struct Layout {
 
 int max_chunks_for(int buckets, int R) {
     const int distinct = buckets < R ? buckets : R;
-    return distinct + R / kChunkTok + 1;
+    return distinct + R + 1;  // any chunk size >= 1
 }
 
 // Layout shared by all entry points.  x_rows: rows of the input panel;
@@ -52,9 +56,9 @@ Layout make_layout(int T, int R, int K, int I, int H_out, int buckets, int E_rou
     L.max_chunks = max_chunks_for(buckets, R);
     L.chunks = take((size_t)L.max_chunks * sizeof(Chunk));
     L.xpanel = take((size_t)x_rows * K * 2);
-    L.xsum = take((size_t)x_rows * (K / 16) * 4);
+    L.xsum = take((size_t)x_rows * (K / 16) * 8);
     L.hpanel = take((size_t)R * I * 2);
-    L.hsum = take((size_t)R * (I / 16) * 4);
+    L.hsum = take((size_t)R * (I / 16) * 8);
     L.yw = take((size_t)R * H_out * 2);
     L.cnt = take((size_t)T * (H_out / 16) * 4);
     L.total = off;
@@ -64,7 +68,7 @@ Layout make_layout(int T, int R, int K, int I, int H_out, int buckets, int E_rou
 Layout layer_layout(const lmoe_layer *l, int T) {
     const int H = l->experts.hidden, I = l->experts.inter;
     const int R = T * l->router.top_k;
-    return make_layout(T, R, H, I, H, l->router.n_experts + 1, l->router.n_experts, H / kRouterKS, T);
+    return make_layout(T, R, H, I, H, l->router.n_experts + 1, l->router.n_experts, 1, T);
 }
 
 template <typename P>
@@ -83,12 +87,21 @@ QView view(const lmoe_qproj &p, int n_slots, int rows, int cols) {
     v.sb_slot_stride = (int64_t)rows * v.groups_per_row;
     v.rows = rows;
     v.cols = cols;
+    v.tiles = static_cast<const uint8_t *>(p.tiles);
+    TileGeo tg;
+    v.tile_slot_stride = tile_geo(cols, p.bits, p.group_size, &tg) ? (int64_t)(rows / 16) * tg.TB : 0;
     (void)n_slots;
     return v;
 }
 
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
 int check_proj(const lmoe_qproj &p, int rows, int cols) {
-    if (!p.weight || !p.scales || !p.biases) return LMOE_EINVAL;
+    if (p.tiles) {
+        if (!aligned16(p.tiles)) return LMOE_EINVAL;
+    } else if (!p.weight || !p.scales || !p.biases) {
+        return LMOE_EINVAL;
+    }
     if (!gemv_ok(p.bits, p.group_size)) return LMOE_EUNSUPPORTED;
     if (rows % 16 != 0 || cols % p.group_size != 0) return LMOE_EUNSUPPORTED;
     return LMOE_OK;
@@ -127,10 +140,11 @@ int cuda_rc(cudaError_t e) {
 
 // Runs dispatch for R routes into buckets [0, n_experts) (+ zero bucket).
 int run_dispatch(const Layout &L, void *ws, const int32_t *idx, int R, int n_experts,
-                 const int32_t *expert_slot, int n_slots, cudaStream_t st) {
+                 const int32_t *expert_slot, int n_slots, int chunk_tok, cudaStream_t st) {
     DispatchIn din;
     din.idx = idx;
     din.R = R;
+    din.chunk_tok = chunk_tok;
     din.n_experts = n_experts;
     din.expert_slot = expert_slot;
     din.n_slots = n_slots;
@@ -158,12 +172,30 @@ GemvArgs gemv_base(const Layout &L, void *ws, int n_slots, int ntok_max) {
     return a;
 }
 
+// Largest chunk (routes of one expert per unit, at most one MMA n-tile of 8)
+// whose shared-memory stages fit, capped by the routes one expert can get.
+int chunk_for(int mode, int bits, int gs, int K, int cap) {
+    int c = cap < kChunkTok ? cap : kChunkTok;
+    GemvCfg cfg;
+    while (c > 1 && !gemv_config(mode, bits, gs, K, c, &cfg)) --c;
+    if (c < 1 || !gemv_config(mode, bits, gs, K, c, &cfg)) return 0;
+    return c;
+}
+
+int layer_chunk(const lmoe_layer *l, int T) {
+    const lmoe_experts &ex = l->experts;
+    const int a = chunk_for(MODE_GATEUP, ex.gate.bits, ex.gate.group_size, ex.hidden, T);
+    const int b = chunk_for(MODE_DOWN, ex.down.bits, ex.down.group_size, ex.inter, T);
+    return a < b ? a : b;
+}
+
 // gate/up + SwiGLU then down + combine over an already dispatched layer.
 int run_experts(const lmoe_layer *l, const Layout &L, void *ws, int T, const float *route_w,
                 void *out, cudaStream_t st, cudaEvent_t ev_gateup = nullptr) {
     const lmoe_experts &ex = l->experts;
     const int H = ex.hidden, I = ex.inter, k = l->router.top_k;
-    const int ntok_max = T < kChunkTok ? T : kChunkTok;
+    const int ntok_max = layer_chunk(l, T);
+    if (ntok_max < 1) return LMOE_EUNSUPPORTED;
     GemvArgs gu = gemv_base(L, ws, ex.n_slots, ntok_max);
     gu.q0 = view(ex.gate, ex.n_slots, I, H);
     gu.q1 = view(ex.up, ex.n_slots, I, H);
@@ -177,6 +209,8 @@ int run_experts(const lmoe_layer *l, const Layout &L, void *ws, int T, const flo
     gu.out_gs = ex.down.group_size;
     gu.limit = l->swiglu_limit;
     gu.swiglu_mode = l->swiglu_mode;
+    gu.trace = g_trace;
+    gu.trace_units = g_trace_units;
     int rc = cuda_rc(launch_gemv(MODE_GATEUP, ex.dtype == LMOE_F16, ex.gate.bits, ex.gate.group_size,
                                  gu, L.max_chunks, st));
     if (rc) return rc;
@@ -200,6 +234,11 @@ int run_experts(const lmoe_layer *l, const Layout &L, void *ws, int T, const flo
 extern "C" {
 
 int lmoe_version(void) { return LMOE_ABI_VERSION; }
+
+void lmoe_profile_trace(uint64_t *buf, int32_t units_per_block) {
+    g_trace = buf;
+    g_trace_units = buf ? units_per_block : 0;
+}
 
 const char *lmoe_strerror(int status) {
     switch (status) {
@@ -253,7 +292,9 @@ static int route_impl(const lmoe_router &r, int H, int dtype, const lmoe_layer *
                       int T, int32_t *idx_user, float *w_user, void *ws, cudaStream_t st) {
     const int k = r.top_k;
     const int R = T * k;
-    const int ksplit = H / kRouterKS;
+    const int ksplit = 1;
+    const int chunk_tok = l ? layer_chunk(l, T) : kChunkTok;
+    if (chunk_tok < 1) return LMOE_EUNSUPPORTED;
     RouterArgs a;
     std::memset(&a, 0, sizeof(a));
     a.x = static_cast<const uint16_t *>(x);
@@ -282,6 +323,7 @@ static int route_impl(const lmoe_router &r, int H, int dtype, const lmoe_layer *
     a.err = at<int32_t>(ws, L.status);
     a.din.idx = a.idx_ws;
     a.din.R = R;
+    a.din.chunk_tok = chunk_tok;
     a.din.n_experts = a.E;
     a.din.expert_slot = l ? l->expert_slot : nullptr;
     a.din.n_slots = l ? l->experts.n_slots : 0;
@@ -299,7 +341,7 @@ static int route_impl(const lmoe_router &r, int H, int dtype, const lmoe_layer *
     if (!small_topk) {
         TopkArgs tk;
         tk.partial = a.partial;
-        tk.ksplit = ksplit;
+        tk.ksplit = 1;
         tk.T = T;
         tk.E = a.E;
         tk.top_k = k;
@@ -315,7 +357,7 @@ static int route_impl(const lmoe_router &r, int H, int dtype, const lmoe_layer *
         if (rc) return rc;
     }
     if (!l || a.do_dispatch) return LMOE_OK;
-    return run_dispatch(L, ws, a.idx_ws, R, a.E, l->expert_slot, l->experts.n_slots, st);
+    return run_dispatch(L, ws, a.idx_ws, R, a.E, l->expert_slot, l->experts.n_slots, chunk_tok, st);
 }
 
 int check_router(const lmoe_router *r, int hidden) {
@@ -331,7 +373,7 @@ size_t lmoe_workspace_size_route(const lmoe_router *router, int32_t hidden, int3
     if (check_router(router, hidden) || max_tokens < 0) return 0;
     const int T = max_tokens > 0 ? max_tokens : 1;
     return make_layout(T, T * router->top_k, 0, 0, 0, router->n_experts + 1, router->n_experts,
-                       hidden / kRouterKS, 0).total;
+                       1, 0).total;
 }
 
 int lmoe_route(const lmoe_router *router, int32_t hidden, int32_t dtype, const void *x, int32_t tokens,
@@ -342,7 +384,7 @@ int lmoe_route(const lmoe_router *router, int32_t hidden, int32_t dtype, const v
     if (tokens < 0 || (tokens > 0 && (!x || !idx || !w || !workspace))) return LMOE_EINVAL;
     if (tokens == 0) return LMOE_OK;
     const Layout L = make_layout(tokens, tokens * router->top_k, 0, 0, 0, router->n_experts + 1,
-                                 router->n_experts, hidden / kRouterKS, 0);
+                                 router->n_experts, 1, 0);
     if (ws_bytes < L.total) return LMOE_EWORKSPACE;
     return route_impl(*router, hidden, dtype, nullptr, L, x, tokens, idx, w, workspace,
                       static_cast<cudaStream_t>(stream));
@@ -455,7 +497,9 @@ int lmoe_moe_routed(const lmoe_layer *layer, const void *x, int32_t tokens, cons
     rc = cuda_rc(launch_panel(pa, st));
     if (rc) return rc;
     const int R = tokens * layer->router.top_k;
-    rc = run_dispatch(L, workspace, idx, R, layer->router.n_experts, layer->expert_slot, ex.n_slots, st);
+    const int ct = layer_chunk(layer, tokens);
+    if (ct < 1) return LMOE_EUNSUPPORTED;
+    rc = run_dispatch(L, workspace, idx, R, layer->router.n_experts, layer->expert_slot, ex.n_slots, ct, st);
     if (rc) return rc;
     return run_experts(layer, L, workspace, tokens, w, out, st);
 }
@@ -493,10 +537,11 @@ int lmoe_gateup_swiglu(const lmoe_experts *experts, const void *x, int32_t token
     pa.act_f16 = experts->dtype == LMOE_F16;
     rc = cuda_rc(launch_panel(pa, st));
     if (rc) return rc;
+    const int ntok_max = chunk_for(MODE_GATEUP, experts->gate.bits, experts->gate.group_size, H, tokens);
+    if (ntok_max < 1) return LMOE_EUNSUPPORTED;
     rc = run_dispatch(L, workspace, reinterpret_cast<const int32_t *>(slots), R, experts->n_slots,
-                      nullptr, experts->n_slots, st);
+                      nullptr, experts->n_slots, ntok_max, st);
     if (rc) return rc;
-    const int ntok_max = tokens < kChunkTok ? tokens : kChunkTok;
     GemvArgs gu = gemv_base(L, workspace, experts->n_slots, ntok_max);
     gu.q0 = view(experts->gate, experts->n_slots, I, H);
     gu.q1 = view(experts->up, experts->n_slots, I, H);
@@ -534,10 +579,11 @@ int lmoe_gather_qmm(const lmoe_qproj *proj, int32_t n_slots, int32_t rows, int32
     pa.act_f16 = dtype == LMOE_F16;
     rc = cuda_rc(launch_panel(pa, st));
     if (rc) return rc;
+    const int ntok_max = chunk_for(MODE_QMM, proj->bits, proj->group_size, cols, routes);
+    if (ntok_max < 1) return LMOE_EUNSUPPORTED;
     rc = run_dispatch(L, workspace, reinterpret_cast<const int32_t *>(slots), routes, n_slots, nullptr,
-                      n_slots, st);
+                      n_slots, ntok_max, st);
     if (rc) return rc;
-    const int ntok_max = routes < kChunkTok ? routes : kChunkTok;
     GemvArgs q = gemv_base(L, workspace, n_slots, ntok_max);
     q.q0 = view(*proj, n_slots, rows, cols);
     q.panel = pa.panel;
@@ -545,6 +591,28 @@ int lmoe_gather_qmm(const lmoe_qproj *proj, int32_t n_slots, int32_t rows, int32
     q.route_div = 1;
     q.out = static_cast<uint16_t *>(y);
     return cuda_rc(launch_gemv(MODE_QMM, pa.act_f16, proj->bits, proj->group_size, q, L.max_chunks, st));
+}
+
+size_t lmoe_tile_bytes(int32_t rows, int32_t cols, int32_t bits, int32_t group_size) {
+    if (rows <= 0 || rows % 16 != 0 || group_size <= 0 || cols <= 0 || cols % group_size != 0) return 0;
+    if (!gemv_ok(bits, group_size)) return 0;
+    TileGeo tg;
+    if (!tile_geo(cols, bits, group_size, &tg)) return 0;
+    return (size_t)(rows / 16) * (size_t)tg.TB;
+}
+
+int lmoe_tile_pack(const lmoe_qproj *src, int32_t n_slots, int32_t rows, int32_t cols, int32_t slot_begin,
+                   int32_t slot_count, void *tiles, void *stream) {
+    if (!src || !tiles || !src->weight || !src->scales || !src->biases) return LMOE_EINVAL;
+    if (n_slots < 1 || slot_begin < 0 || slot_count < 0 || slot_begin + slot_count > n_slots) return LMOE_EINVAL;
+    if (!aligned16(src->weight) || !aligned16(src->scales) || !aligned16(src->biases) || !aligned16(tiles))
+        return LMOE_EINVAL;
+    if (lmoe_tile_bytes(rows, cols, src->bits, src->group_size) == 0) return LMOE_EUNSUPPORTED;
+    lmoe_qproj p = *src;
+    p.tiles = tiles;
+    const QView q = view(p, n_slots, rows, cols);
+    return cuda_rc(launch_tile_pack(q, src->bits, src->group_size, slot_begin, slot_count,
+                                    static_cast<uint8_t *>(tiles), static_cast<cudaStream_t>(stream)));
 }
 
 }  // extern "C"

@@ -44,6 +44,10 @@ struct QView {
     int32_t groups_per_row;
     int32_t rows;
     int32_t cols;
+    // optional pre-tiled copy ([slot][rows/16][tile_bytes], see TileGeo):
+    // when set, the GEMV streams whole tiles with bulk copies
+    const uint8_t *tiles;
+    int64_t tile_slot_stride;  // bytes per slot
 };
 
 // ------------------------------------------------------------ dtype traits
@@ -142,9 +146,9 @@ __host__ __device__ __forceinline__ int panel_pos(int col, int bits, int gs, int
     const int m = j % half_n, half = j / half_n;
     const int s = wi * (cpw >> 2) + (m >> 1);
     const int reg = m & 1;
-    const int kstep = G * (gs >> 4) + s;
     *p_out = (bits == 2) ? pmap2(m) : 0;
-    return ((kstep * 4 + t) * 4) + reg * 2 + half;
+    // [group][lane slot t][k-step s][4 values]: one lane's steps are contiguous
+    return (((G * 4 + t) * (gs >> 4) + s) * 4) + reg * 2 + half;
 }
 
 // Unpack one 32-bit word of codes into kCpw/2 pairs of exact small integers
@@ -192,6 +196,47 @@ struct Unpack<TA, 8> {
         const float c3 = __uint_as_float(0x4B000000u | (w >> 24)) - 8388608.0f;
         P[0] = Act<TA>::pack2(c0, c2);
         P[1] = Act<TA>::pack2(c1, c3);
+    }
+};
+
+// On-demand pair extraction for the MMA A operand.  prep() runs once per code
+// word, get(w, m) yields pair m (c_m, c_{m+kCpw/2}) as packed 16-bit values.
+// For 2- and 4-bit codes the pair keeps the magic offset (value kMagicVal +
+// c*4^p resp. kMagicVal + c); the consumer removes kMagicVal * sum(panel) per
+// group after the MMA instead of subtracting it from every pair.
+template <typename TA, int BITS>
+struct PairX;
+
+template <typename TA>
+struct PairX<TA, 2> {
+    struct W {
+        uint32_t v0, v1, v2;
+    };
+    __device__ __forceinline__ static W prep(uint32_t w) { return W{w, w >> 6, w >> 12}; }
+    __device__ __forceinline__ static uint32_t get(const W &w, int m) {
+        const uint32_t v = m < 3 ? w.v0 : (m < 6 ? w.v1 : w.v2);
+        return (v & (0x00030003u << (2 * (m % 3)))) | Act<TA>::kMagic;
+    }
+};
+
+template <typename TA>
+struct PairX<TA, 4> {
+    using W = uint32_t;
+    __device__ __forceinline__ static W prep(uint32_t w) { return w; }
+    __device__ __forceinline__ static uint32_t get(W w, int m) {
+        return ((w >> (4 * m)) & 0x000F000Fu) | Act<TA>::kMagic;
+    }
+};
+
+template <typename TA>
+struct PairX<TA, 8> {
+    using W = uint32_t;
+    __device__ __forceinline__ static W prep(uint32_t w) { return w; }
+    __device__ __forceinline__ static uint32_t get(W w, int m) {
+        // exact small integers through the fp32 magic 2^23
+        const float lo = __uint_as_float(0x4B000000u | ((w >> (8 * m)) & 0xFFu)) - 8388608.0f;
+        const float hi = __uint_as_float(0x4B000000u | ((w >> (8 * m + 16)) & 0xFFu)) - 8388608.0f;
+        return Act<TA>::pack2(lo, hi);
     }
 };
 
@@ -256,20 +301,46 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
                  "r"(bytes)
                  : "memory");
 }
-// Bounded wait on an mbarrier phase.  Returns false if the wait gave up.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
-    uint32_t done = 0;
-    for (uint32_t it = 0; it < (1u << 26); ++it) {
-        asm volatile(
-            "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; "
-            "selp.u32 %0, 1, 0, p; }"
-            : "=r"(done)
-            : "r"(smem_u32(bar)), "r"(parity)
-            : "memory");
-        if (done) return true;
-    }
-    return false;
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+// Wait on an mbarrier phase, bounded by wall time (kWaitLimitNs).  Returns
+// false if the wait gave up; the caller records an error and stops instead of
+// hanging the GPU.  Between polls the warp sleeps (32 ns doubling to 256 ns):
+// a warp polling flat out takes issue slots from the warps of its
+// sub-partition that do the math.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+__device__ __forceinline__ bool mbar_try(uint64_t *bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; "
+        "selp.u32 %0, 1, 0, p; }"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+    if (mbar_try(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    uint32_t ns = 32;
+    for (;;) {
+        __nanosleep(ns);
+        if (mbar_try(bar, parity)) return true;
+        if (ns < 256) ns <<= 1;
+        if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    }
+}
+
+// XOR swizzle of 16-byte chunks inside each 128-byte line of a shared-memory
+// tile: rows stay contiguous (so 16-byte cp.async of a row writes whole lines)
+// while the consumers' per-row reads land in distinct bank groups.
+__device__ __forceinline__ int swz(int o, int f) { return o ^ (f << 4); }
 // Plain (non-multicast) bulk copy global -> shared, completion on mbarrier.
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes,
                                          uint64_t *bar) {
@@ -278,6 +349,21 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
             smem_u32(dst)),
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
+}
+// 16-byte asynchronous global->shared copy (L2 only, evict-first policy for
+// streamed weights) and the arrive that fires when this thread's copies land.
+__device__ __forceinline__ void cp_async16(void *dst, const void *src, uint64_t policy) {
+    asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
+                 "l"(policy)
+                 : "memory");
+}
+__device__ __forceinline__ uint64_t evict_first_policy() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t *bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 __device__ __forceinline__ void fence_proxy_async() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

@@ -8,6 +8,62 @@ namespace lmoe {
 
 enum GemvMode { MODE_GATEUP = 0, MODE_DOWN = 1, MODE_QMM = 2 };
 
+// Geometry of one 16-row weight tile as the GEMV consumers read it from
+// shared memory: [codes 16 x RB][scales 16 x SB][biases 16 x SB], padded to
+// 128 bytes.  Rows are contiguous; inside each 128-byte line the 16-byte
+// chunks of row r are XOR-swizzled (codes by r & 7, scale/bias rows by r) so
+// the rows a warp reads at once fall in distinct bank groups.  The same
+// layout is the pre-tiled HBM format, so one bulk copy moves a tile.
+struct TileGeo {
+    int32_t RB, SB;        // code / scale bytes per row
+    int32_t rb_l2, sb_l2;  // log2(16-byte chunks per row); sb_l2 < 0: rows < 16 B
+    int32_t fm_c, fm_s;    // swizzle masks
+    int32_t tS, tB, TB;    // scale and bias offsets, padded tile bytes
+};
+
+__host__ __device__ inline int tile_log2_exact(int v) {
+    int l = 0;
+    while ((1 << l) < v) ++l;
+    return (1 << l) == v ? l : -1;
+}
+
+// false when (K, bits, gs) has no tile layout (rows must be a power-of-two
+// number of 16-byte chunks)
+__host__ __device__ inline bool tile_geo(int K, int bits, int gs, TileGeo *g) {
+    TileGeo t;
+    t.RB = K * bits / 8;
+    t.SB = (K / gs) * 2;
+    if (t.RB < 16 || t.RB % 16) return false;
+    t.rb_l2 = tile_log2_exact(t.RB / 16);
+    if (t.rb_l2 < 0) return false;
+    t.fm_c = (t.RB < 128 ? t.RB : 128) / 16 - 1;
+    if (t.SB >= 16) {
+        t.sb_l2 = tile_log2_exact(t.SB / 16);
+        if (t.sb_l2 < 0) return false;
+        t.fm_s = (t.SB < 128 ? t.SB : 128) / 16 - 1;
+    } else {
+        t.sb_l2 = -1;  // rows shorter than a chunk: the 16-row block is stored unswizzled
+        t.fm_s = 0;
+    }
+    t.tS = 16 * t.RB;
+    t.tB = t.tS + 16 * t.SB;
+    t.TB = (t.tB + 16 * t.SB + 127) / 128 * 128;
+    *g = t;
+    return true;
+}
+
+// Byte offset inside a tile of 16-byte chunk i of the code block (chunks in
+// row-major order, 2^rb_l2 per row).
+__host__ __device__ inline int tile_code_chunk(const TileGeo &t, int i) {
+    const int row = i >> t.rb_l2;
+    return (i << 4) ^ (((row & 7) & t.fm_c) << 4);
+}
+// Byte offset, relative to the scale (or bias) block, of its 16-byte chunk i.
+__host__ __device__ inline int tile_sb_chunk(const TileGeo &t, int i) {
+    if (t.sb_l2 < 0) return i << 4;
+    return (i << 4) ^ ((((i >> t.sb_l2)) & t.fm_s) << 4);
+}
+
 struct DispatchOut {
     int32_t *sorted_routes;  // [R]
     Chunk *chunks;           // [max_chunks]
@@ -19,6 +75,7 @@ struct DispatchOut {
 struct DispatchIn {
     const int32_t *idx;          // [R] expert id (or slot) per route
     int32_t R;
+    int32_t chunk_tok;           // routes per chunk (1..8)
     int32_t n_experts;           // valid ids are [0, n_experts); others -> zero bucket
     const int32_t *expert_slot;  // [n_experts] or nullptr (identity: id is the slot)
     int32_t n_slots;
@@ -34,7 +91,7 @@ struct RouterArgs {
     float *partial;  // [ksplit][T][E]
     // panel producer for the gate/up consumer (optional)
     uint16_t *xpanel;
-    float *xsum16;
+    float *xsum16;  // [T, H/16, 2]: per 16 columns, sum of x and sum of the stored panel values
     int32_t pbits, pgs;
     int32_t act_f16;
     // finisher (decode regime): last CTA runs top-k + dispatch
@@ -65,7 +122,7 @@ struct PanelArgs {
     const uint16_t *x;  // natural [rows, K]
     int32_t rows, K;
     uint16_t *panel;    // [rows, K]
-    float *sum16;       // [rows, K/16]
+    float *sum16;       // [rows, K/16, 2] (sum of x, sum of panel values)
     int32_t bits, gs;
     int32_t act_f16;
 };
@@ -73,7 +130,7 @@ struct PanelArgs {
 struct GemvArgs {
     QView q0, q1;
     const uint16_t *panel;
-    const float *sum16;
+    const float *sum16;  // [routes or tokens, K/16, 2]
     int32_t route_div;
     const Chunk *chunks;
     const int32_t *n_chunks;
@@ -81,7 +138,7 @@ struct GemvArgs {
     int32_t n_slots;
     int32_t ntok_max;
     uint16_t *out;
-    float *out_sum16;
+    float *out_sum16;  // [routes, rows/16, 2]
     int32_t out_panel, out_bits, out_gs;
     float limit;
     int32_t swiglu_mode;
@@ -90,9 +147,40 @@ struct GemvArgs {
     uint32_t *counters;
     uint16_t *combined;
     int32_t *err;
+    // optional per-unit timeline (nanoseconds, %globaltimer) for profiling:
+    // [block][unit slot][8]; nullptr in normal use
+    uint64_t *trace;
+    int32_t trace_units;
 };
 
-// host-side launchers (lmoe_kernels.cu)
+// Shared-memory plan of one gemv launch (computed on the host, passed by value).
+struct GemvCfg {
+    int32_t ncw, nst, gw;                       // consumer warps, stages, groups per consumer
+    int32_t RB, SB, TBp;                        // code / scale bytes per row, tile stride (TileGeo)
+    int32_t rb_l2, sb_l2;                       // log2(16-byte chunks per row); sb_l2 < 0: rows < 16 B
+    int32_t fm_c, fm_s;                         // swizzle masks of code / scale tiles
+    int32_t PB, PBp, S16B;                      // panel row bytes, padded stride, sum16 row bytes
+    int32_t off_codes, off_s, off_b;            // matrix m's tile at off_codes + m * TBp
+    int32_t off_panel, off_sum, stage_bytes;
+    int32_t off_bars, off_shdr, off_rhdr, off_red, off_xs, off_list, off_ptab, off_stage, smem, list_cap;
+};
+// Consumer warps per block: two per SM sub-partition.  Legacy mma.sync
+// throughput per sub-partition falls to less than half when four warps
+// interleave MMAs with the code-extraction ALU work (measured on B200).
+constexpr int kGemvMaxConsumers = 8;
+constexpr int kGemvEpi = 4;  // epilogue warps
+constexpr int kGemvMaxThreads = (kGemvMaxConsumers + 2 + kGemvEpi) * 32;  // + 2 producer warps
+constexpr int kGemvMaxStages = 4;
+// per-stage header (ints): [0] ntok, [1] row tile, [2] slot, then the
+// routes, their combine weights and the activation rows held by the stage
+constexpr int kHdrBytes = 128;
+constexpr int kHdrRoute = 4;
+constexpr int kHdrWeight = 12;
+constexpr int kHdrPanel = 20;
+constexpr int kHdrPanelN = 28;
+bool gemv_config(int mode, int bits, int gs, int K, int ntok_max, GemvCfg *out);
+
+// host-side launchers (lmoe_route.cu, lmoe_gemv.cu)
 cudaError_t launch_router(const RouterArgs &a, int ksplit, cudaStream_t st);
 cudaError_t launch_topk(const TopkArgs &a, cudaStream_t st);
 cudaError_t launch_dispatch_small(const DispatchIn &din, const DispatchOut &dout, int32_t *err,
@@ -103,6 +191,9 @@ cudaError_t launch_panel(const PanelArgs &a, cudaStream_t st);
 // returns cudaErrorInvalidValue for an unsupported (bits, gs)
 cudaError_t launch_gemv(int mode, int act_f16, int bits, int gs, const GemvArgs &a,
                         int max_chunks, cudaStream_t st);
+// row-major slots [slot_begin, slot_begin + slot_count) of q -> tiles
+cudaError_t launch_tile_pack(const QView &q, int bits, int gs, int slot_begin, int slot_count, uint8_t *tiles,
+                             cudaStream_t st);
 
 constexpr int kDispatchSmallMaxRoutes = 512;
 constexpr int kDispatchSmallMaxBuckets = 1024;

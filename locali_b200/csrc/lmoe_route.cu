@@ -1,0 +1,563 @@
+// Routing kernels for sm_100a: router logits + top-k, dispatch (routes grouped
+// by expert into chunks) and the activation panel producer.
+#include <float.h>
+
+#include "lmoe_kernels.cuh"
+
+namespace lmoe {
+
+#define LMOE_FULL 0xffffffffu
+
+// ============================================================ block utilities
+// Exclusive scan of one int per thread over a 256-thread block.
+__device__ int block_scan_256(int v, int *s_tmp /*[9]*/, int *total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(LMOE_FULL, incl, o);
+        if (lane >= o) incl += n;
+    }
+    if (lane == 31) s_tmp[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        int w = (lane < 8) ? s_tmp[lane] : 0;
+        int wi = w;
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1) {
+            const int n = __shfl_up_sync(LMOE_FULL, wi, o);
+            if (lane >= o) wi += n;
+        }
+        if (lane < 8) s_tmp[lane] = wi - w;  // exclusive per warp
+        if (lane == 7) s_tmp[8] = wi;
+    }
+    __syncthreads();
+    const int out = s_tmp[warp] + incl - v;
+    *total = s_tmp[8];
+    __syncthreads();
+    return out;
+}
+
+// ============================================================ dispatch
+// Groups routes by expert (stable in route order) and cuts each expert's run
+// into chunks of at most 8 routes.  Replaces the host loop of
+// arena.py:557-566 and the slot sort of arena.py:650-659.  Runs on one
+// 256-thread block; R <= kDispatchSmallMaxRoutes, buckets <= 1024.
+__device__ void dispatch_block(const DispatchIn &din, const DispatchOut &dout, int32_t *err,
+                               int *s_mem) {
+    const int tid = threadIdx.x;
+    const int R = din.R;
+    const int E = din.n_experts;
+    const int NBk = E + 1;  // last bucket collects invalid ids (zero slot)
+    int *s_b = s_mem;                                  // [512]
+    int *s_cnt = s_b + kDispatchSmallMaxRoutes;        // [1025]
+    int *s_roff = s_cnt + kDispatchSmallMaxBuckets + 1;
+    int *s_coff = s_roff + kDispatchSmallMaxBuckets + 1;
+    int *s_tmp = s_coff + kDispatchSmallMaxBuckets + 1;  // [9]
+    for (int i = tid; i < NBk; i += blockDim.x) s_cnt[i] = 0;
+    __syncthreads();
+    for (int r = tid; r < R; r += blockDim.x) {
+        const int id = din.idx[r];
+        int b = id;
+        if (id < 0 || id >= E) {
+            b = E;
+            set_error(err, -3);
+        }
+        s_b[r] = b;
+        atomicAdd(&s_cnt[b], 1);
+    }
+    __syncthreads();
+    const int per = (NBk + 255) >> 8;
+    int lr = 0, lc = 0;
+    for (int q = 0; q < per; ++q) {
+        const int b = tid * per + q;
+        if (b < NBk) {
+            lr += s_cnt[b];
+            lc += (s_cnt[b] + din.chunk_tok - 1) / din.chunk_tok;
+        }
+    }
+    int tr, tc;
+    int er = block_scan_256(lr, s_tmp, &tr);
+    int ec = block_scan_256(lc, s_tmp, &tc);
+    for (int q = 0; q < per; ++q) {
+        const int b = tid * per + q;
+        if (b < NBk) {
+            s_roff[b] = er;
+            s_coff[b] = ec;
+            er += s_cnt[b];
+            ec += (s_cnt[b] + din.chunk_tok - 1) / din.chunk_tok;
+        }
+    }
+    __syncthreads();
+    for (int r = tid; r < R; r += blockDim.x) {
+        const int b = s_b[r];
+        int rank = 0;
+        for (int r2 = 0; r2 < r; ++r2) rank += (s_b[r2] == b);
+        const int pos = s_roff[b] + rank;
+        dout.sorted_routes[pos] = r;
+        if ((rank % din.chunk_tok) == 0) {
+            int slot = 0;
+            if (b < E) {
+                slot = din.expert_slot ? din.expert_slot[b] : b;
+                if (slot < 0 || slot >= din.n_slots) {
+                    set_error(err, -3);
+                    slot = 0;
+                }
+            }
+            Chunk ch;
+            ch.slot = slot;
+            ch.route_start = pos;
+            ch.ntok = min(din.chunk_tok, s_cnt[b] - rank);
+            ch.expert = b;
+            dout.chunks[s_coff[b] + rank / din.chunk_tok] = ch;
+        }
+    }
+    if (tid == 0) *dout.n_chunks = tc;
+    __syncthreads();
+}
+
+__global__ void __launch_bounds__(256) dispatch_small_kernel(DispatchIn din, DispatchOut dout,
+                                                             int32_t *err) {
+    __shared__ int s_mem[kDispatchSmallMaxRoutes + 3 * (kDispatchSmallMaxBuckets + 1) + 16];
+    dispatch_block(din, dout, err, s_mem);
+}
+
+// Large-R dispatch, pass 1: one block per bucket counts its routes and the
+// routes of lower buckets, then ranks its own routes in route order.
+__global__ void __launch_bounds__(256) dispatch_rank_kernel(DispatchIn din, DispatchOut dout,
+                                                            int32_t *err) {
+    __shared__ int s_tmp[9];
+    const int b = blockIdx.x;
+    const int E = din.n_experts;
+    const int tid = threadIdx.x;
+    int lt = 0, eq = 0;
+    for (int r = tid; r < din.R; r += blockDim.x) {
+        int id = din.idx[r];
+        if (id < 0 || id >= E) {
+            id = E;
+            if (b == 0) set_error(err, -3);
+        }
+        lt += (id < b);
+        eq += (id == b);
+    }
+    int tot_lt, tot_eq;
+    block_scan_256(lt, s_tmp, &tot_lt);
+    block_scan_256(eq, s_tmp, &tot_eq);
+    if (tid == 0) {
+        dout.counts[b] = tot_eq;
+        dout.route_off[b] = tot_lt;
+    }
+    if (tot_eq == 0) return;
+    int base = 0;
+    for (int r0 = 0; r0 < din.R; r0 += blockDim.x) {
+        const int r = r0 + tid;
+        int id = (r < din.R) ? din.idx[r] : -2;
+        if (r < din.R && (id < 0 || id >= E)) id = E;
+        const int is = (id == b);
+        int tot;
+        const int ex = block_scan_256(is, s_tmp, &tot);
+        if (is) dout.sorted_routes[tot_lt + base + ex] = r;
+        base += tot;
+    }
+}
+
+// Large-R dispatch, pass 2: chunk table from per-bucket counts (one block).
+__global__ void __launch_bounds__(256) dispatch_chunks_kernel(DispatchIn din, DispatchOut dout,
+                                                              int32_t *err) {
+    __shared__ int s_tmp[9];
+    const int NBk = din.n_experts + 1;
+    const int tid = threadIdx.x;
+    const int per = (NBk + 255) >> 8;
+    int lc = 0;
+    for (int q = 0; q < per; ++q) {
+        const int b = tid * per + q;
+        if (b < NBk) lc += (dout.counts[b] + din.chunk_tok - 1) / din.chunk_tok;
+    }
+    int tc;
+    int ec = block_scan_256(lc, s_tmp, &tc);
+    for (int q = 0; q < per; ++q) {
+        const int b = tid * per + q;
+        if (b >= NBk) continue;
+        const int cnt = dout.counts[b];
+        int slot = 0;
+        if (b < din.n_experts && cnt > 0) {
+            slot = din.expert_slot ? din.expert_slot[b] : b;
+            if (slot < 0 || slot >= din.n_slots) {
+                set_error(err, -3);
+                slot = 0;
+            }
+        }
+        for (int c0 = 0; c0 < cnt; c0 += din.chunk_tok) {
+            Chunk ch;
+            ch.slot = slot;
+            ch.route_start = dout.route_off[b] + c0;
+            ch.ntok = min(din.chunk_tok, cnt - c0);
+            ch.expert = b;
+            dout.chunks[ec++] = ch;
+        }
+    }
+    if (tid == 0) *dout.n_chunks = tc;
+}
+
+// ============================================================ router
+__device__ __forceinline__ float score_fn(float lg, int scoring) {
+    if (scoring == 2) {  // sqrt(softplus)
+        const float sp = lg > 20.0f ? lg : log1pf(expf(lg));
+        return sqrtf(sp);
+    }
+    return 1.0f / (1.0f + expf(-lg));  // sigmoid
+}
+
+// Top-k of one token by one warp (arena.py:501-506): selection on
+// score + bias, weights from the raw scores normalised by sum + 1e-20, then
+// routed scaling.  Ties go to the lower expert id.
+__device__ void topk_token(const float *partial, int ksplit, int T, int E, int tok,
+                           const float *bias, int scoring, int top_k, int norm, float scaling,
+                           int32_t *idx_ws, float *w_ws, int32_t *idx_user, float *w_user) {
+    const int lane = threadIdx.x & 31;
+    float sc[kRouterMaxEPL], bs[kRouterMaxEPL];
+    float mx = -FLT_MAX;
+#pragma unroll
+    for (int i = 0; i < kRouterMaxEPL; ++i) {
+        const int e = lane + 32 * i;
+        float lg = -FLT_MAX;
+        if (e < E) {
+            lg = 0.0f;
+            for (int ky = 0; ky < ksplit; ++ky)
+                lg += __ldcg(partial + ((size_t)ky * T + tok) * E + e);
+            mx = fmaxf(mx, lg);
+        }
+        sc[i] = lg;
+    }
+    if (scoring == 1) {  // softmax over all experts
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(LMOE_FULL, mx, o));
+        float sum = 0.0f;
+#pragma unroll
+        for (int i = 0; i < kRouterMaxEPL; ++i) {
+            const int e = lane + 32 * i;
+            sc[i] = (e < E) ? expf(sc[i] - mx) : 0.0f;
+            sum += sc[i];
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(LMOE_FULL, sum, o);
+#pragma unroll
+        for (int i = 0; i < kRouterMaxEPL; ++i) sc[i] = sc[i] / sum;
+    } else {
+#pragma unroll
+        for (int i = 0; i < kRouterMaxEPL; ++i) {
+            const int e = lane + 32 * i;
+            if (e < E) sc[i] = score_fn(sc[i], scoring);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < kRouterMaxEPL; ++i) {
+        const int e = lane + 32 * i;
+        bs[i] = (e < E) ? sc[i] + (bias ? bias[e] : 0.0f) : -FLT_MAX;
+        if (e >= E) bs[i] = -INFINITY;
+    }
+    // lane j keeps the j-th winner; the selection loop is not unrolled so the
+    // (once per call) finisher code stays small
+    int my_e = -1;
+    float my_s = 0.0f;
+#pragma unroll 1
+    for (int j = 0; j < top_k; ++j) {
+        float bv = -INFINITY;
+        int be = 0x7fffffff;
+#pragma unroll
+        for (int i = 0; i < kRouterMaxEPL; ++i) {
+            if (bs[i] > bv) {
+                bv = bs[i];
+                be = lane + 32 * i;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(LMOE_FULL, bv, o);
+            const int oe = __shfl_xor_sync(LMOE_FULL, be, o);
+            if (ov > bv || (ov == bv && oe < be)) {
+                bv = ov;
+                be = oe;
+            }
+        }
+        float ws = 0.0f;
+#pragma unroll
+        for (int i = 0; i < kRouterMaxEPL; ++i) {
+            if (lane + 32 * i == be) {
+                ws = sc[i];
+                bs[i] = -INFINITY;
+            }
+        }
+        ws = __shfl_sync(LMOE_FULL, ws, be & 31);
+        if (lane == j) {
+            my_e = be;
+            my_s = ws;
+        }
+    }
+    float ssum = 0.0f;  // fp32, in selection order
+#pragma unroll 1
+    for (int j = 0; j < top_k; ++j) ssum += __shfl_sync(LMOE_FULL, my_s, j);
+    if (lane < top_k) {
+        float wv = norm ? my_s / (ssum + 1e-20f) : my_s;
+        wv *= scaling;
+        const size_t o = (size_t)tok * top_k + lane;
+        idx_ws[o] = my_e;
+        w_ws[o] = wv;
+        if (idx_user) idx_user[o] = my_e;
+        if (w_user) w_user[o] = wv;
+    }
+}
+
+template <typename TA>
+__device__ __forceinline__ float act_to_f(uint16_t v) {
+    return Act<TA>::to_f(v);
+}
+
+__device__ __forceinline__ float prescale(int p) { return p == 0 ? 1.0f : (p == 1 ? 0.25f : 0.0625f); }
+
+// Router logits x @ Wg^T in fp32 (products of bf16 values are exact).  Block
+// (b, z) owns experts [2b, 2b+2) over the full hidden width and tokens
+// [64z, 64z+64): each warp reduces its 256-column chunks, warps combine in
+// shared memory in a fixed order, so every logit is final when written (no
+// split-K partials).  Each block also writes its share of the gate/up
+// activation panel (16-column blocks b, b+gridDim.x, ...).  In the decode
+// regime (T <= 64) the last block to finish runs top-k and dispatch, so
+// routing costs one launch and no host synchronisation (the reference syncs
+// here every layer, arena.py:513).
+template <typename TA>
+__global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
+    constexpr int EPB = 2;
+    __shared__ float s_red[8][EPB][8];
+    __shared__ int s_last;
+    __shared__ int s_disp[kDispatchSmallMaxRoutes + 3 * (kDispatchSmallMaxBuckets + 1) + 16];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int e0 = blockIdx.x * EPB;
+    const int tbeg = blockIdx.y * 64;
+    const int tend = min(a.T, tbeg + 64);
+    const int nchunk = a.H / kRouterKS;
+
+    // ---- gate/up activation panel + 16-column sums for this block's share.
+    // Panel positions of group G are G*gs + (position within the group), so a
+    // per-block table of one group's positions replaces the index arithmetic.
+    if (a.xpanel) {
+        __shared__ short s_pos[128];
+        __shared__ float s_scale[128];
+        if (tid < a.pgs) {
+            int p;
+            s_pos[tid] = static_cast<short>(panel_pos(tid, a.pbits, a.pgs, &p));
+            s_scale[tid] = prescale(p);
+        }
+        __syncthreads();
+        const int nblk = a.H / 16;
+        const int ntk = tend - tbeg;
+        const int nmy = max(0, (nblk - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x);
+        // item = (token, my block, half): lanes 2i / 2i+1 hold the two halves of a block
+        const int total = ntk * nmy * 2;
+        for (int base = tid - lane; base < total; base += blockDim.x) {
+            const int item = base + lane;
+            const bool ok = item < total;  // pairs (2i, 2i+1) are valid together
+            const int half = item & 1, nb = item >> 1;
+            const int n = ok ? nb / nmy : 0, j = ok ? nb - n * nmy : 0;
+            const int col0 = (blockIdx.x + j * gridDim.x) * 16 + half * 8;
+            const int t = tbeg + n;
+            float s = 0.0f, sp = 0.0f;
+            if (ok) {
+                const uint4 v = *reinterpret_cast<const uint4 *>(a.x + (size_t)t * a.H + col0);
+                const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+                const int G = col0 / a.pgs, i0 = col0 - G * a.pgs;
+                uint16_t *dst = a.xpanel + (size_t)t * a.H + G * a.pgs;
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    const float f =
+                        act_to_f<TA>(static_cast<uint16_t>(q & 1 ? u[q >> 1] >> 16 : u[q >> 1] & 0xffffu));
+                    const uint16_t pv = Act<TA>::from_f(f * s_scale[i0 + q]);
+                    s += f;
+                    sp += Act<TA>::to_f(pv);
+                    dst[s_pos[i0 + q]] = pv;
+                }
+            }
+            const float other = __shfl_xor_sync(LMOE_FULL, s, 1);
+            const float other_p = __shfl_xor_sync(LMOE_FULL, sp, 1);
+            if (ok && half == 0)
+                *reinterpret_cast<float2 *>(a.xsum16 + ((size_t)t * (a.H / 16) + (col0 >> 4)) * 2) =
+                    make_float2(s + other, sp + other_p);
+        }
+    }
+
+    // ---- logits
+    for (int ts = tbeg; ts < tend; ts += 8) {
+        const int nt = min(8, tend - ts);
+        float acc[EPB][8];
+#pragma unroll
+        for (int i = 0; i < EPB; ++i)
+#pragma unroll
+            for (int n = 0; n < 8; ++n) acc[i][n] = 0.0f;
+#pragma unroll 2
+        for (int ch = warp; ch < nchunk; ch += 8) {
+            const int col = ch * kRouterKS + lane * 8;
+            uint4 wv[EPB];
+#pragma unroll
+            for (int i = 0; i < EPB; ++i) {
+                wv[i] = make_uint4(0, 0, 0, 0);
+                if (e0 + i < a.E) wv[i] = __ldg(reinterpret_cast<const uint4 *>(a.wg + (size_t)(e0 + i) * a.H + col));
+            }
+            uint4 xv[8];
+#pragma unroll
+            for (int n = 0; n < 8; ++n) {
+                xv[n] = make_uint4(0, 0, 0, 0);
+                if (n < nt) xv[n] = __ldg(reinterpret_cast<const uint4 *>(a.x + (size_t)(ts + n) * a.H + col));
+            }
+#pragma unroll
+            for (int n = 0; n < 8; ++n) {
+                if (n >= nt) continue;
+                const uint32_t xu[4] = {xv[n].x, xv[n].y, xv[n].z, xv[n].w};
+                float xf[8];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    xf[2 * q] = act_to_f<TA>(static_cast<uint16_t>(xu[q] & 0xffffu));
+                    xf[2 * q + 1] = act_to_f<TA>(static_cast<uint16_t>(xu[q] >> 16));
+                }
+#pragma unroll
+                for (int i = 0; i < EPB; ++i) {
+                    const uint32_t wu[4] = {wv[i].x, wv[i].y, wv[i].z, wv[i].w};
+                    float s = acc[i][n];
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        s = fmaf(__uint_as_float(wu[q] << 16), xf[2 * q], s);  // router weight is bf16
+                        s = fmaf(__uint_as_float(wu[q] & 0xffff0000u), xf[2 * q + 1], s);
+                    }
+                    acc[i][n] = s;
+                }
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < EPB; ++i)
+#pragma unroll
+            for (int n = 0; n < 8; ++n) {
+                if (n >= nt) continue;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) acc[i][n] += __shfl_xor_sync(LMOE_FULL, acc[i][n], o);
+            }
+        if (lane < EPB * 8) {
+            float v = 0.0f;
+#pragma unroll
+            for (int i = 0; i < EPB; ++i)
+#pragma unroll
+                for (int n = 0; n < 8; ++n)
+                    if (lane == i * 8 + n) v = acc[i][n];
+            s_red[warp][lane >> 3][lane & 7] = v;
+        }
+        __syncthreads();
+        if (tid < EPB * 8) {
+            const int i = tid >> 3, n = tid & 7;
+            float v = 0.0f;
+            for (int w = 0; w < 8; ++w) v += s_red[w][i][n];
+            if (e0 + i < a.E && n < nt) a.partial[(size_t)(ts + n) * a.E + e0 + i] = v;
+        }
+        __syncthreads();
+    }
+    if (!a.finish) return;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        const unsigned total = gridDim.x * gridDim.y * gridDim.z;
+        const unsigned prev = atomicAdd(a.counter, 1u);
+        s_last = (prev == total - 1);
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    if (tid == 0) *a.counter = 0u;
+    for (int tok = warp; tok < a.T; tok += 8)
+        topk_token(a.partial, 1, a.T, a.E, tok, a.bias, a.scoring, a.top_k, a.norm_topk, a.scaling, a.idx_ws,
+                   a.w_ws, a.idx_user, a.w_user);
+    if (!a.do_dispatch) return;
+    __threadfence();
+    __syncthreads();
+    dispatch_block(a.din, a.dout, a.err, s_disp);
+}
+
+__global__ void __launch_bounds__(256) topk_kernel(TopkArgs a) {
+    const int warp = threadIdx.x >> 5;
+    const int tok = blockIdx.x * 8 + warp;
+    if (tok >= a.T) return;
+    topk_token(a.partial, a.ksplit, a.T, a.E, tok, a.bias, a.scoring, a.top_k, a.norm_topk,
+               a.scaling, a.idx_ws, a.w_ws, a.idx_user, a.w_user);
+}
+
+// ============================================================ activation panel
+// Natural [rows, K] activations -> consumer panel layout + 16-column sums
+// (sums in column order, as the router's panel producer computes them).
+template <typename TA>
+__global__ void __launch_bounds__(256) panel_kernel(PanelArgs a) {
+    const int row = blockIdx.x;
+    const int col = blockIdx.y * 256 + threadIdx.x;
+    const uint16_t *src = a.x + (size_t)row * a.K;
+    if (col < a.K) {
+        int p;
+        const int pos = panel_pos(col, a.bits, a.gs, &p);
+        a.panel[(size_t)row * a.K + pos] = Act<TA>::from_f(Act<TA>::to_f(src[col]) * prescale(p));
+    }
+    if (threadIdx.x < 16) {
+        const int c0 = blockIdx.y * 256 + threadIdx.x * 16;
+        if (c0 < a.K) {
+            // two serial 8-column halves, then lo + hi (the router's order);
+            // the second sum is over the stored (prescaled) panel values
+            float lo = 0.0f, hi = 0.0f, plo = 0.0f, phi = 0.0f;
+            for (int q = 0; q < 16; ++q) {
+                int p;
+                panel_pos(c0 + q, a.bits, a.gs, &p);
+                const float f = Act<TA>::to_f(src[c0 + q]);
+                const float fp = Act<TA>::to_f(Act<TA>::from_f(f * prescale(p)));
+                if (q < 8) {
+                    lo += f;
+                    plo += fp;
+                } else {
+                    hi += f;
+                    phi += fp;
+                }
+            }
+            *reinterpret_cast<float2 *>(a.sum16 + ((size_t)row * (a.K / 16) + c0 / 16) * 2) =
+                make_float2(lo + hi, plo + phi);
+        }
+    }
+}
+
+// ============================================================ launchers
+cudaError_t launch_router(const RouterArgs &a, int /*ksplit*/, cudaStream_t st) {
+    dim3 grid((a.E + 1) / 2, (a.T + 63) / 64, 1);
+    if (a.act_f16)
+        router_kernel<__half><<<grid, 256, 0, st>>>(a);
+    else
+        router_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_topk(const TopkArgs &a, cudaStream_t st) {
+    topk_kernel<<<(a.T + 7) / 8, 256, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_dispatch_small(const DispatchIn &din, const DispatchOut &dout, int32_t *err,
+                                  cudaStream_t st) {
+    dispatch_small_kernel<<<1, 256, 0, st>>>(din, dout, err);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_dispatch_large(const DispatchIn &din, const DispatchOut &dout, int32_t *err,
+                                  cudaStream_t st) {
+    dispatch_rank_kernel<<<din.n_experts + 1, 256, 0, st>>>(din, dout, err);
+    dispatch_chunks_kernel<<<1, 256, 0, st>>>(din, dout, err);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_panel(const PanelArgs &a, cudaStream_t st) {
+    dim3 grid(a.rows, (a.K + 255) / 256);
+    if (a.act_f16)
+        panel_kernel<__half><<<grid, 256, 0, st>>>(a);
+    else
+        panel_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+}  // namespace lmoe

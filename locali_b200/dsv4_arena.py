@@ -216,6 +216,10 @@ class V4ArenaMoE(ArenaMoE):
             placed, reads = self.store.submit(self.layer, experts)
         else:
             placed, reads = self.store.slots_for(self.layer, experts), None
+        missing = sorted(set(experts) - set(placed))
+        if missing:
+            raise RuntimeError(f"arena could not place demanded experts {missing} of layer {self.layer}: every "
+                               "usable slot is pinned; raise the ceiling")
         for blk, k in ((self.nxt, self.prefetch_k), (self.nxt2, self.prefetch_k2)):
             if blk is None:
                 continue

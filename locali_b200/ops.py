@@ -55,6 +55,13 @@ class QProjArrays:
     biases: torch.Tensor
     bits: int
     group_size: int
+    # optional pre-tiled copy (uint8 [n_slots, tile_bytes]); the expert GEMVs
+    # stream it with one bulk copy per 16-row tile instead of the arrays above
+    tiles: torch.Tensor | None = None
+
+    @property
+    def n_slots(self) -> int:
+        return int(self.weight.shape[0])
 
     @property
     def rows(self) -> int:
@@ -79,7 +86,31 @@ class QProjArrays:
             if not t.is_contiguous():
                 raise ValueError("arena arrays must be contiguous")
         return _lib.QProj(self.weight.data_ptr(), self.scales.data_ptr(), self.biases.data_ptr(),
-                          int(self.bits), int(self.group_size))
+                          int(self.bits), int(self.group_size), _ptr(self.tiles))
+
+    def tile_bytes(self) -> int:
+        """Bytes per slot of the pre-tiled copy (0: geometry has no tile layout)."""
+        return int(lmoe().lmoe_tile_bytes(self.rows, self.cols, int(self.bits), int(self.group_size)))
+
+    def pack_tiles(self, slot_begin: int = 0, slot_count: int | None = None) -> "QProjArrays":
+        """(Re)pack slots [slot_begin, slot_begin + slot_count) into ``tiles``.
+
+        Allocates ``tiles`` on first use.  Enqueued on the current stream;
+        call again for slots whose row-major arrays were rewritten.
+        """
+        _need_cuda(self.weight, self.scales, self.biases)
+        nb = self.tile_bytes()
+        if nb == 0:
+            raise ValueError(f"no tile layout for [{self.rows}, {self.cols}] bits={self.bits} gs={self.group_size}")
+        if self.tiles is None:
+            self.tiles = torch.empty((self.n_slots, nb), dtype=torch.uint8, device=self.weight.device)
+        if slot_count is None:
+            slot_count = self.n_slots - slot_begin
+        q = _lib.QProj(self.weight.data_ptr(), self.scales.data_ptr(), self.biases.data_ptr(),
+                       int(self.bits), int(self.group_size), None)
+        check(lmoe().lmoe_tile_pack(ctypes.byref(q), self.n_slots, self.rows, self.cols, int(slot_begin),
+                                    int(slot_count), self.tiles.data_ptr(), _stream()), "lmoe_tile_pack")
+        return self
 
 
 @dataclass
@@ -103,6 +134,12 @@ class ExpertArrays:
     @property
     def dtype(self) -> torch.dtype:
         return self.gate.scales.dtype
+
+    def pack_tiles(self, slot_begin: int = 0, slot_count: int | None = None) -> "ExpertArrays":
+        """Pre-tile all three projections (see :meth:`QProjArrays.pack_tiles`)."""
+        for q in (self.gate, self.up, self.down):
+            q.pack_tiles(slot_begin, slot_count)
+        return self
 
     def ctype(self) -> _lib.Experts:
         if self.dtype not in _ACT:

@@ -67,9 +67,25 @@ def test_workspace_size_and_validation(built):
 
 def test_strerror_and_version(built):
     lib = _lib.lmoe()
-    assert lib.lmoe_version() == 1
+    assert lib.lmoe_version() == 2
     assert lib.lmoe_strerror(_lib.LMOE_EINDEX).decode().startswith("expert id")
     assert lib.lmoe_workspace_size_routes(8, 512, 256, 5) > 0
+
+
+def test_tile_geometry(built):
+    """Pre-tiled format: 16-row tiles of codes + scales + biases, 128-byte padded."""
+    lib = _lib.lmoe()
+    # 2-bit g64, K=4096: codes 16*1024, scales and biases 16*128 each
+    assert lib.lmoe_tile_bytes(2048, 4096, 2, 64) == 128 * (16 * 1024 + 2 * 16 * 128)
+    # 4-bit g32, K=2048: codes 16*1024, scale rows of 128 bytes
+    assert lib.lmoe_tile_bytes(4096, 2048, 4, 32) == 256 * (16 * 1024 + 2 * 16 * 128)
+    # small K: 16*32 codes + 2*16*2 scale bytes -> padded to 640
+    assert lib.lmoe_tile_bytes(16, 128, 2, 128) == 640
+    assert lib.lmoe_tile_bytes(2048, 4096, 3, 64) == 0     # bits not compiled
+    assert lib.lmoe_tile_bytes(2040, 4096, 2, 64) == 0     # rows not a multiple of 16
+    assert lib.lmoe_tile_bytes(2048, 3072, 2, 64) == 0     # rows of 768 B: not a power-of-two chunk count
+    q = _lib.QProj(None, None, None, 2, 64, None)
+    assert lib.lmoe_tile_pack(ctypes.byref(q), 1, 16, 256, 0, 1, None, None) == _lib.LMOE_EINVAL
 
 
 def test_product_path_fails_loudly_without_cuda(built):

@@ -57,12 +57,11 @@ def test_v4_module_streams_from_pack_with_small_arena(built, tmp_path, native):
     layers = [synth.make_layer(cfg, seed=s, device="cpu") for s in range(3)]
     idx_path = write_pack(tmp_path / "pack", [l.experts for l in layers], top_k=cfg.top_k)
     per = cfg.expert_bytes() / 1e9
-    # plain LRU: an SLRU probation segment of two slots could not hold the
-    # four experts one layer call needs at once (in the reference planner too)
-    store = V4ArenaStore(idx_path, native_scheduler=native, ceiling_gb=per * 5.5, threads=2, device="cuda",
+    # 8 usable slots: one layer pins up to 4 while the next claims 4 more
+    store = V4ArenaStore(idx_path, native_scheduler=native, ceiling_gb=per * 9.5, threads=2, device="cuda",
                          cache_policy="lru")
     try:
-        assert store.slots["cold"] == 5
+        assert store.slots["cold"] == 9
         x = synth.make_tokens(cfg, 2, seed=9, device="cuda")
         for step in range(4):
             li = step % 3
@@ -75,8 +74,29 @@ def test_v4_module_streams_from_pack_with_small_arena(built, tmp_path, native):
             ref = O.moe_layer(t2np(x), L, idx=t2np(idx).astype(np.int64), w=t2np(w))
             assert O.rel_l2(t2np(out), ref["out"]) < 4e-3
         st = store.stats()
-        assert st["misses"] > 0 and st["bytes_read"] > 0
+        assert st["misses"] > 0 and st["bytes_read"] > 0 and st["evictions"] > 0
         assert st["scheduler"] == ("c" if native else "python")
+    finally:
+        store.close()
+
+
+def test_v4_module_raises_when_arena_cannot_hold_a_layer(built, tmp_path):
+    cfg = synth.config("c0", n_experts=8, top_k=2)
+    layers = [synth.make_layer(cfg, seed=s, device="cpu") for s in range(2)]
+    idx_path = write_pack(tmp_path / "pack", [l.experts for l in layers], top_k=cfg.top_k)
+    per = cfg.expert_bytes() / 1e9
+    store = V4ArenaStore(idx_path, native_scheduler=False, ceiling_gb=per * 5.5, threads=1, device="cuda")
+    try:
+        x = synth.make_tokens(cfg, 2, seed=9, device="cuda")
+        for li in range(2):
+            idx = torch.tensor([[0, 1], [2, 3]], dtype=torch.int32, device="cuda") + 4 * li
+            w = torch.full((2, 2), 0.5, device="cuda")
+            moe = V4ArenaMoE(store, li, FixedGate(idx, w), cfg.top_k)
+            if li == 0:
+                moe(x)
+            else:  # layer 0 still pins all four usable slots
+                with pytest.raises(RuntimeError, match="pinned"):
+                    moe(x)
     finally:
         store.close()
 

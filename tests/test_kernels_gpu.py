@@ -54,6 +54,43 @@ def test_gather_qmm_matches_oracle(built, bits, gs):
     assert np.all(got[7] == 0)  # slot 0 is the zero slot
 
 
+@pytest.mark.parametrize("bits,gs", COMBOS)
+@pytest.mark.parametrize("cols", [1024, 4096])
+def test_gather_qmm_single_token_chunks(built, bits, gs, cols):
+    """Every slot routed once: all units take the single-token (group-column)
+    path; the pre-tiled copy must give bit-identical results."""
+    rows, n_slots = 48, 7
+    proj = _proj(rows, cols, bits, gs, n_slots, seed=bits * 7 + gs + cols)
+    x = torch.randn((n_slots - 1, cols), generator=torch.Generator().manual_seed(9)).bfloat16()
+    slots = torch.arange(1, n_slots, dtype=torch.int32)
+    y = ops.gather_qmm(x.cuda(), slots.cuda(), proj)
+    proj.pack_tiles()
+    y_t = ops.gather_qmm(x.cuda(), slots.cuda(), proj)
+    torch.cuda.synchronize()
+    ref = O.gather_qmm(t2np(x), qproj_np(proj), slots.numpy())
+    got = t2np(y)
+    assert O.rel_l2(got, ref) < PROJ_TOL
+    assert _ulp_mismatch(got, ref) < 0.05
+    assert torch.equal(y, y_t)
+
+
+@pytest.mark.parametrize("bits,gs", COMBOS)
+def test_gather_qmm_tiled_identical(built, bits, gs):
+    rows, cols, n_slots, R = 64, 512, 5, 11
+    proj = _proj(rows, cols, bits, gs, n_slots, seed=bits * 1000 + gs)
+    x = torch.randn((R, cols), generator=torch.Generator().manual_seed(3)).bfloat16().cuda()
+    slots = torch.tensor([1, 2, 3, 4, 1, 1, 2, 0, 3, 4, 4], dtype=torch.int32).cuda()
+    y = ops.gather_qmm(x, slots, proj)
+    proj.pack_tiles()
+    y_t = ops.gather_qmm(x, slots, proj)
+    # repacking a subset of slots leaves the others intact
+    proj.pack_tiles(2, 2)
+    y_t2 = ops.gather_qmm(x, slots, proj)
+    torch.cuda.synchronize()
+    assert torch.equal(y, y_t)
+    assert torch.equal(y, y_t2)
+
+
 @pytest.mark.parametrize("bits,gs", [(2, 64), (2, 128), (4, 64), (8, 128)])
 @pytest.mark.parametrize("mode", ["fused", "stock"])
 def test_gateup_swiglu_matches_oracle(built, bits, gs, mode):
@@ -101,6 +138,21 @@ def _check_layer(cfg, T, seed=0, device="cuda", acc=np.float64):
     err = O.rel_l2(got, ref["out"])
     assert err < LAYER_TOL, err
     return err, got, ref
+
+
+@pytest.mark.parametrize("name,T", [("c1", 1), ("c1", 5), ("c2", 16)])
+def test_layer_tiled_identical(built, name, T):
+    cfg = synth.config(name)
+    layer = synth.make_layer(cfg, seed=1, device="cuda")
+    x = synth.make_tokens(cfg, T, seed=2, device="cuda")
+    kern = ops.MoEKernel(layer.router, layer.experts, layer.expert_slot, cfg.swiglu_limit, "fused")
+    out = kern(x).clone()
+    layer.experts.pack_tiles()
+    kern_t = ops.MoEKernel(layer.router, layer.experts, layer.expert_slot, cfg.swiglu_limit, "fused")
+    out_t = kern_t(x)
+    torch.cuda.synchronize()
+    kern_t.ws.check()
+    assert torch.equal(out, out_t)
 
 
 def test_layer_c0_matches_oracle(built):
