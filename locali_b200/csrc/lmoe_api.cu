@@ -46,7 +46,8 @@ Layout make_layout(int T, int R, int K, int I, int H_out, int buckets, int E_rou
         return o;
     };
     L.status = take(256);
-    L.partial = take((size_t)ksplit * T * E_router * 4);
+    // logits, then (score, biased score) per (token, expert)
+    L.partial = take((size_t)ksplit * T * E_router * 4 + 8 + (size_t)T * E_router * 8);
     L.idx = take((size_t)R * 4);
     L.w = take((size_t)R * 4);
     L.sorted = take((size_t)R * 4);
@@ -308,6 +309,10 @@ static int route_impl(const lmoe_router &r, int H, int dtype, const lmoe_layer *
     a.norm_topk = r.norm_topk;
     a.scaling = r.routed_scaling;
     a.partial = at<float>(ws, L.partial);
+    // element-wise scorings are finished by the logit blocks themselves
+    a.scores = r.scoring == LMOE_SCORE_SOFTMAX
+                   ? nullptr
+                   : reinterpret_cast<float2 *>(a.partial + (((size_t)ksplit * T * r.n_experts + 1) & ~size_t(1)));
     if (l) {
         a.xpanel = at<uint16_t>(ws, L.xpanel);
         a.xsum16 = at<float>(ws, L.xsum);
@@ -341,6 +346,7 @@ static int route_impl(const lmoe_router &r, int H, int dtype, const lmoe_layer *
     if (!small_topk) {
         TopkArgs tk;
         tk.partial = a.partial;
+        tk.scores = a.scores;
         tk.ksplit = 1;
         tk.T = T;
         tk.E = a.E;

@@ -309,12 +309,13 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
     asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
     return t;
 }
-// Wait on an mbarrier phase, bounded by wall time (kWaitLimitNs).  Returns
-// false if the wait gave up; the caller records an error and stops instead of
-// hanging the GPU.  Between polls the warp sleeps (32 ns doubling to 256 ns):
-// a warp polling flat out takes issue slots from the warps of its
-// sub-partition that do the math.
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+// Wait on an mbarrier phase, bounded (kWaitLimitCycles of the SM clock,
+// about 2 s).  Returns false if the wait gave up; the caller records an error
+// and stops instead of hanging the GPU.  Between polls the warp sleeps (32 ns
+// doubling to 256 ns): a warp polling flat out takes issue slots from the
+// warps of its sub-partition that do the math.  The bound is kept on clock64,
+// which is cheap to read, rather than on the global timer.
+constexpr long long kWaitLimitCycles = 4000000000ll;
 __device__ __forceinline__ bool mbar_try(uint64_t *bar, uint32_t parity) {
     uint32_t done;
     asm volatile(
@@ -327,13 +328,13 @@ __device__ __forceinline__ bool mbar_try(uint64_t *bar, uint32_t parity) {
 }
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
     if (mbar_try(bar, parity)) return true;
-    const uint64_t t0 = globaltimer_ns();
+    const long long t0 = clock64();
     uint32_t ns = 32;
     for (;;) {
         __nanosleep(ns);
         if (mbar_try(bar, parity)) return true;
         if (ns < 256) ns <<= 1;
-        if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+        if (clock64() - t0 > kWaitLimitCycles) return false;
     }
 }
 
@@ -368,6 +369,16 @@ __device__ __forceinline__ void cp_async_arrive_noinc(uint64_t *bar) {
 __device__ __forceinline__ void fence_proxy_async() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
+
+// Programmatic dependent launch.  The routing and expert kernels are launched
+// with programmatic stream serialisation: a kernel may start while its
+// predecessor in the stream is still running.  pdl_wait() blocks until the
+// predecessor has completed and its memory is visible; every kernel calls it
+// before touching data another kernel produces or consumes (constant inputs
+// such as weights may be read earlier).  pdl_trigger() lets the successor
+// launch.  Without the launch attribute both are no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 __device__ __forceinline__ void set_error(int32_t *err, int code) {
     if (err) atomicCAS(err, 0, code);

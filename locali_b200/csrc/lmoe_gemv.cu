@@ -118,8 +118,6 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) gemv_kernel(const GemvArgs
     const int rows = a.q0.rows;
     const int RT = rows >> 4;
     const int GT = K / GS;
-    const int nch = *a.n_chunks;
-    const int units = nch * RT;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < c.nst; ++s) {
@@ -147,6 +145,11 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) gemv_kernel(const GemvArgs
         }
     }
     __syncthreads();
+    // the chunk table and activations come from the preceding kernels
+    pdl_wait();
+    pdl_trigger();
+    const int nch = *a.n_chunks;
+    const int units = nch * RT;
 
     if (warp == c.ncw || warp == c.ncw + 1) {
         // ===================================================== producers
@@ -915,8 +918,7 @@ static cudaError_t launch_gemv_t(const GemvArgs &a, int max_chunks, cudaStream_t
     long grid = num_sms();
     if (grid > units_max) grid = units_max;
     if (grid < 1) grid = 1;
-    kern<<<static_cast<unsigned>(grid), (c.ncw + 2 + kGemvEpi) * 32, c.smem, st>>>(a, c);
-    return cudaGetLastError();
+    return launch_pdl(kern, dim3(static_cast<unsigned>(grid)), dim3((c.ncw + 2 + kGemvEpi) * 32), c.smem, st, a, c);
 }
 
 template <typename TA, int MODE>

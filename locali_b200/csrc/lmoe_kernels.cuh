@@ -88,7 +88,8 @@ struct RouterArgs {
     const float *bias;   // [E] or nullptr
     int32_t E, top_k, scoring, norm_topk;
     float scaling;
-    float *partial;  // [ksplit][T][E]
+    float *partial;  // [ksplit][T][E] logits
+    float2 *scores;  // [T][E] (score, score + bias) for the element-wise scorings, or nullptr
     // panel producer for the gate/up consumer (optional)
     uint16_t *xpanel;
     float *xsum16;  // [T, H/16, 2]: per 16 columns, sum of x and sum of the stored panel values
@@ -109,6 +110,7 @@ struct RouterArgs {
 
 struct TopkArgs {
     const float *partial;
+    const float2 *scores;  // precomputed (score, biased score) or nullptr
     int32_t ksplit, T, E, top_k, scoring, norm_topk;
     float scaling;
     const float *bias;
@@ -179,6 +181,23 @@ constexpr int kHdrWeight = 12;
 constexpr int kHdrPanel = 20;
 constexpr int kHdrPanelN = 28;
 bool gemv_config(int mode, int bits, int gs, int K, int ntok_max, GemvCfg *out);
+
+// Launch with programmatic stream serialisation (see pdl_wait).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
 
 // host-side launchers (lmoe_route.cu, lmoe_gemv.cu)
 cudaError_t launch_router(const RouterArgs &a, int ksplit, cudaStream_t st);

@@ -116,9 +116,66 @@ __device__ void dispatch_block(const DispatchIn &din, const DispatchOut &dout, i
     __syncthreads();
 }
 
+// Dispatch of at most 32 routes by one warp: same output as dispatch_block
+// (routes grouped by expert in expert order, stable in route order; chunks
+// of at most chunk_tok routes in expert order) without block barriers.
+__device__ void dispatch_warp(const DispatchIn &din, const DispatchOut &dout, int32_t *err,
+                              const int *s_idx = nullptr, const int *s_slot = nullptr) {
+    const int lane = threadIdx.x & 31;
+    const int R = din.R, E = din.n_experts, ct = din.chunk_tok;
+    int b = 0x7fffffff;  // lanes without a route sort after every bucket
+    if (lane < R) {
+        const int id = s_idx ? s_idx[lane] : din.idx[lane];
+        b = id;
+        if (id < 0 || id >= E) {
+            b = E;
+            set_error(err, -3);
+        }
+    }
+    const unsigned same = __match_any_sync(LMOE_FULL, b);
+    const int rank = __popc(same & ((1u << lane) - 1u));
+    const int cnt = __popc(same);
+    const int nch = rank == 0 ? (cnt + ct - 1) / ct : 0;  // bucket leaders carry the chunk count
+    int before_r = 0, before_c = 0, total_c = 0;
+    for (int j = 0; j < R; ++j) {
+        const int bj = __shfl_sync(LMOE_FULL, b, j);
+        const int cj = __shfl_sync(LMOE_FULL, nch, j);
+        before_r += (bj < b);
+        before_c += (bj < b) ? cj : 0;
+        total_c += cj;
+    }
+    if (lane < R) {
+        const int pos = before_r + rank;
+        dout.sorted_routes[pos] = lane;
+        if (rank % ct == 0) {
+            int slot = 0;
+            if (b < E) {
+                slot = s_slot ? s_slot[b] : (din.expert_slot ? din.expert_slot[b] : b);
+                if (slot < 0 || slot >= din.n_slots) {
+                    set_error(err, -3);
+                    slot = 0;
+                }
+            }
+            Chunk ch;
+            ch.slot = slot;
+            ch.route_start = pos;
+            ch.ntok = min(ct, cnt - rank);
+            ch.expert = b;
+            dout.chunks[before_c + rank / ct] = ch;
+        }
+    }
+    if (lane == 0) *dout.n_chunks = total_c;
+}
+
 __global__ void __launch_bounds__(256) dispatch_small_kernel(DispatchIn din, DispatchOut dout,
                                                              int32_t *err) {
     __shared__ int s_mem[kDispatchSmallMaxRoutes + 3 * (kDispatchSmallMaxBuckets + 1) + 16];
+    pdl_wait();
+    pdl_trigger();
+    if (din.R <= 32) {
+        if (threadIdx.x < 32) dispatch_warp(din, dout, err);
+        return;
+    }
     dispatch_block(din, dout, err, s_mem);
 }
 
@@ -127,6 +184,8 @@ __global__ void __launch_bounds__(256) dispatch_small_kernel(DispatchIn din, Dis
 __global__ void __launch_bounds__(256) dispatch_rank_kernel(DispatchIn din, DispatchOut dout,
                                                             int32_t *err) {
     __shared__ int s_tmp[9];
+    pdl_wait();
+    pdl_trigger();
     const int b = blockIdx.x;
     const int E = din.n_experts;
     const int tid = threadIdx.x;
@@ -165,6 +224,8 @@ __global__ void __launch_bounds__(256) dispatch_rank_kernel(DispatchIn din, Disp
 __global__ void __launch_bounds__(256) dispatch_chunks_kernel(DispatchIn din, DispatchOut dout,
                                                               int32_t *err) {
     __shared__ int s_tmp[9];
+    pdl_wait();
+    pdl_trigger();
     const int NBk = din.n_experts + 1;
     const int tid = threadIdx.x;
     const int per = (NBk + 255) >> 8;
@@ -210,67 +271,85 @@ __device__ __forceinline__ float score_fn(float lg, int scoring) {
 
 // Top-k of one token by one warp (arena.py:501-506): selection on
 // score + bias, weights from the raw scores normalised by sum + 1e-20, then
-// routed scaling.  Ties go to the lower expert id.
-__device__ void topk_token(const float *partial, int ksplit, int T, int E, int tok,
+// routed scaling.  Ties go to the lower expert id.  `scores`, when given,
+// holds (score, score + bias) already (element-wise scorings, computed by
+// the logit blocks); otherwise the logits are scored here.
+__device__ void topk_token(const float *partial, const float2 *scores, int ksplit, int T, int E, int tok,
                            const float *bias, int scoring, int top_k, int norm, float scaling,
-                           int32_t *idx_ws, float *w_ws, int32_t *idx_user, float *w_user) {
+                           int32_t *idx_ws, float *w_ws, int32_t *idx_user, float *w_user,
+                           int *s_idx = nullptr) {
     const int lane = threadIdx.x & 31;
     float sc[kRouterMaxEPL], bs[kRouterMaxEPL];
-    float mx = -FLT_MAX;
-#pragma unroll
-    for (int i = 0; i < kRouterMaxEPL; ++i) {
-        const int e = lane + 32 * i;
-        float lg = -FLT_MAX;
-        if (e < E) {
-            lg = 0.0f;
-            for (int ky = 0; ky < ksplit; ++ky)
-                lg += __ldcg(partial + ((size_t)ky * T + tok) * E + e);
-            mx = fmaxf(mx, lg);
-        }
-        sc[i] = lg;
-    }
-    if (scoring == 1) {  // softmax over all experts
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(LMOE_FULL, mx, o));
-        float sum = 0.0f;
+    if (scores) {
 #pragma unroll
         for (int i = 0; i < kRouterMaxEPL; ++i) {
             const int e = lane + 32 * i;
-            sc[i] = (e < E) ? expf(sc[i] - mx) : 0.0f;
-            sum += sc[i];
+            sc[i] = 0.0f;
+            bs[i] = -INFINITY;
+            if (e < E) {
+                const float2 v = __ldcg(scores + (size_t)tok * E + e);
+                sc[i] = v.x;
+                bs[i] = v.y;
+            }
         }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(LMOE_FULL, sum, o);
-#pragma unroll
-        for (int i = 0; i < kRouterMaxEPL; ++i) sc[i] = sc[i] / sum;
     } else {
+        float mx = -FLT_MAX;
 #pragma unroll
         for (int i = 0; i < kRouterMaxEPL; ++i) {
             const int e = lane + 32 * i;
-            if (e < E) sc[i] = score_fn(sc[i], scoring);
+            float lg = -FLT_MAX;
+            if (e < E) {
+                lg = 0.0f;
+                for (int ky = 0; ky < ksplit; ++ky) lg += __ldcg(partial + ((size_t)ky * T + tok) * E + e);
+                mx = fmaxf(mx, lg);
+            }
+            sc[i] = lg;
+        }
+        if (scoring == 1) {  // softmax over all experts
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(LMOE_FULL, mx, o));
+            float sum = 0.0f;
+#pragma unroll
+            for (int i = 0; i < kRouterMaxEPL; ++i) {
+                const int e = lane + 32 * i;
+                sc[i] = (e < E) ? expf(sc[i] - mx) : 0.0f;
+                sum += sc[i];
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(LMOE_FULL, sum, o);
+#pragma unroll
+            for (int i = 0; i < kRouterMaxEPL; ++i) sc[i] = sc[i] / sum;
+        } else {
+#pragma unroll
+            for (int i = 0; i < kRouterMaxEPL; ++i) {
+                const int e = lane + 32 * i;
+                if (e < E) sc[i] = score_fn(sc[i], scoring);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < kRouterMaxEPL; ++i) {
+            const int e = lane + 32 * i;
+            bs[i] = (e < E) ? sc[i] + (bias ? bias[e] : 0.0f) : -INFINITY;
         }
     }
+    // Each lane keeps its own best candidate; a round takes the warp-wide
+    // best and only the winning lane rescans its candidates.  Lane j keeps
+    // the j-th winner.
+    float lbv = -INFINITY, lbs = 0.0f;
+    int lbe = 0x7fffffff;
 #pragma unroll
-    for (int i = 0; i < kRouterMaxEPL; ++i) {
-        const int e = lane + 32 * i;
-        bs[i] = (e < E) ? sc[i] + (bias ? bias[e] : 0.0f) : -FLT_MAX;
-        if (e >= E) bs[i] = -INFINITY;
-    }
-    // lane j keeps the j-th winner; the selection loop is not unrolled so the
-    // (once per call) finisher code stays small
+    for (int i = 0; i < kRouterMaxEPL; ++i)
+        if (bs[i] > lbv) {
+            lbv = bs[i];
+            lbe = lane + 32 * i;
+            lbs = sc[i];
+        }
     int my_e = -1;
     float my_s = 0.0f;
 #pragma unroll 1
     for (int j = 0; j < top_k; ++j) {
-        float bv = -INFINITY;
-        int be = 0x7fffffff;
-#pragma unroll
-        for (int i = 0; i < kRouterMaxEPL; ++i) {
-            if (bs[i] > bv) {
-                bv = bs[i];
-                be = lane + 32 * i;
-            }
-        }
+        float bv = lbv;
+        int be = lbe;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
             const float ov = __shfl_xor_sync(LMOE_FULL, bv, o);
@@ -280,18 +359,23 @@ __device__ void topk_token(const float *partial, int ksplit, int T, int E, int t
                 be = oe;
             }
         }
-        float ws = 0.0f;
-#pragma unroll
-        for (int i = 0; i < kRouterMaxEPL; ++i) {
-            if (lane + 32 * i == be) {
-                ws = sc[i];
-                bs[i] = -INFINITY;
-            }
-        }
-        ws = __shfl_sync(LMOE_FULL, ws, be & 31);
+        const float ws = __shfl_sync(LMOE_FULL, lbs, be & 31);
         if (lane == j) {
             my_e = be;
             my_s = ws;
+        }
+        if (lbe == be) {  // the winner drops it and rescans
+            lbv = -INFINITY;
+            lbe = 0x7fffffff;
+#pragma unroll
+            for (int i = 0; i < kRouterMaxEPL; ++i) {
+                if (lane + 32 * i == be) bs[i] = -INFINITY;
+                if (bs[i] > lbv) {
+                    lbv = bs[i];
+                    lbe = lane + 32 * i;
+                    lbs = sc[i];
+                }
+            }
         }
     }
     float ssum = 0.0f;  // fp32, in selection order
@@ -305,6 +389,7 @@ __device__ void topk_token(const float *partial, int ksplit, int T, int E, int t
         w_ws[o] = wv;
         if (idx_user) idx_user[o] = my_e;
         if (w_user) w_user[o] = wv;
+        if (s_idx) s_idx[o] = my_e;
     }
 }
 
@@ -335,6 +420,37 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
     const int tbeg = blockIdx.y * 64;
     const int tend = min(a.T, tbeg + 64);
     const int nchunk = a.H / kRouterKS;
+    __shared__ float s_bias[EPB];
+    if (tid < EPB) s_bias[tid] = (a.bias && e0 + tid < a.E) ? a.bias[e0 + tid] : 0.0f;
+    // Decode (one pass of at most 8 tokens): this warp's first two weight
+    // chunks are requested before the panel work so their latency overlaps it.
+    const bool one_pass = (tend - tbeg) <= 8;
+    uint4 wpre[2][EPB];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        const int ch = warp + 8 * j;
+#pragma unroll
+        for (int i = 0; i < EPB; ++i) {
+            wpre[j][i] = make_uint4(0, 0, 0, 0);
+            if (one_pass && ch < nchunk && e0 + i < a.E)
+                wpre[j][i] = __ldg(reinterpret_cast<const uint4 *>(a.wg + (size_t)(e0 + i) * a.H + ch * kRouterKS +
+                                                                   lane * 8));
+        }
+    }
+
+    // everything above reads constants only; x and the workspace come from
+    // the preceding kernels
+    pdl_wait();
+    pdl_trigger();
+    // single token: its first two activation chunks are requested now too
+    const bool one_tok = (tend - tbeg) == 1;
+    uint4 xpre[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        const int ch = warp + 8 * j;
+        xpre[j] = make_uint4(0, 0, 0, 0);
+        if (one_tok && ch < nchunk) xpre[j] = __ldg(reinterpret_cast<const uint4 *>(a.x + (size_t)tbeg * a.H + ch * kRouterKS + lane * 8));
+    }
 
     // ---- gate/up activation panel + 16-column sums for this block's share.
     // Panel positions of group G are G*gs + (position within the group), so a
@@ -393,19 +509,28 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
 #pragma unroll
             for (int n = 0; n < 8; ++n) acc[i][n] = 0.0f;
 #pragma unroll 2
-        for (int ch = warp; ch < nchunk; ch += 8) {
+        for (int ch = warp, j = 0; ch < nchunk; ch += 8, ++j) {
             const int col = ch * kRouterKS + lane * 8;
             uint4 wv[EPB];
 #pragma unroll
             for (int i = 0; i < EPB; ++i) {
-                wv[i] = make_uint4(0, 0, 0, 0);
-                if (e0 + i < a.E) wv[i] = __ldg(reinterpret_cast<const uint4 *>(a.wg + (size_t)(e0 + i) * a.H + col));
+                if (one_pass && j == 0) {
+                    wv[i] = wpre[0][i];
+                } else if (one_pass && j == 1) {
+                    wv[i] = wpre[1][i];
+                } else {
+                    wv[i] = make_uint4(0, 0, 0, 0);
+                    if (e0 + i < a.E)
+                        wv[i] = __ldg(reinterpret_cast<const uint4 *>(a.wg + (size_t)(e0 + i) * a.H + col));
+                }
             }
             uint4 xv[8];
 #pragma unroll
             for (int n = 0; n < 8; ++n) {
                 xv[n] = make_uint4(0, 0, 0, 0);
-                if (n < nt) xv[n] = __ldg(reinterpret_cast<const uint4 *>(a.x + (size_t)(ts + n) * a.H + col));
+                if (n == 0 && one_tok && j == 0) xv[0] = xpre[0];
+                else if (n == 0 && one_tok && j == 1) xv[0] = xpre[1];
+                else if (n < nt) xv[n] = __ldg(reinterpret_cast<const uint4 *>(a.x + (size_t)(ts + n) * a.H + col));
             }
 #pragma unroll
             for (int n = 0; n < 8; ++n) {
@@ -452,7 +577,13 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
             const int i = tid >> 3, n = tid & 7;
             float v = 0.0f;
             for (int w = 0; w < 8; ++w) v += s_red[w][i][n];
-            if (e0 + i < a.E && n < nt) a.partial[(size_t)(ts + n) * a.E + e0 + i] = v;
+            if (e0 + i < a.E && n < nt) {
+                a.partial[(size_t)(ts + n) * a.E + e0 + i] = v;
+                if (a.scores) {
+                    const float sc = score_fn(v, a.scoring);
+                    a.scores[(size_t)(ts + n) * a.E + e0 + i] = make_float2(sc, sc + s_bias[i]);
+                }
+            }
         }
         __syncthreads();
     }
@@ -468,20 +599,34 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
     if (!s_last) return;
     __threadfence();
     if (tid == 0) *a.counter = 0u;
+    // small dispatch: the winners and the expert -> slot table go through
+    // shared memory (the slot table load overlaps the top-k)
+    const bool warp_disp = a.do_dispatch && a.din.R <= 32 && a.E <= kDispatchSmallMaxRoutes;
+    int *s_idx = s_disp;                              // [32]
+    int *s_slot = s_disp + 32;                        // [E]
+    if (warp_disp)
+        for (int e = tid; e < a.E; e += blockDim.x) s_slot[e] = a.din.expert_slot ? a.din.expert_slot[e] : e;
     for (int tok = warp; tok < a.T; tok += 8)
-        topk_token(a.partial, 1, a.T, a.E, tok, a.bias, a.scoring, a.top_k, a.norm_topk, a.scaling, a.idx_ws,
-                   a.w_ws, a.idx_user, a.w_user);
+        topk_token(a.partial, a.scores, 1, a.T, a.E, tok, a.bias, a.scoring, a.top_k, a.norm_topk, a.scaling,
+                   a.idx_ws, a.w_ws, a.idx_user, a.w_user, warp_disp ? s_idx : nullptr);
     if (!a.do_dispatch) return;
+    if (warp_disp) {
+        __syncthreads();
+        if (warp == 0) dispatch_warp(a.din, a.dout, a.err, s_idx, s_slot);
+        return;
+    }
     __threadfence();
     __syncthreads();
     dispatch_block(a.din, a.dout, a.err, s_disp);
 }
 
 __global__ void __launch_bounds__(256) topk_kernel(TopkArgs a) {
+    pdl_wait();
+    pdl_trigger();
     const int warp = threadIdx.x >> 5;
     const int tok = blockIdx.x * 8 + warp;
     if (tok >= a.T) return;
-    topk_token(a.partial, a.ksplit, a.T, a.E, tok, a.bias, a.scoring, a.top_k, a.norm_topk,
+    topk_token(a.partial, a.scores, a.ksplit, a.T, a.E, tok, a.bias, a.scoring, a.top_k, a.norm_topk,
                a.scaling, a.idx_ws, a.w_ws, a.idx_user, a.w_user);
 }
 
@@ -490,6 +635,8 @@ __global__ void __launch_bounds__(256) topk_kernel(TopkArgs a) {
 // (sums in column order, as the router's panel producer computes them).
 template <typename TA>
 __global__ void __launch_bounds__(256) panel_kernel(PanelArgs a) {
+    pdl_wait();
+    pdl_trigger();
     const int row = blockIdx.x;
     const int col = blockIdx.y * 256 + threadIdx.x;
     const uint16_t *src = a.x + (size_t)row * a.K;
@@ -526,38 +673,32 @@ __global__ void __launch_bounds__(256) panel_kernel(PanelArgs a) {
 // ============================================================ launchers
 cudaError_t launch_router(const RouterArgs &a, int /*ksplit*/, cudaStream_t st) {
     dim3 grid((a.E + 1) / 2, (a.T + 63) / 64, 1);
-    if (a.act_f16)
-        router_kernel<__half><<<grid, 256, 0, st>>>(a);
-    else
-        router_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(a);
-    return cudaGetLastError();
+    if (a.act_f16) return launch_pdl(router_kernel<__half>, grid, dim3(256), 0, st, a);
+    return launch_pdl(router_kernel<__nv_bfloat16>, grid, dim3(256), 0, st, a);
 }
 
 cudaError_t launch_topk(const TopkArgs &a, cudaStream_t st) {
-    topk_kernel<<<(a.T + 7) / 8, 256, 0, st>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(topk_kernel, dim3((a.T + 7) / 8), dim3(256), 0, st, a);
 }
 
 cudaError_t launch_dispatch_small(const DispatchIn &din, const DispatchOut &dout, int32_t *err,
                                   cudaStream_t st) {
-    dispatch_small_kernel<<<1, 256, 0, st>>>(din, dout, err);
-    return cudaGetLastError();
+    return launch_pdl(dispatch_small_kernel, dim3(1), dim3(256), 0, st, din, dout, err);
 }
 
 cudaError_t launch_dispatch_large(const DispatchIn &din, const DispatchOut &dout, int32_t *err,
                                   cudaStream_t st) {
-    dispatch_rank_kernel<<<din.n_experts + 1, 256, 0, st>>>(din, dout, err);
-    dispatch_chunks_kernel<<<1, 256, 0, st>>>(din, dout, err);
-    return cudaGetLastError();
+    cudaError_t e = launch_pdl(dispatch_rank_kernel, dim3(din.n_experts + 1), dim3(256), 0, st, din, dout, err);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(dispatch_chunks_kernel, dim3(1), dim3(256), 0, st, din, dout, err);
 }
 
 cudaError_t launch_panel(const PanelArgs &a, cudaStream_t st) {
     dim3 grid(a.rows, (a.K + 255) / 256);
     if (a.act_f16)
-        panel_kernel<__half><<<grid, 256, 0, st>>>(a);
+        return launch_pdl(panel_kernel<__half>, grid, dim3(256), 0, st, a);
     else
-        panel_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(a);
-    return cudaGetLastError();
+        return launch_pdl(panel_kernel<__nv_bfloat16>, grid, dim3(256), 0, st, a);
 }
 
 }  // namespace lmoe
