@@ -63,7 +63,7 @@ def parse():
     p.add_argument("--layers", type=int, default=0, help="distinct layers cycled (0 = auto)")
     p.add_argument("--e2e-steps", type=int, default=200)
     p.add_argument("--kernel-steps", type=int, default=200)
-    p.add_argument("--cpu-sample", type=int, default=2, help="tokens timed for the CPU baseline")
+    p.add_argument("--cpu-sample", type=int, default=24, help="decode steps timed for the CPU baseline")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--layout", choices=["tiled", "rowmajor"], default="tiled",
                    help="expert weights in HBM: pre-tiled (one bulk copy per 16-row tile) or the row-major arrays")
@@ -166,6 +166,20 @@ def cpu_baseline_sample(cfg, layer_cpu, xs_cpu, n_tokens: int):
                       f"accumulation, {dt:.1f}s"}
 
 
+def workload_config(cfg, T, world, n_layers, layout):
+    """The ``config`` object of the JSON line (identical for both arms)."""
+    return {
+        "workload": f"{cfg.name} decode: hidden {cfg.hidden}, {cfg.n_experts} experts top-{cfg.top_k}, inter "
+                    f"{cfg.inter}, {cfg.bits_gate}/{cfg.bits_up}/{cfg.bits_down}-bit affine g{cfg.group_size}, "
+                    f"routed scaling {cfg.routed_scaling}, T={T} tokens/step, all experts HBM-resident",
+        "global_batch": T * world, "parallelism": f"replicas{world}" if world > 1 else "single",
+        "layers_cycled": n_layers,
+        "l2": f"{n_layers} distinct layers cycled; >{4 * 126} MB of expert bytes touched between reuses",
+        "weights": f"{cfg.bits_gate}-bit affine g{cfg.group_size} (uint32 codes, bf16 scales/biases)",
+        "layout": layout,
+    }
+
+
 # ------------------------------------------------------------------ reference arm
 def run_reference(args):
     world, rank, _ = dist_env()
@@ -183,24 +197,31 @@ def run_reference(args):
     from oracle.bridge import layer_np, t2np
 
     L = layer_np(layer)
-    for i in range(args.warmup):
+    # each step is one decode step of the workload; the run is bounded to
+    # about a minute of CPU work (at most one warm-up step, timed steps until
+    # --steps or the time budget is reached)
+    for i in range(min(args.warmup, 1)):
         O.moe_layer(t2np(xs[i]), L, acc=np.float32)
+    budget_s = 60.0
+    done = 0
     t0 = time.perf_counter()
     for i in range(args.warmup, n):
         O.moe_layer(t2np(xs[i]), L, acc=np.float32)
+        done += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
     dt = time.perf_counter() - t0
-    value = cfg.tokens * args.steps / dt
+    value = cfg.tokens * done / dt
     threads = os.cpu_count() or 1
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps, "higher_is_better": True,
+        "warmup": args.warmup, "ms_per_step": 1e3 * dt / done, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "impl": "reference",
-        "config": {"workload": f"{cfg.name}: hidden {cfg.hidden}, {cfg.n_experts} experts top-{cfg.top_k}, inter "
-                               f"{cfg.inter}, bits {cfg.bits_gate}/{cfg.bits_up}/{cfg.bits_down} g{cfg.group_size}, "
-                               f"T={cfg.tokens}", "global_batch": cfg.tokens},
+        "config": workload_config(cfg, cfg.tokens, world, args.layers or 16, args.layout),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": f"{args.steps} timed decode steps of {cfg.name} through the numpy oracle "
-                                   "(the reference MLX CPU path is not importable here)"},
+                         "sample": f"{done} timed decode steps of {cfg.name} ({dt:.1f}s; at most {args.steps} "
+                                   "or about 60s) through the numpy oracle (the reference MLX CPU path is not "
+                                   "importable here)"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -319,24 +340,16 @@ def run_ours(args):
     cpu = None
     if not args.no_cpu_baseline and world == 1:
         layer_cpu = synth.layer_to(layers[0], "cpu")
-        xs_cpu = [xs[i].cpu() for i in range(args.cpu_sample)]
+        n_cpu = min(args.cpu_sample, xs.shape[0])
+        xs_cpu = [xs[i].cpu() for i in range(n_cpu)]
         del layers
-        cpu = cpu_baseline_sample(cfg, layer_cpu, xs_cpu, args.cpu_sample)
+        cpu = cpu_baseline_sample(cfg, layer_cpu, xs_cpu, n_cpu)
 
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16", "data": "synthetic",
-        "config": {
-            "workload": f"{cfg.name} decode: hidden {cfg.hidden}, {cfg.n_experts} experts top-{cfg.top_k}, inter "
-                        f"{cfg.inter}, {cfg.bits_gate}/{cfg.bits_up}/{cfg.bits_down}-bit affine g{cfg.group_size}, "
-                        f"routed scaling {cfg.routed_scaling}, T={T} tokens/step, all experts HBM-resident",
-            "global_batch": T * world, "parallelism": f"replicas{world}" if world > 1 else "single",
-            "layers_cycled": n_layers,
-            "l2": f"{n_layers} distinct layers cycled; >{4 * 126} MB of expert bytes touched between reuses",
-            "weights": f"{cfg.bits_gate}-bit affine g{cfg.group_size} (uint32 codes, bf16 scales/biases)",
-            "layout": args.layout,
-        },
+        "config": workload_config(cfg, T, world, n_layers, args.layout),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": traffic, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
                      "kernel": "gemv_kernel<bf16, gate/up>", "algorithmic_bytes_per_launch": gu_bytes},

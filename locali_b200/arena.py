@@ -66,7 +66,8 @@ class _Fill:
 
 class ArenaStore:
     def __init__(self, index_path=None, ceiling_gb=8.0, hot_share=0.33, threads=8, nocache=True,
-                 cache_policy="lru", *, device=None, index: dict | None = None, slots: dict | None = None):
+                 cache_policy="lru", *, device=None, index: dict | None = None, slots: dict | None = None,
+                 tiled: bool = True):
         idx = index if index is not None else json.loads(Path(index_path).read_text())
         if cache_policy not in POLICIES:
             raise ValueError("cache_policy must be 'lru', 'slru-cold', 'slru-all', or 'lfu-decay'")
@@ -116,6 +117,17 @@ class ArenaStore:
         self._table_dirty = set()
         self.copy_stream = torch.cuda.Stream(self.device) if self.device.type == "cuda" else None
         self._staging: dict[str, queue.Queue] = {}
+        # Pre-tiled copy of every slot (16-row tiles of codes + scales +
+        # biases, one bulk copy each for the decode GEMV), kept in step with
+        # the row-major slot arrays by repacking a slot whenever it is filled.
+        # Device arenas only; no counterpart in the reference.
+        self.tiles = {}
+        if tiled and self.device.type == "cuda":
+            for t in self.tiers:
+                for p in PROJS:
+                    nb = self._qproj(t, p).tile_bytes()
+                    if nb:
+                        self.tiles[(t, p)] = torch.zeros((self.slots[t], nb), dtype=torch.uint8, device=self.device)
 
     # ------------------------------------------------------------ metadata
     def tier(self, layer, expert):
@@ -135,6 +147,21 @@ class ArenaStore:
         if field == "mode":
             return "affine"
         raise KeyError(field)
+
+    def _qproj(self, tier, proj):
+        """Kernel descriptor of one projection of all slots of a tier."""
+        from . import ops
+
+        a = self.arena
+        return ops.QProjArrays(a[(tier, proj, "weight")], a[(tier, proj, "scales")], a[(tier, proj, "biases")],
+                               self.quant(tier, "bits", proj), self.quant(tier, "group_size", proj),
+                               getattr(self, "tiles", {}).get((tier, proj)))
+
+    def _pack(self, tier, s0, n=1):
+        """Repack slots [s0, s0 + n) of a tier into its tiles (current stream)."""
+        for p in PROJS:
+            if (tier, p) in self.tiles:
+                self._qproj(tier, p).pack_tiles(s0, n)
 
     def cols(self, tier, proj):
         """Logical input width of a projection (hidden for gate/up, inter for down)."""
@@ -300,6 +327,7 @@ class ArenaStore:
                 for (o, n), (p, k) in zip(views, [(p, k) for p in PROJS for k in ARRS]):
                     dst = self.arena[(t, p, k)][s].view(-1).view(torch.uint8)
                     dst.copy_(buf[o:o + n], non_blocking=True)
+                self._pack(t, s)
                 ev = torch.cuda.Event()
                 ev.record(self.copy_stream)
             ev.synchronize()  # the staging buffer is reusable once its copies are done
@@ -410,13 +438,15 @@ class ArenaStore:
                 store.lru["cold"][key] = s
                 store._set_table(key, s)
         store.free["cold"] = []
+        store._pack("cold", 0, n)
         store.sync_table()
         torch.cuda.synchronize(store.device)
         return store
 
-    def _init_resident(self, idx, n_slots, device, cache_policy="lru", threads=2):
+    def _init_resident(self, idx, n_slots, device, cache_policy="lru", threads=2, tiled=True):
         ArenaStore.__init__(self, None, ceiling_gb=0.0, threads=threads, cache_policy=cache_policy, device=device,
-                            index=idx, slots={t: n_slots for t in sorted({m["tier"] for m in idx["experts"].values()})})
+                            index=idx, slots={t: n_slots for t in sorted({m["tier"] for m in idx["experts"].values()})},
+                            tiled=tiled)
 
 
 class ArenaMoE:

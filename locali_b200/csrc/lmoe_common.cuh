@@ -201,9 +201,21 @@ struct Unpack<TA, 8> {
 
 // On-demand pair extraction for the MMA A operand.  prep() runs once per code
 // word, get(w, m) yields pair m (c_m, c_{m+kCpw/2}) as packed 16-bit values.
-// For 2- and 4-bit codes the pair keeps the magic offset (value kMagicVal +
-// c*4^p resp. kMagicVal + c); the consumer removes kMagicVal * sum(panel) per
-// group after the MMA instead of subtracting it from every pair.
+// bf16, 2- and 4-bit codes: the pair keeps the magic offset (value 128 +
+// c*4^p resp. 128 + c) and the consumer removes 128 * sum(panel) per group
+// after the MMA (kFoldOffset); the cancellation costs about 7 of fp32's 24
+// bits, far below bf16 output precision.  f16: the offset is 1024 and the
+// 10 lost bits would show in f16 outputs, so the magic is subtracted from
+// every pair (exact small integers) instead.
+template <typename TA>
+struct FoldOffset {
+    static constexpr bool value = false;
+};
+template <>
+struct FoldOffset<__nv_bfloat16> {
+    static constexpr bool value = true;
+};
+
 template <typename TA, int BITS>
 struct PairX;
 
@@ -215,7 +227,8 @@ struct PairX<TA, 2> {
     __device__ __forceinline__ static W prep(uint32_t w) { return W{w, w >> 6, w >> 12}; }
     __device__ __forceinline__ static uint32_t get(const W &w, int m) {
         const uint32_t v = m < 3 ? w.v0 : (m < 6 ? w.v1 : w.v2);
-        return (v & (0x00030003u << (2 * (m % 3)))) | Act<TA>::kMagic;
+        const uint32_t r = (v & (0x00030003u << (2 * (m % 3)))) | Act<TA>::kMagic;
+        return FoldOffset<TA>::value ? r : Act<TA>::sub_magic(r);
     }
 };
 
@@ -224,7 +237,8 @@ struct PairX<TA, 4> {
     using W = uint32_t;
     __device__ __forceinline__ static W prep(uint32_t w) { return w; }
     __device__ __forceinline__ static uint32_t get(W w, int m) {
-        return ((w >> (4 * m)) & 0x000F000Fu) | Act<TA>::kMagic;
+        const uint32_t r = ((w >> (4 * m)) & 0x000F000Fu) | Act<TA>::kMagic;
+        return FoldOffset<TA>::value ? r : Act<TA>::sub_magic(r);
     }
 };
 

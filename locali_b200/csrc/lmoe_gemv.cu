@@ -512,7 +512,7 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) gemv_kernel(const GemvArgs
 
     // ========================================================= consumers
     using PX = PairX<TA, BITS>;
-    constexpr bool OFFSET = (BITS != 8);  // codes carry the magic offset, removed after the MMA
+    constexpr bool OFFSET = (BITS != 8) && FoldOffset<TA>::value;  // magic offset removed after the MMA
     constexpr float kM = Act<TA>::kMagicVal;
     const int Gw = c.gw;
     const int Gbeg = warp * Gw;

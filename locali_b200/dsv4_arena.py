@@ -72,6 +72,7 @@ class V4ArenaStore(ArenaStore):
                 store.lru["cold"][(l, e)] = s
                 store._set_table((l, e), s)
         store.free["cold"] = []
+        store._pack("cold", 0, L * E + 1)
         store.sync_table()
         torch.cuda.synchronize(store.device)
         return store
@@ -181,12 +182,8 @@ class V4ArenaMoE(ArenaMoE):
         return self.gate(x, input_ids)
 
     def experts(self, tier) -> ops.ExpertArrays:
-        def proj(p):
-            a = self.store.arena
-            return ops.QProjArrays(a[(tier, p, "weight")], a[(tier, p, "scales")], a[(tier, p, "biases")],
-                                   self.store.quant(tier, "bits", p), self.store.quant(tier, "group_size", p))
-
-        return ops.ExpertArrays(proj("gate_proj"), proj("up_proj"), proj("down_proj"))
+        q = self.store._qproj
+        return ops.ExpertArrays(q(tier, "gate_proj"), q(tier, "up_proj"), q(tier, "down_proj"))
 
     def kernel(self, tier) -> ops.MoEKernel:
         k = self._kernels.get(tier)

@@ -51,6 +51,21 @@ def test_v4_module_direct_path_matches_oracle(built):
         assert torch.equal(out, out_h)
 
 
+def test_v4_module_tiled_store_matches_row_major(built):
+    """The store's pre-tiled slot copies give the same bits as the row-major arrays."""
+    cfg = synth.config("c1", n_experts=16)
+    layers = [synth.make_layer(cfg, seed=s, device="cuda") for s in range(2)]
+    tiled = V4ArenaStore.from_layers([l.experts for l in layers], top_k=cfg.top_k, device="cuda")
+    plain = V4ArenaStore.from_layers([l.experts for l in layers], top_k=cfg.top_k, device="cuda", tiled=False)
+    assert tiled.tiles and not plain.tiles
+    x = synth.make_tokens(cfg, 1, seed=5, device="cuda")
+    for li in range(2):
+        outs = [V4ArenaMoE(st, li, V4Gate(layers[li].router), cfg.top_k, swiglu_limit=cfg.swiglu_limit,
+                           fused_decode=True)(x) for st in (tiled, plain)]
+        torch.cuda.synchronize()
+        assert torch.equal(outs[0], outs[1])
+
+
 @pytest.mark.parametrize("native", [True, False])
 def test_v4_module_streams_from_pack_with_small_arena(built, tmp_path, native):
     cfg = synth.config("c0", n_experts=8, top_k=2)
@@ -75,6 +90,7 @@ def test_v4_module_streams_from_pack_with_small_arena(built, tmp_path, native):
             assert O.rel_l2(t2np(out), ref["out"]) < 4e-3
         st = store.stats()
         assert st["misses"] > 0 and st["bytes_read"] > 0 and st["evictions"] > 0
+        assert store.tiles  # fills repacked the tiled copies the kernels read
         assert st["scheduler"] == ("c" if native else "python")
     finally:
         store.close()

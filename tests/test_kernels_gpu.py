@@ -155,6 +155,23 @@ def test_layer_tiled_identical(built, name, T):
     assert torch.equal(out, out_t)
 
 
+@pytest.mark.parametrize("T", [1, 5])
+def test_layer_staged_identical(built, T):
+    """The staged entry (events between the kernels) computes the same bits."""
+    cfg = synth.config("c1", n_experts=32)
+    layer = synth.make_layer(cfg, seed=4, device="cuda")
+    layer.experts.pack_tiles()
+    x = synth.make_tokens(cfg, T, seed=6, device="cuda")
+    kern = ops.MoEKernel(layer.router, layer.experts, layer.expert_slot, cfg.swiglu_limit, "fused")
+    want = kern(x).clone()
+    out = torch.empty_like(want)
+    e1, e2 = torch.cuda.Event(), torch.cuda.Event()
+    kern.staged(x, out, e1, e2)
+    torch.cuda.synchronize()
+    kern.ws.check()
+    assert torch.equal(out, want)
+
+
 def test_layer_c0_matches_oracle(built):
     cfg = synth.config("c0")
     err, _, _ = _check_layer(cfg, cfg.tokens)
