@@ -65,6 +65,8 @@ def parse():
     p.add_argument("--kernel-steps", type=int, default=200)
     p.add_argument("--cpu-sample", type=int, default=24, help="decode steps timed for the CPU baseline")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--ep", action="store_true",
+                   help="expert-parallel layer (experts sharded over the ranks, NCCL all-to-all dispatch/combine)")
     p.add_argument("--layout", choices=["tiled", "rowmajor"], default="tiled",
                    help="expert weights in HBM: pre-tiled (one bulk copy per 16-row tile) or the row-major arrays")
     return p.parse_args()
@@ -120,7 +122,7 @@ class ClockSampler:
                         self.reasons.add(k)
             except Exception:
                 pass
-            time.sleep(0.001)
+            time.sleep(0.0005)
 
     def __enter__(self):
         if self.nv is not None:
@@ -281,6 +283,8 @@ def run_ours(args):
         start.record()
         graph.replay()
         end.record()
+        while not end.query():  # sleep-poll: the sampler thread runs meanwhile
+            time.sleep(0.0005)
         torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
@@ -403,10 +407,98 @@ def run_e2e(args, cfg, layers, n_layers, dev):
             "d2h_bytes_per_step": bytes_step, "api": "V4ArenaMoE.__call__ (fused router+experts, device slot table)"}
 
 
+def run_ep(args):
+    """Expert-parallel mode: rank r owns experts [r*E/N, (r+1)*E/N) of every
+    layer, routes its own T tokens, and exchanges token rows and partial
+    outputs with NCCL all-to-all.  Timed with CUDA events around K steps (the
+    variable all-to-all splits need host-side counts, so no graph), max over
+    ranks."""
+    import datetime
+
+    import torch.distributed as dist
+
+    from locali_b200 import ep, synth
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    over = {}
+    if args.tokens is not None:
+        over["tokens"] = args.tokens
+    if args.experts is not None:
+        over["n_experts"] = args.experts
+    cfg = synth.config(args.config, **over)
+    T = cfg.tokens
+    n_layers = args.layers or 16
+    mods = []
+    for i in range(n_layers):
+        layer = synth.make_layer(cfg, seed=1000 + i, device=dev)  # same weights on every rank
+        shard = ep.shard_experts(layer.experts, rank, world, cfg.n_experts)
+        if args.layout == "tiled":
+            shard.pack_tiles()
+        st = ep.EPRank(layer.router, shard, rank, world, cfg.n_experts, cfg.swiglu_limit)
+        mods.append(ep.ExpertParallelMoE(st) if world > 1 else st)
+        del layer
+    torch.cuda.empty_cache()
+    K, W = args.steps, args.warmup
+    g = torch.Generator(device=dev).manual_seed(77 + rank)
+    xs = torch.randn((K + W, T, cfg.hidden), generator=g, device=dev).to(torch.bfloat16)
+
+    def step(i):
+        m = mods[i % n_layers]
+        if world > 1:
+            return m(xs[i])
+        return ep.loopback_forward([m], [xs[i]])[0]
+
+    for i in range(W):
+        step(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index) as clocks:
+        start.record()
+        for s in range(K):
+            step(W + s)
+        end.record()
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = world * T * K / (ms / 1e3)
+    # algorithmic bytes: every selected expert's weights once per step
+    # (all ranks together), plus the router weights on every rank
+    layer_bytes = 6 * cfg.expert_bytes() if T == 1 else None
+    peak, peak_kind = measured_peak()
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic",
+        "config": dict(workload_config(cfg, T, world, n_layers, args.layout), parallelism=f"ep{world}"),
+        "roofline": {"bound": "hbm", "achieved": None, "peak": peak, "unit": "GB/s", "frac": None, "traffic": None,
+                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                     "note": "expert-parallel mode: per-kernel rooflines are in the single-GPU line"},
+        "gpu_launches": None, "clocks": clocks.summary(), "e2e": None, "cpu_baseline": None,
+    }
+    if layer_bytes:
+        line["layer_bytes_per_step_all_ranks"] = layer_bytes
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.ep:
+        run_ep(args)
     else:
         run_ours(args)
 

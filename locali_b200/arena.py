@@ -115,6 +115,7 @@ class ArenaStore:
         self.slot_table = torch.full((self.layers, self.E), -1, dtype=torch.int32, device=self.device)
         self._table_host = np.full((self.layers, self.E), -1, dtype=np.int32)
         self._table_dirty = set()
+        self.table_version = 0  # bumped on every slot-table change
         self.copy_stream = torch.cuda.Stream(self.device) if self.device.type == "cuda" else None
         self._staging: dict[str, queue.Queue] = {}
         # Pre-tiled copy of every slot (16-row tiles of codes + scales +
@@ -228,6 +229,7 @@ class ArenaStore:
         if 0 <= layer < self.layers and 0 <= expert < self.E:
             self._table_host[layer, expert] = slot
             self._table_dirty.add(layer)
+            self.table_version += 1
 
     def sync_table(self, stream=None):
         """Push changed rows of the slot table to the device (async, small)."""

@@ -199,13 +199,18 @@ class V4ArenaMoE(ArenaMoE):
     def __call__(self, x, input_ids=None):
         shape = x.shape
         flat = x.reshape(-1, shape[-1])
-        tier = self.store.tier(self.layer, 0)
-        direct = (isinstance(self.gate, V4Gate) and self.nxt is None and self.nxt2 is None
-                  and self.store.layer_resident(self.layer))
+        # the layer's tier and residency only change with the slot table
+        ver = self.store.table_version
+        if self.__dict__.get("_ver") != ver:
+            self._tier = self.store.tier(self.layer, 0)
+            self._resident = self.store.layer_resident(self.layer)
+            self._ver = ver
+        tier = self._tier
+        direct = (self._resident and isinstance(self.gate, V4Gate) and self.nxt is None and self.nxt2 is None)
         if direct:
             self.store.sync_table()
-            out = self.kernel(tier)(flat)
-            return out.reshape(shape).to(x.dtype)
+            out = self.kernel(tier)(flat).reshape(shape)
+            return out if out.dtype == x.dtype else out.to(x.dtype)
         inds, gates = self.route(x, input_ids)
         ii = inds.reshape(-1, self.top_k)
         experts = [e for row in ii.tolist() for e in row]  # host sync, as arena.py:513

@@ -223,10 +223,14 @@ class MoEKernel:
         self.ws = Workspace(expert_slot.device)
 
     def workspace_bytes(self, tokens: int) -> int:
-        n = lmoe().lmoe_workspace_size(ctypes.byref(self.desc), int(tokens))
-        if n == 0:
-            raise _lib.LmoeError(_lib.LMOE_EUNSUPPORTED, "layer descriptor")
-        return int(n)
+        cache = self.__dict__.setdefault("_ws_bytes", {})
+        n = cache.get(tokens)
+        if n is None:
+            n = int(lmoe().lmoe_workspace_size(ctypes.byref(self.desc), int(tokens)))
+            if n == 0:
+                raise _lib.LmoeError(_lib.LMOE_EUNSUPPORTED, "layer descriptor")
+            cache[tokens] = n
+        return n
 
     def _x(self, x: torch.Tensor) -> torch.Tensor:
         _need_cuda(x)
