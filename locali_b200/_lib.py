@@ -7,10 +7,12 @@ loudly: there is no CPU or pure-PyTorch fallback for any kernel.
 from __future__ import annotations
 
 import ctypes
+import os
 from pathlib import Path
 
 PKG = Path(__file__).resolve().parent
-LMOE_PATH = PKG / "liblmoe.so"
+# LMOE_LIBRARY overrides the library path (for comparing builds)
+LMOE_PATH = Path(os.environ["LMOE_LIBRARY"]) if os.environ.get("LMOE_LIBRARY") else PKG / "liblmoe.so"
 CORE_PATH = PKG / "liblocali_core.so"
 
 LMOE_OK = 0

@@ -46,6 +46,13 @@ Layout make_layout(int T, int R, int K, int I, int H_out, int buckets, int E_rou
         return o;
     };
     L.status = take(256);
+    // The regions that must start at zero (status word and router counter
+    // above, combine counters here) sit at fixed offsets at the start, so a
+    // workspace zeroed once serves calls with any token count that fits:
+    // every call restores the counters it used, and a smaller call uses a
+    // prefix of the same zero region.  Everything after is rewritten by each
+    // call before it is read.
+    L.cnt = take((size_t)T * (H_out / 16) * 4);
     // logits, then (score, biased score) per (token, expert)
     L.partial = take((size_t)ksplit * T * E_router * 4 + 8 + (size_t)T * E_router * 8);
     L.idx = take((size_t)R * 4);
@@ -61,7 +68,6 @@ Layout make_layout(int T, int R, int K, int I, int H_out, int buckets, int E_rou
     L.hpanel = take((size_t)R * I * 2);
     L.hsum = take((size_t)R * (I / 16) * 8);
     L.yw = take((size_t)R * H_out * 2);
-    L.cnt = take((size_t)T * (H_out / 16) * 4);
     L.total = off;
     return L;
 }
@@ -314,6 +320,10 @@ static int route_impl(const lmoe_router &r, int H, int dtype, const lmoe_layer *
                    ? nullptr
                    : reinterpret_cast<float2 *>(a.partial + (((size_t)ksplit * T * r.n_experts + 1) & ~size_t(1)));
     if (l) {
+        // this call's combine counters start at zero whatever the workspace
+        // held before (another token count or entry point)
+        a.zero = at<uint32_t>(ws, L.cnt);
+        a.zero_words = T * (l->experts.hidden / 16);
         a.xpanel = at<uint16_t>(ws, L.xpanel);
         a.xsum16 = at<float>(ws, L.xsum);
         a.pbits = l->experts.gate.bits;
@@ -492,9 +502,12 @@ int lmoe_moe_routed(const lmoe_layer *layer, const void *x, int32_t tokens, cons
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const lmoe_experts &ex = layer->experts;
     PanelArgs pa;
+    std::memset(&pa, 0, sizeof(pa));
     pa.x = static_cast<const uint16_t *>(x);
     pa.rows = tokens;
     pa.K = ex.hidden;
+    pa.zero = at<uint32_t>(workspace, L.cnt);  // this call's combine counters
+    pa.zero_words = tokens * (ex.hidden / 16);
     pa.panel = at<uint16_t>(workspace, L.xpanel);
     pa.sum16 = at<float>(workspace, L.xsum);
     pa.bits = ex.gate.bits;
@@ -533,6 +546,7 @@ int lmoe_gateup_swiglu(const lmoe_experts *experts, const void *x, int32_t token
     if (ws_bytes < L.total) return LMOE_EWORKSPACE;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     PanelArgs pa;
+    std::memset(&pa, 0, sizeof(pa));
     pa.x = static_cast<const uint16_t *>(x);
     pa.rows = tokens;
     pa.K = H;
@@ -575,6 +589,7 @@ int lmoe_gather_qmm(const lmoe_qproj *proj, int32_t n_slots, int32_t rows, int32
     if (ws_bytes < L.total) return LMOE_EWORKSPACE;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     PanelArgs pa;
+    std::memset(&pa, 0, sizeof(pa));
     pa.x = static_cast<const uint16_t *>(x);
     pa.rows = routes;
     pa.K = cols;

@@ -106,6 +106,9 @@ struct RouterArgs {
     DispatchIn din;
     DispatchOut dout;
     int32_t *err;
+    // combine counters of this call, zeroed by the router blocks
+    uint32_t *zero;
+    int32_t zero_words;
 };
 
 struct TopkArgs {
@@ -127,6 +130,8 @@ struct PanelArgs {
     float *sum16;       // [rows, K/16, 2] (sum of x, sum of panel values)
     int32_t bits, gs;
     int32_t act_f16;
+    uint32_t *zero;  // combine counters of this call, zeroed here (or nullptr)
+    int32_t zero_words;
 };
 
 struct GemvArgs {

@@ -442,6 +442,11 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
     // the preceding kernels
     pdl_wait();
     pdl_trigger();
+    if (a.zero) {
+        const int nb = gridDim.x * gridDim.y;
+        for (int i = (blockIdx.y * gridDim.x + blockIdx.x) * blockDim.x + tid; i < a.zero_words; i += nb * blockDim.x)
+            a.zero[i] = 0u;
+    }
     // single token: its first two activation chunks are requested now too
     const bool one_tok = (tend - tbeg) == 1;
     uint4 xpre[2];
@@ -637,6 +642,10 @@ template <typename TA>
 __global__ void __launch_bounds__(256) panel_kernel(PanelArgs a) {
     pdl_wait();
     pdl_trigger();
+    if (a.zero) {
+        const int b = blockIdx.y * gridDim.x + blockIdx.x, nb = gridDim.x * gridDim.y;
+        for (int i = b * blockDim.x + threadIdx.x; i < a.zero_words; i += nb * blockDim.x) a.zero[i] = 0u;
+    }
     const int row = blockIdx.x;
     const int col = blockIdx.y * 256 + threadIdx.x;
     const uint16_t *src = a.x + (size_t)row * a.K;

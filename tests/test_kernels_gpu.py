@@ -172,6 +172,25 @@ def test_layer_staged_identical(built, T):
     assert torch.equal(out, want)
 
 
+def test_workspace_reused_across_token_counts(built):
+    """One workspace serves calls with different token counts and entry
+    points (the combine counters are re-zeroed per call)."""
+    cfg = synth.config("c1", n_experts=32)
+    layer = synth.make_layer(cfg, seed=8, device="cuda")
+    kern = ops.MoEKernel(layer.router, layer.experts, layer.expert_slot, cfg.swiglu_limit, "fused")
+    for T in (7, 1, 3, 1, 5):
+        x = synth.make_tokens(cfg, T, seed=100 + T, device="cuda")
+        got = kern(x).clone()
+        idx, w = kern.route(x)
+        got_r = kern.routed(x, idx, w).clone()
+        fresh = ops.MoEKernel(layer.router, layer.experts, layer.expert_slot, cfg.swiglu_limit, "fused")
+        want = fresh(x)
+        torch.cuda.synchronize()
+        kern.ws.check()
+        assert torch.equal(got, want), T
+        assert torch.equal(got_r, want), T
+
+
 def test_layer_c0_matches_oracle(built):
     cfg = synth.config("c0")
     err, _, _ = _check_layer(cfg, cfg.tokens)
