@@ -851,7 +851,9 @@ bool gemv_config(int mode, int bits, int gs, int K, int ntok_max, GemvCfg *out) 
     c.off_xs = h;
     h = al(h + c.ncw * c.gw * 16 * 4, 128);
     c.off_list = h;
-    c.list_cap = 128;  // per epilogue warp
+    // per epilogue warp; 8 = every unit is combined as soon as it is written
+    // (four epilogue warps have the slack), so no burst is left for the tail
+    c.list_cap = 8;
     h = al(h + kGemvEpi * c.list_cap * 4, 128);
     c.off_ptab = h;
     h = al(h + 128 * 2, 128);
