@@ -152,6 +152,36 @@ int lmoe_moe_layer_staged(const lmoe_layer *layer, const void *x, int32_t tokens
                           size_t ws_bytes, void *stream, void *ev_routed,
                           void *ev_gateup);
 
+/* Expert-product path of a layer call.  The decode path runs the fused
+ * dequant GEMVs (legacy tensor-core MMA on exact codes, fp32 scale and bias
+ * per group).  The prefill path runs the tcgen05 grouped GEMM: each 128-row
+ * weight block is dequantised once per chunk of up to 128 routes of one
+ * expert into the activation dtype (one rounding of scale * q + bias per
+ * weight, as a tensor-core operand) and contracted on the 5th-generation
+ * tensor cores; it needs hidden % 256 == 0, inter % 128 == 0, both a multiple
+ * of 8 quantisation groups, and row-major arena arrays.  AUTO takes the
+ * prefill path when tokens * top_k >= LMOE_PREFILL_MIN_ROUTES_PER_EXPERT *
+ * n_experts and the geometry allows it.  No counterpart in the reference's
+ * own code; MLX's gather_qmm (dsv4_arena.py:198-221) also changes kernels
+ * with the batch size. */
+#define LMOE_PATH_AUTO 0
+#define LMOE_PATH_DECODE 1
+#define LMOE_PATH_PREFILL 2
+#define LMOE_PREFILL_MIN_ROUTES_PER_EXPERT 16
+
+/* lmoe_moe_layer_staged on an explicit path (LMOE_PATH_*); LMOE_EUNSUPPORTED
+ * when the layer's geometry does not allow the requested path. */
+int lmoe_moe_layer_path(const lmoe_layer *layer, const void *x, int32_t tokens,
+                        void *out, int32_t *idx, float *w, void *workspace,
+                        size_t ws_bytes, void *stream, int32_t path,
+                        void *ev_routed, void *ev_gateup);
+
+/* Workspace bytes for lmoe_moe_layer_path calls of up to max_tokens tokens
+ * on `path` (0 when the path is unavailable).  lmoe_workspace_size equals
+ * this with LMOE_PATH_AUTO. */
+size_t lmoe_workspace_size_path(const lmoe_layer *layer, int32_t max_tokens,
+                                int32_t path);
+
 /* Allocation-free lmoe_moe_layer.  No counterpart in the reference: it exists
  * for callers that cannot allocate device memory for a workspace (a serving
  * loop whose device memory belongs to another allocator, a runtime that

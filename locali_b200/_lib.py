@@ -27,6 +27,9 @@ LMOE_F16 = 1
 
 SCORING = {"sigmoid": 0, "softmax": 1, "sqrtsoftplus": 2}
 SWIGLU_MODE = {"fused": 0, "stock": 1}
+# expert-product path of a layer call (LMOE_PATH_*)
+PATH = {"auto": 0, "decode": 1, "prefill": 2}
+PREFILL_MIN_ROUTES_PER_EXPERT = 16
 
 
 class QProj(ctypes.Structure):
@@ -96,6 +99,9 @@ _SIGS = {
                         _VP], ctypes.c_int),
     "lmoe_moe_layer_staged": ([ctypes.POINTER(Layer), _VP, ctypes.c_int32, _VP, _VP, _VP, _VP, ctypes.c_size_t,
                                _VP, _VP, _VP], ctypes.c_int),
+    "lmoe_moe_layer_path": ([ctypes.POINTER(Layer), _VP, ctypes.c_int32, _VP, _VP, _VP, _VP, ctypes.c_size_t,
+                             _VP, ctypes.c_int32, _VP, _VP], ctypes.c_int),
+    "lmoe_workspace_size_path": ([ctypes.POINTER(Layer), ctypes.c_int32, ctypes.c_int32], ctypes.c_size_t),
     "lmoe_moe_layer_static": ([ctypes.POINTER(Layer), _VP, ctypes.c_int32, _VP, _VP, _VP, _VP], ctypes.c_int),
     "lmoe_static_workspace_bytes": ([], ctypes.c_size_t),
     "lmoe_moe_routed": ([ctypes.POINTER(Layer), _VP, ctypes.c_int32, _VP, _VP, _VP, _VP, ctypes.c_size_t,

@@ -26,6 +26,10 @@ struct Layout {
            nchunks = 0, chunks = 0, xpanel = 0, xsum = 0, hpanel = 0, hsum = 0, yw = 0,
            cnt = 0, total = 0;
     int max_chunks = 0;
+    // prefill path: tiled activation panels of the tcgen05 grouped GEMM
+    size_t pfx = 0, pfh = 0;
+    int pf_rows = 0, pf_chunks = 0;
+    bool prefill = false;
 };
 
 int max_chunks_for(int buckets, int R) {
@@ -76,6 +80,25 @@ Layout layer_layout(const lmoe_layer *l, int T) {
     const int H = l->experts.hidden, I = l->experts.inter;
     const int R = T * l->router.top_k;
     return make_layout(T, R, H, I, H, l->router.n_experts + 1, l->router.n_experts, 1, T);
+}
+
+// Layout of the prefill path: the shared routing regions and the y*w rows
+// of make_layout (no GEMV panels), then the two tiled activation panels.
+Layout prefill_layout(const lmoe_layer *l, int T) {
+    const int H = l->experts.hidden, I = l->experts.inter;
+    const int R = T * l->router.top_k;
+    const int buckets = l->router.n_experts + 1;
+    Layout L = make_layout(T, R, H, 0, H, buckets, l->router.n_experts, 1, 0);
+    L.prefill = true;
+    L.pf_chunks = pf_max_chunks(buckets, R);
+    L.pf_rows = pf_panel_rows(R, L.pf_chunks);
+    size_t off = (L.total + 1023) & ~size_t(1023);
+    L.pfx = off;
+    off += (((size_t)L.pf_rows * H * 2) + 1023) & ~size_t(1023);
+    L.pfh = off;
+    off += (((size_t)L.pf_rows * I * 2) + 1023) & ~size_t(1023);
+    L.total = off;
+    return L;
 }
 
 template <typename P>
@@ -236,6 +259,83 @@ int run_experts(const lmoe_layer *l, const Layout &L, void *ws, int T, const flo
                                L.max_chunks, st));
 }
 
+// Prefill path over an already dispatched layer (chunks of at most kPfNmax
+// routes): x rows -> tiled panel, gate/up + SwiGLU on tcgen05 (h straight
+// into the down panel), down on tcgen05 (y*w rows), combine per token.
+int run_experts_pf(const lmoe_layer *l, const Layout &L, void *ws, const void *x, int T, const float *route_w,
+                   void *out, cudaStream_t st, cudaEvent_t ev_gateup = nullptr) {
+    const lmoe_experts &ex = l->experts;
+    const int H = ex.hidden, I = ex.inter, k = l->router.top_k;
+    const int f16 = ex.dtype == LMOE_F16;
+    PfPanelArgs pa;
+    std::memset(&pa, 0, sizeof(pa));
+    pa.x = static_cast<const uint16_t *>(x);
+    pa.K = H;
+    pa.route_div = k;
+    pa.chunks = at<Chunk>(ws, L.chunks);
+    pa.n_chunks = at<int32_t>(ws, L.nchunks);
+    pa.sorted_routes = at<int32_t>(ws, L.sorted);
+    pa.panel = at<uint8_t>(ws, L.pfx);
+    pa.prow = L.pf_rows;
+    pa.bits = ex.gate.bits;
+    int rc = cuda_rc(launch_pf_panel(pa, L.pf_chunks, st));
+    if (rc) return rc;
+    PfArgs g;
+    std::memset(&g, 0, sizeof(g));
+    g.q0 = view(ex.gate, ex.n_slots, I, H);
+    g.q1 = view(ex.up, ex.n_slots, I, H);
+    g.panel = pa.panel;
+    g.prow = L.pf_rows;
+    g.K = H;
+    g.chunks = pa.chunks;
+    g.n_chunks = pa.n_chunks;
+    g.sorted_routes = pa.sorted_routes;
+    g.rbn = I / 128;
+    g.hpanel = at<uint8_t>(ws, L.pfh);
+    g.hprow = L.pf_rows;
+    g.hbits = ex.down.bits;
+    g.limit = l->swiglu_limit;
+    g.swiglu_mode = l->swiglu_mode;
+    g.err = at<int32_t>(ws, L.status);
+    rc = cuda_rc(launch_pf_gemm(PF_GATEUP, f16, ex.gate.bits, ex.gate.group_size, g, st));
+    if (rc) return rc;
+    if (ev_gateup && cudaEventRecord(ev_gateup, st) != cudaSuccess) return LMOE_ECUDA;
+    PfArgs d = g;
+    std::memset(&d.q1, 0, sizeof(d.q1));
+    d.q0 = view(ex.down, ex.n_slots, H, I);
+    d.panel = g.hpanel;
+    d.K = I;
+    d.rbn = H / 256;
+    d.hpanel = nullptr;
+    d.yw = at<uint16_t>(ws, L.yw);
+    d.H = H;
+    d.route_w = route_w;
+    rc = cuda_rc(launch_pf_gemm(PF_DOWN, f16, ex.down.bits, ex.down.group_size, d, st));
+    if (rc) return rc;
+    return cuda_rc(launch_pf_combine(f16, d.yw, T, H, k, static_cast<uint16_t *>(out), st));
+}
+
+// The prefill kernels read the row-major arena arrays in 16-byte pieces.
+bool layer_pf_ok(const lmoe_layer *l) {
+    const lmoe_experts &ex = l->experts;
+    const lmoe_qproj *ps[3] = {&ex.gate, &ex.up, &ex.down};
+    for (const lmoe_qproj *p : ps)
+        if (!p->weight || !p->scales || !p->biases || !aligned16(p->weight) || !aligned16(p->scales) ||
+            !aligned16(p->biases))
+            return false;
+    return pf_supported(ex.hidden, ex.inter, ex.gate.bits, ex.gate.group_size, PF_GATEUP) &&
+           pf_supported(ex.inter, ex.hidden, ex.down.bits, ex.down.group_size, PF_DOWN);
+}
+
+// 1 = prefill grouped GEMM, 0 = decode GEMVs, -1 = the requested path is unavailable
+int choose_path(const lmoe_layer *l, int T, int path) {
+    if (path == LMOE_PATH_DECODE) return 0;
+    const bool ok = layer_pf_ok(l);
+    if (path == LMOE_PATH_PREFILL) return ok ? 1 : -1;
+    if (path != LMOE_PATH_AUTO) return -1;
+    return ok && (long)T * l->router.top_k >= (long)LMOE_PREFILL_MIN_ROUTES_PER_EXPERT * l->router.n_experts;
+}
+
 }  // namespace
 
 extern "C" {
@@ -260,9 +360,7 @@ const char *lmoe_strerror(int status) {
 }
 
 size_t lmoe_workspace_size(const lmoe_layer *layer, int32_t max_tokens) {
-    if (check_layer(layer) || max_tokens < 0) return 0;
-    const int T = max_tokens > 0 ? max_tokens : 1;
-    return layer_layout(layer, T).total;
+    return lmoe_workspace_size_path(layer, max_tokens, LMOE_PATH_AUTO);
 }
 
 size_t lmoe_workspace_size_routes(int32_t max_routes, int32_t hidden, int32_t inter, int32_t n_slots) {
@@ -300,7 +398,7 @@ static int route_impl(const lmoe_router &r, int H, int dtype, const lmoe_layer *
     const int k = r.top_k;
     const int R = T * k;
     const int ksplit = 1;
-    const int chunk_tok = l ? layer_chunk(l, T) : kChunkTok;
+    const int chunk_tok = l ? (L.prefill ? kPfNmax : layer_chunk(l, T)) : kChunkTok;
     if (chunk_tok < 1) return LMOE_EUNSUPPORTED;
     RouterArgs a;
     std::memset(&a, 0, sizeof(a));
@@ -324,10 +422,12 @@ static int route_impl(const lmoe_router &r, int H, int dtype, const lmoe_layer *
         // held before (another token count or entry point)
         a.zero = at<uint32_t>(ws, L.cnt);
         a.zero_words = T * (l->experts.hidden / 16);
-        a.xpanel = at<uint16_t>(ws, L.xpanel);
-        a.xsum16 = at<float>(ws, L.xsum);
-        a.pbits = l->experts.gate.bits;
-        a.pgs = l->experts.gate.group_size;
+        if (!L.prefill) {  // the decode GEMVs read x through the router's panel
+            a.xpanel = at<uint16_t>(ws, L.xpanel);
+            a.xsum16 = at<float>(ws, L.xsum);
+            a.pbits = l->experts.gate.bits;
+            a.pgs = l->experts.gate.group_size;
+        }
     }
     a.act_f16 = dtype == LMOE_F16;
     a.counter = at<uint32_t>(ws, L.status) + 1;
@@ -406,28 +506,54 @@ int lmoe_route(const lmoe_router *router, int32_t hidden, int32_t dtype, const v
                       static_cast<cudaStream_t>(stream));
 }
 
-int lmoe_moe_layer_staged(const lmoe_layer *layer, const void *x, int32_t tokens, void *out, int32_t *idx,
-                          float *w, void *workspace, size_t ws_bytes, void *stream, void *ev_routed,
-                          void *ev_gateup) {
+int lmoe_moe_layer_path(const lmoe_layer *layer, const void *x, int32_t tokens, void *out, int32_t *idx, float *w,
+                        void *workspace, size_t ws_bytes, void *stream, int32_t path, void *ev_routed,
+                        void *ev_gateup) {
     int rc = check_layer(layer);
     if (rc) return rc;
     if (tokens < 0 || (tokens > 0 && (!x || !out || !workspace))) return LMOE_EINVAL;
     if (tokens == 0) return LMOE_OK;
     if (layer->experts.hidden % kRouterKS) return LMOE_EUNSUPPORTED;
-    const Layout L = layer_layout(layer, tokens);
+    const int pf = choose_path(layer, tokens, path);
+    if (pf < 0) return LMOE_EUNSUPPORTED;
+    const Layout L = pf ? prefill_layout(layer, tokens) : layer_layout(layer, tokens);
     if (ws_bytes < L.total) return LMOE_EWORKSPACE;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     rc = route_impl(layer->router, layer->experts.hidden, layer->experts.dtype, layer, L, x, tokens, idx, w,
                     workspace, st);
     if (rc) return rc;
     if (ev_routed && cudaEventRecord(static_cast<cudaEvent_t>(ev_routed), st) != cudaSuccess) return LMOE_ECUDA;
-    return run_experts(layer, L, workspace, tokens, at<float>(workspace, L.w), out, st,
-                       static_cast<cudaEvent_t>(ev_gateup));
+    const float *rw = at<float>(workspace, L.w);
+    if (pf) return run_experts_pf(layer, L, workspace, x, tokens, rw, out, st, static_cast<cudaEvent_t>(ev_gateup));
+    return run_experts(layer, L, workspace, tokens, rw, out, st, static_cast<cudaEvent_t>(ev_gateup));
+}
+
+size_t lmoe_workspace_size_path(const lmoe_layer *layer, int32_t max_tokens, int32_t path) {
+    if (check_layer(layer) || max_tokens < 0) return 0;
+    const int T = max_tokens > 0 ? max_tokens : 1;
+    const int pf = choose_path(layer, T, path);
+    if (pf < 0) return 0;
+    if (path == LMOE_PATH_PREFILL) return prefill_layout(layer, T).total;
+    size_t n = layer_layout(layer, T).total;
+    // AUTO may take either path at token counts up to T; both layouts grow with T
+    if (pf) {
+        const size_t p = prefill_layout(layer, T).total;
+        if (p > n) n = p;
+    }
+    return n;
+}
+
+int lmoe_moe_layer_staged(const lmoe_layer *layer, const void *x, int32_t tokens, void *out, int32_t *idx,
+                          float *w, void *workspace, size_t ws_bytes, void *stream, void *ev_routed,
+                          void *ev_gateup) {
+    return lmoe_moe_layer_path(layer, x, tokens, out, idx, w, workspace, ws_bytes, stream, LMOE_PATH_AUTO,
+                               ev_routed, ev_gateup);
 }
 
 int lmoe_moe_layer(const lmoe_layer *layer, const void *x, int32_t tokens, void *out, int32_t *idx,
                    float *w, void *workspace, size_t ws_bytes, void *stream) {
-    return lmoe_moe_layer_staged(layer, x, tokens, out, idx, w, workspace, ws_bytes, stream, nullptr, nullptr);
+    return lmoe_moe_layer_path(layer, x, tokens, out, idx, w, workspace, ws_bytes, stream, LMOE_PATH_AUTO, nullptr,
+                               nullptr);
 }
 
 }  // extern "C"
@@ -488,7 +614,8 @@ int lmoe_moe_layer_static(const lmoe_layer *layer, const void *x, int32_t tokens
     if (cudaMemsetAsync(at<uint8_t>(ws, L.status), 0, 256, st) != cudaSuccess ||
         cudaMemsetAsync(at<uint8_t>(ws, L.cnt), 0, cnt_bytes, st) != cudaSuccess)
         return LMOE_ECUDA;
-    return lmoe_moe_layer(layer, x, tokens, out, idx, w, ws, LMOE_STATIC_WORKSPACE_BYTES, stream);
+    return lmoe_moe_layer_path(layer, x, tokens, out, idx, w, ws, LMOE_STATIC_WORKSPACE_BYTES, stream,
+                               LMOE_PATH_DECODE, nullptr, nullptr);
 }
 
 int lmoe_moe_routed(const lmoe_layer *layer, const void *x, int32_t tokens, const int32_t *idx,

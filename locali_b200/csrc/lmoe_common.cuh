@@ -116,6 +116,24 @@ struct Act<__half> {
     }
 };
 
+// Clamped SwiGLU of one (gate, up) pair of fp32 accumulators
+// (dsv4_arena.py:223-235): both rounded to the activation dtype first, then
+// up clamped to [-L, L] and gate to min(gate, L) when L > 0.  Mode 0 takes
+// silu in fp32 with one rounding of silu * up (dsv4_kernels.py:165-170);
+// mode 1 rounds op by op in the activation dtype (nn.silu(gate) * up).
+template <typename TA>
+__device__ __forceinline__ float swiglu_h(float gacc, float uacc, float limit, int mode) {
+    float gv = Act<TA>::round(gacc);
+    float uv = Act<TA>::round(uacc);
+    if (limit > 0.0f) {
+        uv = fminf(fmaxf(uv, -limit), limit);
+        gv = fminf(gv, limit);
+    }
+    if (mode == 0) return Act<TA>::round((gv / (1.0f + expf(-gv))) * uv);
+    const float sig = Act<TA>::round(1.0f / (1.0f + expf(-gv)));
+    return Act<TA>::round(Act<TA>::round(gv * sig) * uv);
+}
+
 // ------------------------------------------------------------ code geometry
 template <int BITS, int GS>
 struct Geo {

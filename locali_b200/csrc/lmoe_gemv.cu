@@ -400,19 +400,7 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) gemv_kernel(const GemvArgs
                 float hv[4], hp[4];
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
-                    float gv = Act<TA>::round(fin[0][e]);
-                    float uv = Act<TA>::round(fin[1][e]);
-                    if (a.limit > 0.0f) {
-                        uv = fminf(fmaxf(uv, -a.limit), a.limit);
-                        gv = fminf(gv, a.limit);
-                    }
-                    float h;
-                    if (a.swiglu_mode == 0) {
-                        h = Act<TA>::round((gv / (1.0f + expf(-gv))) * uv);
-                    } else {
-                        const float sig = Act<TA>::round(1.0f / (1.0f + expf(-gv)));
-                        h = Act<TA>::round(Act<TA>::round(gv * sig) * uv);
-                    }
+                    const float h = swiglu_h<TA>(fin[0][e], fin[1][e], a.limit, a.swiglu_mode);
                     const int n = 2 * t + (e & 1);
                     const int row = rt * 16 + g + 8 * (e >> 1);
                     hv[e] = 0.0f;

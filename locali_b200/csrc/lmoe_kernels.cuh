@@ -219,6 +219,69 @@ cudaError_t launch_gemv(int mode, int act_f16, int bits, int gs, const GemvArgs 
 cudaError_t launch_tile_pack(const QView &q, int bits, int gs, int slot_begin, int slot_count, uint8_t *tiles,
                              cudaStream_t st);
 
+// ------------------------------------------------------------ prefill grouped GEMM
+// (lmoe_prefill.cu).  Routes are grouped by expert into chunks of at most
+// kPfNmax (the MMA N); each chunk owns a block of panel rows starting at
+// pf_row_base, 16-aligned and at least round_up(ntok, 16) long.
+constexpr int kPfNmax = 128;
+enum PfMode { PF_GATEUP = 0, PF_DOWN = 1 };
+
+__host__ __device__ inline int pf_row_base(int route_start, int chunk) {
+    return ((route_start + 15) & ~15) + 16 * chunk;
+}
+// panel rows needed for R routes in at most n_chunks chunks
+inline int pf_panel_rows(int R, int n_chunks) { return ((R + 15) & ~15) + 16 * n_chunks + 16; }
+// chunks of at most kPfNmax routes over `buckets` experts (+ zero bucket)
+inline int pf_max_chunks(int buckets, int R) {
+    const int distinct = buckets < R ? buckets : R;
+    return distinct + R / kPfNmax + 1;
+}
+
+// Activation panel of the prefill kernels: [K/64][rows/8][1024 bytes].  Each
+// 1024-byte block holds 8 rows x 64 columns in the 128-byte-swizzled K-major
+// layout of the tensor core's shared-memory operands (16-byte chunk j of row
+// r at chunk position j ^ (r & 7)), with the in-word pair permutation of the
+// consuming projection's bit width (pf_perm_pos).
+struct PfPanelArgs {
+    const uint16_t *x;  // [rows of x, K]
+    int32_t K;
+    int32_t route_div;  // route r reads x row r / route_div
+    const Chunk *chunks;
+    const int32_t *n_chunks;
+    const int32_t *sorted_routes;
+    uint8_t *panel;
+    int32_t prow;  // panel rows
+    int32_t bits;  // bit width of the projection that consumes the panel
+};
+
+struct PfArgs {
+    QView q0, q1;           // gate, up (PF_GATEUP); down (PF_DOWN, q1 unused)
+    const uint8_t *panel;   // activation panel of this kernel
+    int32_t prow;
+    int32_t K;
+    const Chunk *chunks;
+    const int32_t *n_chunks;
+    const int32_t *sorted_routes;
+    int32_t rbn;            // work items per chunk (row-block pairs)
+    // PF_GATEUP: h into the down kernel's panel
+    uint8_t *hpanel;
+    int32_t hprow;
+    int32_t hbits;
+    float limit;
+    int32_t swiglu_mode;
+    // PF_DOWN: bf16(y) * bf16(w) rows [R, H]
+    uint16_t *yw;
+    int32_t H;
+    const float *route_w;
+    int32_t *err;
+};
+
+bool pf_supported(int K, int rows, int bits, int gs, int mode);
+cudaError_t launch_pf_panel(const PfPanelArgs &a, int max_chunks, cudaStream_t st);
+cudaError_t launch_pf_gemm(int mode, int act_f16, int bits, int gs, const PfArgs &a, cudaStream_t st);
+cudaError_t launch_pf_combine(int act_f16, const uint16_t *yw, int T, int H, int top_k, uint16_t *out,
+                              cudaStream_t st);
+
 constexpr int kDispatchSmallMaxRoutes = 512;
 constexpr int kDispatchSmallMaxBuckets = 1024;
 constexpr int kRouterKS = 256;      // K columns per router CTA

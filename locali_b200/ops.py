@@ -211,8 +211,13 @@ class MoEKernel:
     """
 
     def __init__(self, router: RouterArrays, experts: ExpertArrays, expert_slot: torch.Tensor,
-                 swiglu_limit: float = 10.0, swiglu_mode: str = "fused"):
+                 swiglu_limit: float = 10.0, swiglu_mode: str = "fused", path: str = "auto"):
         _need_cuda(router.weight, experts.gate.weight, expert_slot)
+        if path not in _lib.PATH:
+            raise ValueError(f"path must be one of {sorted(_lib.PATH)}")
+        # "decode": fused dequant GEMVs; "prefill": tcgen05 grouped GEMM;
+        # "auto": prefill once tokens * top_k >= 16 * n_experts
+        self.path = path
         if expert_slot.dtype != torch.int32 or not expert_slot.is_contiguous():
             raise ValueError("expert_slot must be contiguous int32")
         self.router, self.experts, self.expert_slot = router, experts, expert_slot
@@ -224,12 +229,12 @@ class MoEKernel:
 
     def workspace_bytes(self, tokens: int) -> int:
         cache = self.__dict__.setdefault("_ws_bytes", {})
-        n = cache.get(tokens)
+        n = cache.get((tokens, self.path))
         if n is None:
-            n = int(lmoe().lmoe_workspace_size(ctypes.byref(self.desc), int(tokens)))
+            n = int(lmoe().lmoe_workspace_size_path(ctypes.byref(self.desc), int(tokens), _lib.PATH[self.path]))
             if n == 0:
                 raise _lib.LmoeError(_lib.LMOE_EUNSUPPORTED, "layer descriptor")
-            cache[tokens] = n
+            cache[(tokens, self.path)] = n
         return n
 
     def _x(self, x: torch.Tensor) -> torch.Tensor:
@@ -245,8 +250,9 @@ class MoEKernel:
         if out is None:
             out = torch.empty_like(flat)
         self.ws.ensure(self.workspace_bytes(T))
-        check(lmoe().lmoe_moe_layer(ctypes.byref(self.desc), flat.data_ptr(), T, out.data_ptr(), _ptr(idx),
-                                    _ptr(w), self.ws.ptr(), self.ws.nbytes, _stream()), "lmoe_moe_layer")
+        check(lmoe().lmoe_moe_layer_path(ctypes.byref(self.desc), flat.data_ptr(), T, out.data_ptr(), _ptr(idx),
+                                         _ptr(w), self.ws.ptr(), self.ws.nbytes, _stream(), _lib.PATH[self.path],
+                                         None, None), "lmoe_moe_layer")
         return out.reshape(x.shape)
 
     def call_static(self, x: torch.Tensor, out: torch.Tensor | None = None, idx: torch.Tensor | None = None,
@@ -270,9 +276,9 @@ class MoEKernel:
         flat = self._x(x)
         T = flat.shape[0]
         self.ws.ensure(self.workspace_bytes(T))
-        check(lmoe().lmoe_moe_layer_staged(ctypes.byref(self.desc), flat.data_ptr(), T, out.data_ptr(), _ptr(idx),
-                                           None, self.ws.ptr(), self.ws.nbytes, _stream(), _event(ev_routed),
-                                           _event(ev_gateup)), "lmoe_moe_layer_staged")
+        check(lmoe().lmoe_moe_layer_path(ctypes.byref(self.desc), flat.data_ptr(), T, out.data_ptr(), _ptr(idx),
+                                         None, self.ws.ptr(), self.ws.nbytes, _stream(), _lib.PATH[self.path],
+                                         _event(ev_routed), _event(ev_gateup)), "lmoe_moe_layer_staged")
         return out
 
     def route(self, x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:

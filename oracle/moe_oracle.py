@@ -32,6 +32,11 @@ What is restated, and from where (paths within gabrielekarra/locali):
 * Combine (``arena.py:543`` and ``:619-624``): weights cast to the activation
   dtype, ``y * w`` rounded per element, summed over k (fp32 accumulation in
   route order, one final rounding; MLX's bf16 reduction order is not pinned).
+* Prefill weights (``weights="rounded"``): the build's prefill path
+  dequantises each weight to the activation dtype before the matrix product
+  (one rounding of the exact ``scale * q + bias``), the dequantise-then-GEMM
+  form MLX's quantized matmul takes for large batches (not pinned here).  The
+  decode path and ``weights="exact"`` never round a weight.
 """
 
 from __future__ import annotations
@@ -50,6 +55,7 @@ __all__ = [
     "unpack_codes",
     "dequantize",
     "gather_qmm",
+    "round_act_exact",
     "swiglu",
     "router",
     "near_ties",
@@ -147,6 +153,16 @@ def unpack_codes(words: np.ndarray, bits: int, K: int | None = None) -> np.ndarr
     return out.reshape(*lead, K).astype(np.uint8)
 
 
+def round_act_exact(a, dtype: str = "bf16") -> np.ndarray:
+    """Round float64 values once to the activation dtype (nearest, ties to
+    even), without an intermediate float32 rounding."""
+    a = np.asarray(a, np.float64)
+    prec, qmin = (8, -133) if dtype == "bf16" else (11, -24)
+    _, e = np.frexp(a)
+    q = np.ldexp(1.0, np.maximum(e - prec, qmin))
+    return (np.rint(a / q) * q).astype(np.float32)
+
+
 def dequantize(words, scales, biases, bits, group_size, K=None):
     """Affine dequantisation ``scale*q + bias`` per group (float64)."""
     q = unpack_codes(words, bits, K).astype(np.float64)
@@ -181,13 +197,14 @@ class QProjNP:
 
 
 def gather_qmm(x: np.ndarray, proj: QProjNP, slots: np.ndarray, dtype: str = "bf16",
-               acc=np.float64) -> np.ndarray:
+               acc=np.float64, weights: str = "exact") -> np.ndarray:
     """``mx.gather_qmm(x, w, s, b, rhs_indices=slots, transpose=True)``.
 
     x: [R, K] float (values already in the activation dtype), one row per
     route; slots: [R] arena slot per route.  Returns [R, N] rounded to dtype.
     Arithmetic per ``dsv4_kernels.py:152-154``: per group
-    ``scale * sum(x*q) + bias * sum(x)``.
+    ``scale * sum(x*q) + bias * sum(x)``.  ``weights="rounded"``: each
+    dequantised weight rounded once to dtype first (the prefill path).
     """
     x = np.asarray(x, dtype=np.float32)
     slots = np.asarray(slots).reshape(-1)
@@ -195,6 +212,15 @@ def gather_qmm(x: np.ndarray, proj: QProjNP, slots: np.ndarray, dtype: str = "bf
     gs = proj.group_size
     G = K // gs
     out = np.zeros((R, proj.rows), dtype=np.float64)
+    if weights == "rounded":
+        for slot in np.unique(slots):
+            rows = np.nonzero(slots == slot)[0]
+            wq = dequantize(proj.weight[slot], proj.scales[slot], proj.biases[slot], proj.bits, gs, K)
+            wr = round_act_exact(wq, dtype).astype(np.float64)
+            out[rows] = x[rows].astype(np.float64) @ wr.T
+        return round_act(out, dtype)
+    if weights != "exact":
+        raise ValueError(weights)
     xg = x.astype(acc).reshape(R, G, gs)
     xsum = xg.sum(-1)  # [R, G]
     for slot in np.unique(slots):
@@ -321,22 +347,22 @@ class LayerNP:
     extra: dict = field(default_factory=dict)
 
 
-def expert_ffn(x: np.ndarray, idx: np.ndarray, layer: LayerNP, acc=np.float64):
+def expert_ffn(x: np.ndarray, idx: np.ndarray, layer: LayerNP, acc=np.float64, weights: str = "exact"):
     """``V4ArenaMoE._gather`` for [T,k] routes: returns (up, gate, h, y)."""
     T, k = idx.shape
     slots = np.asarray(layer.expert_slot)[idx.reshape(-1)]
     xr = np.repeat(np.asarray(x, np.float32), k, axis=0)  # route r = t*k + j
     ex = layer.experts
-    up = gather_qmm(xr, ex.up, slots, layer.dtype, acc)
-    gate = gather_qmm(xr, ex.gate, slots, layer.dtype, acc)
+    up = gather_qmm(xr, ex.up, slots, layer.dtype, acc, weights)
+    gate = gather_qmm(xr, ex.gate, slots, layer.dtype, acc, weights)
     h = swiglu(up, gate, layer.swiglu_limit, layer.swiglu_mode, layer.dtype)
-    y = gather_qmm(h, ex.down, slots, layer.dtype, acc)
+    y = gather_qmm(h, ex.down, slots, layer.dtype, acc, weights)
     return (up.reshape(T, k, -1), gate.reshape(T, k, -1), h.reshape(T, k, -1),
             y.reshape(T, k, -1))
 
 
 def moe_layer(x: np.ndarray, layer: LayerNP, idx: np.ndarray | None = None,
-              w: np.ndarray | None = None, acc=np.float64) -> dict:
+              w: np.ndarray | None = None, acc=np.float64, weights: str = "exact") -> dict:
     """One routed-MoE layer, ``ArenaMoE.__call__`` single-tier path
     (``arena.py:508-547`` with ``_apply`` ``:569-624``)."""
     x = np.asarray(x, np.float32)
@@ -346,7 +372,7 @@ def moe_layer(x: np.ndarray, layer: LayerNP, idx: np.ndarray | None = None,
                                         layer.scoring, layer.routed_scaling, layer.norm_topk)
         out["scores"], out["biased"] = scores, biased
         out["ties"] = near_ties(biased, layer.top_k)
-    up, gate, h, y = expert_ffn(x, idx, layer, acc)
+    up, gate, h, y = expert_ffn(x, idx, layer, acc, weights)
     out.update(idx=idx, w=w, up=up, gate=gate, h=h, y=y, out=combine(y, w, layer.dtype))
     return out
 

@@ -99,3 +99,33 @@ def test_product_path_fails_loudly_without_cuda(built):
                         torch.zeros((2, 64, 8), dtype=torch.bfloat16), 2, 64)
     with pytest.raises(RuntimeError, match="CUDA"):
         ops.gather_qmm(x, slots, q)
+
+
+def test_prefill_path_selection(built):
+    """Path choice and workspace sizing of lmoe_moe_layer_path (host logic)."""
+    lib = _lib.lmoe()
+    P = _lib.PATH
+    L = _layer()  # hidden 1024, inter 512, 2-bit g64, 16 experts: both paths available
+    ws = lambda layer, T, p: lib.lmoe_workspace_size_path(ctypes.byref(layer), T, P[p])  # noqa: E731
+    dec, pre, auto = ws(L, 4096, "decode"), ws(L, 4096, "prefill"), ws(L, 4096, "auto")
+    assert dec > 0 and pre > 0 and auto == max(dec, pre)
+    assert lib.lmoe_workspace_size(ctypes.byref(L), 4096) == auto
+    # below the AUTO threshold (tokens * top_k < 16 * n_experts) AUTO sizes the decode path
+    assert 8 * 6 < _lib.PREFILL_MIN_ROUTES_PER_EXPERT * 16
+    assert ws(L, 8, "auto") == ws(L, 8, "decode")
+    # inter not a multiple of 128: no prefill path, AUTO falls back to decode
+    odd = _layer(inter=320)
+    assert ws(odd, 64, "prefill") == 0
+    assert ws(odd, 4096, "auto") == ws(odd, 4096, "decode")
+    big = 1 << 40
+    rc = lib.lmoe_moe_layer_path(ctypes.byref(odd), 256, 4, 256, None, None, 256, big, None, P["prefill"], None, None)
+    assert rc == _lib.LMOE_EUNSUPPORTED
+    # unknown path value
+    assert lib.lmoe_moe_layer_path(ctypes.byref(L), 256, 4, 256, None, None, 256, big, None, 9, None, None) == \
+        _lib.LMOE_EUNSUPPORTED
+    # the prefill workspace is checked before any launch
+    small = ws(L, 512, "decode")
+    assert ws(L, 512, "prefill") > small
+    rc = lib.lmoe_moe_layer_path(ctypes.byref(L), 256, 512, 256, None, None, 256, small, None, P["prefill"], None,
+                                 None)
+    assert rc == _lib.LMOE_EWORKSPACE

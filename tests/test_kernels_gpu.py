@@ -117,7 +117,8 @@ def test_gateup_swiglu_matches_oracle(built, bits, gs, mode):
 def _check_layer(cfg, T, seed=0, device="cuda", acc=np.float64):
     layer = synth.make_layer(cfg, seed=seed, device=device)
     x = synth.make_tokens(cfg, T, seed=seed + 100, device=device)
-    kern = ops.MoEKernel(layer.router, layer.experts, layer.expert_slot, cfg.swiglu_limit, "fused")
+    # the decode GEMV kernels (the prefill path has its own tests)
+    kern = ops.MoEKernel(layer.router, layer.experts, layer.expert_slot, cfg.swiglu_limit, "fused", path="decode")
     idx = torch.empty((T, cfg.top_k), dtype=torch.int32, device=device)
     w = torch.empty((T, cfg.top_k), dtype=torch.float32, device=device)
     out = kern(x, idx=idx, w=w)
