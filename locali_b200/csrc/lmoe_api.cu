@@ -24,7 +24,7 @@ int32_t g_trace_units = 0;
 struct Layout {
     size_t status = 0, partial = 0, idx = 0, w = 0, sorted = 0, counts = 0, roff = 0,
            nchunks = 0, chunks = 0, xpanel = 0, xsum = 0, hpanel = 0, hsum = 0, yw = 0,
-           cnt = 0, total = 0;
+           cnt = 0, dblk = 0, total = 0;
     int max_chunks = 0;
     // prefill path: tiled activation panels of the tcgen05 grouped GEMM
     size_t pfx = 0, pfh = 0;
@@ -67,6 +67,7 @@ Layout make_layout(int T, int R, int K, int I, int H_out, int buckets, int E_rou
     L.nchunks = take(16);
     L.max_chunks = max_chunks_for(buckets, R);
     L.chunks = take((size_t)L.max_chunks * sizeof(Chunk));
+    L.dblk = take((size_t)((R + 255) / 256) * buckets * 4);
     L.xpanel = take((size_t)x_rows * K * 2);
     L.xsum = take((size_t)x_rows * (K / 16) * 8);
     L.hpanel = take((size_t)R * I * 2);
@@ -184,6 +185,7 @@ int run_dispatch(const Layout &L, void *ws, const int32_t *idx, int R, int n_exp
     dout.n_chunks = at<int32_t>(ws, L.nchunks);
     dout.counts = at<int32_t>(ws, L.counts);
     dout.route_off = at<int32_t>(ws, L.roff);
+    dout.blk = at<int32_t>(ws, L.dblk);
     int32_t *err = at<int32_t>(ws, L.status);
     if (R <= kDispatchSmallMaxRoutes && n_experts + 1 <= kDispatchSmallMaxBuckets)
         return cuda_rc(launch_dispatch_small(din, dout, err, st));
@@ -282,8 +284,9 @@ int run_experts_pf(const lmoe_layer *l, const Layout &L, void *ws, const void *x
     if (rc) return rc;
     PfArgs g;
     std::memset(&g, 0, sizeof(g));
-    g.q0 = view(ex.gate, ex.n_slots, I, H);
-    g.q1 = view(ex.up, ex.n_slots, I, H);
+    const QView qg = view(ex.gate, ex.n_slots, I, H), qu = view(ex.up, ex.n_slots, I, H);
+    rc = cuda_rc(pf_prepare(g, PF_GATEUP, qg, qu, ex.gate.bits, ex.gate.group_size, ex.n_slots));
+    if (rc) return rc;
     g.panel = pa.panel;
     g.prow = L.pf_rows;
     g.K = H;
@@ -301,8 +304,9 @@ int run_experts_pf(const lmoe_layer *l, const Layout &L, void *ws, const void *x
     if (rc) return rc;
     if (ev_gateup && cudaEventRecord(ev_gateup, st) != cudaSuccess) return LMOE_ECUDA;
     PfArgs d = g;
-    std::memset(&d.q1, 0, sizeof(d.q1));
-    d.q0 = view(ex.down, ex.n_slots, H, I);
+    const QView qd = view(ex.down, ex.n_slots, H, I);
+    rc = cuda_rc(pf_prepare(d, PF_DOWN, qd, qd, ex.down.bits, ex.down.group_size, ex.n_slots));
+    if (rc) return rc;
     d.panel = g.hpanel;
     d.K = I;
     d.rbn = H / 256;
@@ -447,12 +451,35 @@ static int route_impl(const lmoe_router &r, int H, int dtype, const lmoe_layer *
     a.dout.n_chunks = at<int32_t>(ws, L.nchunks);
     a.dout.counts = at<int32_t>(ws, L.counts);
     a.dout.route_off = at<int32_t>(ws, L.roff);
+    a.dout.blk = at<int32_t>(ws, L.dblk);
     const bool small_topk = T <= 64;
     const bool small_disp = l && R <= kDispatchSmallMaxRoutes && a.E + 1 <= kDispatchSmallMaxBuckets;
     a.finish = small_topk ? 1 : 0;
     a.do_dispatch = (small_topk && small_disp) ? 1 : 0;
-    int rc = cuda_rc(launch_router(a, ksplit, st));
-    if (rc) return rc;
+    int rc;
+    if (!small_topk && !a.act_f16) {
+        // many tokens: logits on the tensor cores; the decode GEMVs' panel
+        // (when this layout has one) from the panel kernel
+        rc = cuda_rc(launch_router_logits_mma(a, st));
+        if (rc) return rc;
+        if (a.xpanel) {
+            PanelArgs pa;
+            std::memset(&pa, 0, sizeof(pa));
+            pa.x = a.x;
+            pa.rows = T;
+            pa.K = H;
+            pa.panel = a.xpanel;
+            pa.sum16 = a.xsum16;
+            pa.bits = a.pbits;
+            pa.gs = a.pgs;
+            pa.act_f16 = 0;
+            rc = cuda_rc(launch_panel(pa, st));
+            if (rc) return rc;
+        }
+    } else {
+        rc = cuda_rc(launch_router(a, ksplit, st));
+        if (rc) return rc;
+    }
     if (!small_topk) {
         TopkArgs tk;
         tk.partial = a.partial;

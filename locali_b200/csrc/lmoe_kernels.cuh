@@ -2,6 +2,8 @@
 // lmoe_api.cu.
 #pragma once
 
+#include <cuda.h>
+
 #include "lmoe_common.cuh"
 
 namespace lmoe {
@@ -70,6 +72,7 @@ struct DispatchOut {
     int32_t *n_chunks;       // [1]
     int32_t *counts;         // [buckets] (large path)
     int32_t *route_off;      // [buckets] (large path)
+    int32_t *blk;            // [ceil(R / 256)][buckets] scratch of the large path, or nullptr
 };
 
 struct DispatchIn {
@@ -207,6 +210,9 @@ inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, siz
 // host-side launchers (lmoe_route.cu, lmoe_gemv.cu)
 cudaError_t launch_router(const RouterArgs &a, int ksplit, cudaStream_t st);
 cudaError_t launch_topk(const TopkArgs &a, cudaStream_t st);
+// logits (+ element-wise scores) of many bf16 tokens on the tensor cores; the
+// top-k then runs in launch_topk
+cudaError_t launch_router_logits_mma(const RouterArgs &a, cudaStream_t st);
 cudaError_t launch_dispatch_small(const DispatchIn &din, const DispatchOut &dout, int32_t *err,
                                   cudaStream_t st);
 cudaError_t launch_dispatch_large(const DispatchIn &din, const DispatchOut &dout, int32_t *err,
@@ -255,7 +261,14 @@ struct PfPanelArgs {
 };
 
 struct PfArgs {
-    QView q0, q1;           // gate, up (PF_GATEUP); down (PF_DOWN, q1 unused)
+    // 2-D TMA maps over the arena arrays of the item's two 128-row blocks
+    // (gate and up for PF_GATEUP; the down array twice for PF_DOWN): codes
+    // [n_slots * rows][row bytes] (uint8), scales and biases
+    // [n_slots * rows][groups] (16-bit)
+    CUtensorMap tm_code[2];
+    CUtensorMap tm_scale[2];
+    CUtensorMap tm_bias[2];
+    int32_t wrows;          // rows of the projection array (per slot)
     const uint8_t *panel;   // activation panel of this kernel
     int32_t prow;
     int32_t K;
@@ -276,6 +289,8 @@ struct PfArgs {
     int32_t *err;
 };
 
+// Fills a.tm_* for the projection(s) of `mode` (q1 = up for PF_GATEUP).
+cudaError_t pf_prepare(PfArgs &a, int mode, const QView &q0, const QView &q1, int bits, int gs, int n_slots);
 bool pf_supported(int K, int rows, int bits, int gs, int mode);
 cudaError_t launch_pf_panel(const PfPanelArgs &a, int max_chunks, cudaStream_t st);
 cudaError_t launch_pf_gemm(int mode, int act_f16, int bits, int gs, const PfArgs &a, cudaStream_t st);

@@ -7,12 +7,13 @@
 // pair of 128-row weight blocks: (gate rows, up rows) for the gate/up kernel,
 // two consecutive 128-row blocks of the down projection for the down kernel.
 // For each 64-column K stage:
-//   * 8 dequantisation warps turn the packed codes of one weight row each
-//     into operand A in shared memory, in the activation dtype (one rounding
-//     of scale * q + bias per weight: fma.rn on the packed pair), laid out in
-//     the 128-byte-swizzled K-major form the tensor core reads.  Their code,
-//     scale and bias bytes stream through a per-thread cp.async ring several
-//     stages ahead;
+//   * a weight-stream warp moves the packed codes of both 128-row blocks
+//     (2-D TMA tiles of 128 rows x one stage, into a ring of stages) and
+//     their scales and biases (8 groups at a time);
+//   * 8 dequantisation warps turn the codes of one weight row each into
+//     operand A in shared memory, in the activation dtype (one rounding of
+//     scale * q + bias per weight: fma.rn on the packed pair), laid out in
+//     the 128-byte-swizzled K-major form the tensor core reads;
 //   * a producer warp moves operand B (N routes x 64 columns) with one bulk
 //     copy (no multicast) from a panel kept in the same swizzled form;
 //   * one thread issues tcgen05.mma (M 128, N = routes rounded up to 16,
@@ -32,22 +33,30 @@
 // Every wait is bounded (mbar_wait); a wait that gives up latches LMOE_ECUDA,
 // raises the block's abort flag, and the block drains its tensor-core work
 // and frees its TMEM before returning.
+#include <cudaTypedefs.h>
+
 #include "lmoe_kernels.cuh"
 
 namespace lmoe {
 
 namespace {
 
-constexpr int kPfM = 128;       // weight rows per accumulator (MMA M)
-constexpr int kPfKS = 64;       // K columns per stage: one 128-byte swizzle row of 16-bit values
-constexpr int kPfStages = 3;
-constexpr int kPfDeqWarps = 8;  // 256 threads: one (accumulator, row) each
+constexpr int kPfM = 128;        // weight rows per accumulator (MMA M)
+constexpr int kPfKS = 128;       // K columns per stage: two 128-byte swizzle atoms of 16-bit values
+constexpr int kPfSS = 2;         // stages in flight: operand A in tensor memory, operand B in shared memory
+constexpr int kPfDeqWarps = 16;  // 512 threads: one (accumulator, row, K half) each
 constexpr int kPfEpiWarps = 4;
-constexpr int kPfThreads = (2 + kPfDeqWarps + kPfEpiWarps) * 32;
-constexpr int kPfATile = kPfM * kPfKS * 2;           // 16 KB
-constexpr int kPfBTile = kPfNmax * kPfKS * 2;        // 16 KB
-constexpr int kPfStageBytes = 2 * kPfATile + kPfBTile;
-constexpr int kPfTmemCols = 512;                     // 2 buffers x 2 accumulators x 128 columns
+constexpr int kPfDeq0 = 3;       // warps: 0 operand B, 1 MMA, 2 weights, 3..18 dequantisation, 19..22 epilogue
+constexpr int kPfThreads = (kPfDeq0 + kPfDeqWarps + kPfEpiWarps) * 32;
+constexpr int kPfBAtom = kPfNmax * 128;              // one 64-column atom of B: 16 KB
+constexpr int kPfBTile = 2 * kPfBAtom;               // B slot: 2 atoms, 32 KB
+constexpr int kPfOpBytes = kPfSS * kPfBTile;
+constexpr int kPfStgBytes = kPfM * 512;              // epilogue staging: 128 rows x 256 16-bit values
+// TMEM columns: accumulators [0, 256) (two of 128 columns); operand A stages
+// [256, 512): stage s, accumulator p, K half hf at 256 + 128 s + 64 p + 32 hf
+// (a row's 16-bit K values packed two per 32-bit column)
+constexpr int kPfTmemA = 256;
+constexpr int kPfTmemCols = 512;
 constexpr int kPfPanelAtoms = 8;                     // 64-column blocks per panel-builder block
 
 // ------------------------------------------------------------ tcgen05 primitives
@@ -77,6 +86,46 @@ __device__ __forceinline__ void umma_f16(uint32_t d, uint64_t adesc, uint64_t bd
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
+// same with operand A in tensor memory (M = 128 lanes, 8 columns per K step of 16)
+__device__ __forceinline__ void umma_f16_ts(uint32_t d, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Four K steps for two accumulators (A from TMEM): d0 += A0[k] B[k], d1 +=
+// A1[k] B[k] for k = 0..3, in one asm block so nothing is scheduled between
+// the MMAs (an MMA blocks its issuing thread while it runs).  `acc` = 0
+// overwrites the accumulators at the first K step.
+__device__ __forceinline__ void umma4x2_ts(uint32_t d0, uint32_t d1, uint32_t a0, uint32_t a1, uint64_t b0,
+                                          uint64_t b1, uint64_t b2, uint64_t b3, uint32_t idesc, uint32_t acc) {
+    // operands: %0 a0, %1 a1 (advanced by 8 columns per K step), %2 d0, %3 d1,
+    // %4..%7 B descriptors, %8 instruction descriptor, %9 accumulate flag
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.b32 p, %9, 0;\n\t"
+        "setp.eq.b32 q, %9, %9;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%2], [%0], %4, %8, p;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%3], [%1], %4, %8, p;\n\t"
+        "add.u32 %0, %0, 8;\n\t"
+        "add.u32 %1, %1, 8;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%2], [%0], %5, %8, q;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%3], [%1], %5, %8, q;\n\t"
+        "add.u32 %0, %0, 8;\n\t"
+        "add.u32 %1, %1, 8;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%2], [%0], %6, %8, q;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%3], [%1], %6, %8, q;\n\t"
+        "add.u32 %0, %0, 8;\n\t"
+        "add.u32 %1, %1, 8;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%2], [%0], %7, %8, q;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%3], [%1], %7, %8, q;\n\t"
+        "}\n"
+        : "+r"(a0), "+r"(a1)
+        : "r"(d0), "r"(d1), "l"(b0), "l"(b1), "l"(b2), "l"(b3), "r"(idesc), "r"(acc)
+        : "memory");
+}
 // arrive once on `bar` when every MMA issued so far by this thread has completed
 __device__ __forceinline__ void umma_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -102,6 +151,16 @@ __device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[16]) {
                  :
                  : "memory");
 }
+// 32 lanes x 16 consecutive 32-bit columns, from registers (lane = row)
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row atoms of
 // 1024 bytes (stride byte offset 1024), Blackwell descriptor version 1.
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
@@ -115,26 +174,52 @@ __device__ __forceinline__ uint32_t idesc_f16(int n, bool f16) {
     return (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kPfM >> 4) << 24);
 }
 
-__device__ __forceinline__ void cp16(uint32_t dst, const void *src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+// Non-blocking test of an mbarrier phase (try_wait may suspend the thread for
+// hundreds of cycles when the phase is not complete yet).
+__device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2; "
+        "selp.u32 %0, 1, 0, p; }"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
 }
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_wait() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+
+// Pipeline wait of the prefill roles: mbarrier.try_wait suspends the thread
+// in hardware until the phase completes (or a short time limit passes), so a
+// plain loop keeps hand-off latency low; bounded like mbar_wait.
+__device__ __forceinline__ bool pf_wait(uint64_t *bar, uint32_t parity) {
+    if (mbar_try(bar, parity)) return true;
+    const long long t0 = clock64();
+    for (;;) {
+        if (mbar_try(bar, parity)) return true;
+        if (clock64() - t0 > kWaitLimitCycles) return false;
+    }
+}
+
+// 2-D tiled TMA load (no multicast): box at (x, y) of `map` -> shared memory,
+// completion counted in bytes on `bar`
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
 }
 __device__ __forceinline__ uint4 lds128(uint32_t a) {
     uint4 v;
     asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
     return v;
 }
-__device__ __forceinline__ uint32_t lds16(uint32_t a) {
-    uint16_t v;
-    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
-    return v;
-}
-__device__ __forceinline__ void sts128(uint32_t a, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
+__device__ __forceinline__ void sts128v(uint32_t a, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
     asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(x), "r"(y), "r"(z), "r"(w) : "memory");
+}
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+    return v;
 }
 
 // ------------------------------------------------------------ packed 16-bit pair math
@@ -202,24 +287,23 @@ struct PfCodes {
     }
 };
 
-// Per-thread cp.async ring of the dequantisation threads: the code bytes of
-// RS stages and two 8-group blocks of scales and biases.  The ring stride is
-// an odd number of 16-byte chunks so the 16-byte accesses of consecutive
-// threads hit distinct bank groups.
+// Weight stream of one block: the producer warp moves the codes of both
+// 128-row blocks, stage by stage, into a ring of CR stages, and their scales
+// and biases, 8 groups at a time, into a ring of 2 blocks (2-D TMA copies,
+// never multicast).  The dequantisation threads read their row from there.
+constexpr int kPfScaleSlotBytes = 2 * 2 * kPfM * 16;  // [block][scale|bias][row][8 groups]
 template <int BITS, int GS>
 struct PfRing {
-    static constexpr int CB = 8 * BITS;   // code bytes of one row per stage
-    static constexpr int SPB = GS / 8;    // stages per block of 8 groups
-    static constexpr int RS0 = 128 / CB;
-    static constexpr int RS = RS0 < SPB ? RS0 : SPB;  // stages in flight (lookahead RS - 1 < SPB)
-    static constexpr int RAW = RS * CB + 64;
-    static constexpr int BYTES = ((RAW / 16) | 1) * 16;
-    static_assert(RS >= 2, "ring");
+    static constexpr int CB = 16 * BITS;  // code bytes of one row per stage
+    static constexpr int SPB = GS / 16;   // stages per block of 8 groups
+    static constexpr int RING = BITS == 2 ? 32 * 1024 : (BITS == 4 ? 48 * 1024 : 64 * 1024);
+    static constexpr int CR = RING / (2 * kPfM * CB);
+    static_assert(CR >= 2 && SPB >= 2, "rings");
 };
 
 template <int BITS, int GS>
 constexpr int pf_smem_bytes() {
-    return 1024 + kPfStages * kPfStageBytes + 256 * PfRing<BITS, GS>::BYTES + 256;
+    return 1024 + kPfOpBytes + kPfStgBytes + PfRing<BITS, GS>::RING + 2 * kPfScaleSlotBytes + 512;
 }
 
 // Panel position of column f for a projection quantised with `bits`.
@@ -328,40 +412,54 @@ __global__ void __launch_bounds__(256) pf_combine_kernel(const uint16_t *yw, int
 
 // ------------------------------------------------------------ the grouped GEMM
 template <typename TA, int BITS, int GS, int MODE>
-__global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const PfArgs a) {
+__global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_constant__ PfArgs a) {
     using RG = PfRing<BITS, GS>;
     using C = PfCodes<TA, BITS>;
     using P = Pf2<TA>;
-    constexpr int NW = RG::CB / 4;           // code words of one row per stage
+    constexpr int HW = RG::CB / 8;           // code words of half a row per stage (64 weights)
     constexpr int CPW = 32 / BITS;           // codes per word
-    constexpr int NPAIR = NW * C::kPairs;    // 32 packed pairs = 64 weights
-    static_assert(NPAIR == 32, "a stage row is 64 weights");
+    static_assert(HW * C::kPairs == 32, "half a stage row is 64 weights");
     constexpr bool kF16 = std::is_same<TA, __half>::value;
+    constexpr int CSTAGE = 2 * kPfM * RG::CB;  // code bytes of one ring stage
 
     extern __shared__ __align__(1024) uint8_t pf_raw[];
     uint8_t *smem = pf_raw + ((1024u - (smem_u32(pf_raw) & 1023u)) & 1023u);
     const uint32_t sbase = smem_u32(smem);
-    uint8_t *ring = smem + kPfStages * kPfStageBytes;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(ring + 256 * RG::BYTES);
+    const uint32_t stg = sbase + kPfOpBytes;
+    const uint32_t cring = stg + kPfStgBytes;
+    const uint32_t sring = cring + RG::RING;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kPfOpBytes + kPfStgBytes + RG::RING + 2 * kPfScaleSlotBytes);
+    // stage s: operand A written (dequantisation warps), operand B landed
+    // (bulk copies), stage free again (one tcgen05.commit after its MMAs)
     uint64_t *full_a = bars;
-    uint64_t *full_b = bars + kPfStages;
-    uint64_t *empty = bars + 2 * kPfStages;
-    uint64_t *acc_full = bars + 3 * kPfStages;
-    uint64_t *acc_empty = acc_full + 2;
-    uint64_t *drain = acc_empty + 2;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+    uint64_t *full_b = full_a + kPfSS;
+    uint64_t *empty = full_b + kPfSS;
+    uint64_t *acc_full = empty + kPfSS;
+    uint64_t *acc_empty = acc_full + 1;
+    uint64_t *drain = acc_empty + 1;
+    uint64_t *code_full = drain + 1;
+    uint64_t *code_empty = code_full + RG::CR;
+    uint64_t *sc_full = code_empty + RG::CR;
+    uint64_t *sc_empty = sc_full + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sc_empty + 2);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kPfStages; ++s) {
+        for (int s = 0; s < kPfSS; ++s) {
             mbar_init(&full_a[s], kPfDeqWarps);
             mbar_init(&full_b[s], 1);
             mbar_init(&empty[s], 1);
         }
+        mbar_init(acc_full, 1);
+        mbar_init(acc_empty, kPfEpiWarps);
         for (int b = 0; b < 2; ++b) {
-            mbar_init(&acc_full[b], 1);
-            mbar_init(&acc_empty[b], kPfEpiWarps);
+            mbar_init(&sc_full[b], 1);
+            mbar_init(&sc_empty[b], kPfDeqWarps);
+        }
+        for (int c = 0; c < RG::CR; ++c) {
+            mbar_init(&code_full[c], 1);
+            mbar_init(&code_empty[c], kPfDeqWarps);
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -384,8 +482,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const PfArgs a) 
     if (warp == 0) {
         // ---------------------------------------------------- operand B producer
         if (lane == 0) {
-            const size_t kstride = (size_t)(a.prow >> 3) * 1024u;
-            int g = 0;
+            const size_t kstride = (size_t)(a.prow >> 3) * 1024u;  // one 64-column atom of the panel
+            int sb = 0;
+            uint32_t ph = 0;
             bool ok = true;
             for (int item = blockIdx.x; item < items && ok; item += gridDim.x) {
                 if (*abort_flag) break;
@@ -393,15 +492,19 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const PfArgs a) 
                 const Chunk ch = a.chunks[c];
                 const uint32_t bytes = (uint32_t)((ch.ntok + 15) & ~15) * 128u;
                 const uint8_t *src = a.panel + (size_t)(pf_row_base(ch.route_start, c) >> 3) * 1024u;
-                for (int ks = 0; ks < KS; ++ks, ++g) {
-                    const int s = g % kPfStages;
-                    if (!mbar_wait(&empty[s], ((g / kPfStages) & 1) ^ 1)) {
+                for (int ks = 0; ks < KS; ++ks) {
+                    if (!pf_wait(&empty[sb], ph ^ 1u)) {
                         ok = false;
                         break;
                     }
-                    mbar_expect_tx(&full_b[s], bytes);
-                    bulk_g2s(smem + s * kPfStageBytes + 2 * kPfATile, src + (size_t)ks * kstride, bytes,
-                             &full_b[s]);
+                    mbar_expect_tx(&full_b[sb], 2u * bytes);
+                    uint8_t *dst = smem + sb * kPfBTile;
+                    bulk_g2s(dst, src + (size_t)(2 * ks) * kstride, bytes, &full_b[sb]);
+                    bulk_g2s(dst + kPfBAtom, src + (size_t)(2 * ks + 1) * kstride, bytes, &full_b[sb]);
+                    if (++sb == kPfSS) {
+                        sb = 0;
+                        ph ^= 1u;
+                    }
                 }
             }
             if (!ok) {
@@ -411,42 +514,49 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const PfArgs a) 
         }
     } else if (warp == 1) {
         // ---------------------------------------------------- MMA issuer
+        // An MMA blocks its issuing thread for its whole duration (52 cycles
+        // below N = 104, N / 2 above), a tcgen05.commit for about 256 and an
+        // mbarrier.try_wait on an incomplete phase for several hundred
+        // (measured on B200).  So one commit per stage, and the next stage's
+        // barriers are polled between this stage's MMAs with the non-blocking
+        // test_wait.
         if (lane == 0) {
-            int g = 0, it = 0;
+            int it = 0, s = 0;
+            uint32_t ph = 0;
             bool ok = true;
+            const uint64_t db_base = sw128_desc(sbase);
             for (int item = blockIdx.x; item < items && ok; item += gridDim.x, ++it) {
                 if (*abort_flag) break;
                 const Chunk ch = a.chunks[item / a.rbn];
                 const uint32_t idesc = idesc_f16((ch.ntok + 15) & ~15, kF16);
-                const int b = it & 1;
-                if (!mbar_wait(&acc_empty[b], ((it >> 1) & 1) ^ 1)) {
+                // the accumulators are free once the epilogue has copied out the previous item
+                if (!pf_wait(acc_empty, (it & 1) ^ 1u)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t d0 = tmem + (uint32_t)(b * 256), d1 = d0 + 128u;
-                for (int ks = 0; ks < KS; ++ks, ++g) {
-                    const int s = g % kPfStages;
-                    const uint32_t ph = (g / kPfStages) & 1;
-                    if (!mbar_wait(&full_b[s], ph) || !mbar_wait(&full_a[s], ph)) {
+                bool ready = false;  // this stage's operands known to be in place
+                for (int ks = 0; ks < KS; ++ks) {
+                    if (!ready && (!pf_wait(&full_b[s], ph) || !pf_wait(&full_a[s], ph))) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t st = sbase + (uint32_t)(s * kPfStageBytes);
-                    const uint64_t da0 = sw128_desc(st), da1 = sw128_desc(st + kPfATile);
-                    const uint64_t db = sw128_desc(st + 2 * kPfATile);
-#pragma unroll
-                    for (int kk = 0; kk < kPfKS / 16; ++kk) {
-                        // K step of 16 = 32 bytes along the swizzled row
-                        const uint32_t acc = (ks | kk) ? 1u : 0u;
-                        umma_f16(d0, da0 + 2u * kk, db + 2u * kk, idesc, acc);
-                        umma_f16(d1, da1 + 2u * kk, db + 2u * kk, idesc, acc);
-                    }
+                    const uint32_t a0 = tmem + (uint32_t)(kPfTmemA + s * 128), a1 = a0 + 64u;
+                    const uint64_t db = db_base + (uint64_t)(s * (kPfBTile >> 4));
+                    // B: 32 bytes per K step along the swizzled row; K 64..127 in the second atom
+                    const uint64_t dbh = db + (uint64_t)(kPfBAtom >> 4);
+                    umma4x2_ts(tmem, tmem + 128u, a0, a1, db, db + 2u, db + 4u, db + 6u, idesc, ks ? 1u : 0u);
+                    umma4x2_ts(tmem, tmem + 128u, a0 + 32u, a1 + 32u, dbh, dbh + 2u, dbh + 4u, dbh + 6u, idesc, 1u);
+                    const int ns = s + 1 == kPfSS ? 0 : s + 1;
+                    const uint32_t nph = ns == 0 ? ph ^ 1u : ph;
+                    ready = ks + 1 < KS && mbar_test(&full_b[ns], nph) && mbar_test(&full_a[ns], nph);
                     umma_commit(&empty[s]);
+                    s = ns;
+                    ph = nph;
                 }
                 if (!ok) break;
-                umma_commit(&acc_full[b]);
+                umma_commit(acc_full);
             }
             if (!ok) {
                 *abort_flag = 1;
@@ -456,72 +566,112 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const PfArgs a) 
             umma_commit(drain);
             if (!mbar_wait(drain, 0)) set_error(a.err, -4);
         }
-    } else if (warp < 2 + kPfDeqWarps) {
-        // ---------------------------------------------------- dequantisation (operand A)
-        const int td = threadIdx.x - 64;
-        const int p = td >> 7, r = td & (kPfM - 1);
-        const QView &q = (MODE == PF_GATEUP && p == 1) ? a.q1 : a.q0;
-        const uint32_t ring_t = smem_u32(ring) + (uint32_t)(td * RG::BYTES);
-        const uint32_t sring_t = ring_t + RG::RS * RG::CB;  // 2 x (16 B scales, 16 B biases)
-        const uint32_t arow = sbase + (uint32_t)(p * kPfATile + (r >> 3) * 1024 + (r & 7) * 128);
-        const int r7 = r & 7;
-        // issue cursor: the cp.async stream runs RS - 1 stages ahead, across items
-        int iss_item = blockIdx.x, iss_ks = 0, iss_nb = 0;
-        const uint8_t *iss_codes = nullptr;
-        const uint16_t *iss_s = nullptr, *iss_b = nullptr;
-        auto locate = [&](int item) {
-            const int c = item / a.rbn, rb = item - c * a.rbn;
-            const long slot = a.chunks[c].slot;
-            const long row = MODE == PF_GATEUP ? (long)rb * kPfM + r : (long)rb * 2 * kPfM + p * kPfM + r;
-            iss_codes = reinterpret_cast<const uint8_t *>(q.w + slot * q.w_slot_stride + row * q.words_per_row);
-            iss_s = q.s + slot * q.sb_slot_stride + row * q.groups_per_row;
-            iss_b = q.b + slot * q.sb_slot_stride + row * q.groups_per_row;
-        };
-        auto issue = [&](int n) {
-            if (iss_item < items) {
-                const uint32_t dst = ring_t + (uint32_t)((n % RG::RS) * RG::CB);
+    } else if (warp == 2) {
+        // ---------------------------------------------------- weight stream producer
+        if (lane == 0) {
+            int g = 0, nb = 0;
+            bool ok = true;
+            for (int item = blockIdx.x; item < items && ok; item += gridDim.x) {
+                if (*abort_flag) break;
+                const int c = item / a.rbn, rb = item - c * a.rbn;
+                const int y0 = a.chunks[c].slot * a.wrows;
+                const int y[2] = {MODE == PF_GATEUP ? y0 + rb * kPfM : y0 + rb * 2 * kPfM,
+                                  MODE == PF_GATEUP ? y0 + rb * kPfM : y0 + rb * 2 * kPfM + kPfM};
+                for (int ks = 0; ks < KS; ++ks, ++g) {
+                    if (ks % RG::SPB == 0) {
+                        const int j = nb & 1;
+                        if (!pf_wait(&sc_empty[j], ((nb >> 1) & 1) ^ 1)) {
+                            ok = false;
+                            break;
+                        }
+                        mbar_expect_tx(&sc_full[j], kPfScaleSlotBytes);
+                        const uint32_t sd = sring + (uint32_t)(j * kPfScaleSlotBytes);
 #pragma unroll
-                for (int i = 0; i < RG::CB / 16; ++i) cp16(dst + 16 * i, iss_codes + iss_ks * RG::CB + 16 * i);
-                if (iss_ks % RG::SPB == 0) {
-                    const int blk = iss_ks / RG::SPB;
-                    const uint32_t sd = sring_t + (uint32_t)((iss_nb & 1) * 32);
-                    cp16(sd, iss_s + blk * 8);
-                    cp16(sd + 16, iss_b + blk * 8);
-                    ++iss_nb;
-                }
-                if (++iss_ks == KS) {
-                    iss_ks = 0;
-                    iss_item += gridDim.x;
-                    if (iss_item < items) locate(iss_item);
+                        for (int p = 0; p < 2; ++p) {
+                            tma_load_2d(sd + p * 4096, &a.tm_scale[p], (ks / RG::SPB) * 8, y[p], &sc_full[j]);
+                            tma_load_2d(sd + p * 4096 + 2048, &a.tm_bias[p], (ks / RG::SPB) * 8, y[p], &sc_full[j]);
+                        }
+                        ++nb;
+                    }
+                    const int cs = g % RG::CR;
+                    if (!pf_wait(&code_empty[cs], ((g / RG::CR) & 1) ^ 1)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(&code_full[cs], CSTAGE);
+#pragma unroll
+                    for (int p = 0; p < 2; ++p)
+                        tma_load_2d(cring + (uint32_t)(cs * CSTAGE + p * kPfM * RG::CB), &a.tm_code[p], ks * RG::CB,
+                                    y[p], &code_full[cs]);
                 }
             }
-            cp_commit();
-        };
-        if (iss_item < items) locate(iss_item);
-        for (int n = 0; n < RG::RS - 1; ++n) issue(n);
+            if (!ok) {
+                *abort_flag = 1;
+                set_error(a.err, -4);
+            }
+        }
+    } else if (warp < kPfDeq0 + kPfDeqWarps) {
+        // ---------------------------------------------------- dequantisation (operand A)
+        // thread = (accumulator p, K half hf, row r): 64 weights of one row
+        // per stage.  A warp reaches only its quarter of the TMEM lanes
+        // (warp % 4): rows 32 * (warp % 4) + lane; the 16 warps cover
+        // (p, hf) x 4 quarters.
+        const int wi = (warp - kPfDeq0) >> 2;
+        const int p = wi >> 1, hf = wi & 1, r = (warp & 3) * 32 + lane;
+        const uint32_t arow = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(kPfTmemA + p * 64 + hf * 32);
+        const uint32_t crow = cring + (uint32_t)(p * kPfM * RG::CB + r * RG::CB + hf * (RG::CB / 2));
+        const uint32_t srow = sring + (uint32_t)(p * 4096 + r * 16);
         int g = 0, nb = 0;
+        uint4 sreg = make_uint4(0u, 0u, 0u, 0u), breg = make_uint4(0u, 0u, 0u, 0u);
         bool ok = true;
         for (int item = blockIdx.x; item < items && ok; item += gridDim.x) {
             if (*abort_flag) break;
             for (int ks = 0; ks < KS; ++ks, ++g) {
-                issue(g + RG::RS - 1);
-                cp_wait<RG::RS - 1>();
-                const int s = g % kPfStages;
-                if (!mbar_wait(&empty[s], ((g / kPfStages) & 1) ^ 1)) {
+                if (ks % RG::SPB == 0) {
+                    // scales and biases of this row for the next 8 groups
+                    const int j = nb & 1;
+                    if (!pf_wait(&sc_full[j], (nb >> 1) & 1)) {
+                        ok = false;
+                        break;
+                    }
+                    sreg = lds128(srow + (uint32_t)(j * kPfScaleSlotBytes));
+                    breg = lds128(srow + (uint32_t)(j * kPfScaleSlotBytes + 2048));
+                    ++nb;
+                }
+                const int cs = g % RG::CR;
+                if (!pf_wait(&code_full[cs], (g / RG::CR) & 1)) {
                     ok = false;
                     break;
                 }
-                if (ks % RG::SPB == 0) ++nb;
-                const uint32_t sslot = sring_t + (uint32_t)(((nb - 1) & 1) * 32);
-                const int gi = ((ks % RG::SPB) * kPfKS) / GS;  // first group of this stage in the block
-                // scale variants per group of this stage (GS = 32: two groups)
-                uint32_t sp[2][3], b2[2];
+                uint32_t words[HW];
 #pragma unroll
-                for (int gg = 0; gg < (GS < kPfKS ? 2 : 1); ++gg) {
-                    const uint32_t s16 = lds16(sslot + 2 * (gi + gg));
-                    const uint32_t bb16 = lds16(sslot + 16 + 2 * (gi + gg));
-                    sp[gg][0] = s16 | (s16 << 16);
+                for (int i = 0; i < HW / 4; ++i) {
+                    const uint4 v = lds128(crow + (uint32_t)(cs * CSTAGE + 16 * i));
+                    words[4 * i] = v.x;
+                    words[4 * i + 1] = v.y;
+                    words[4 * i + 2] = v.z;
+                    words[4 * i + 3] = v.w;
+                }
+                const int s = g % kPfSS;
+                if (!pf_wait(&empty[s], ((g / kPfSS) & 1) ^ 1)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                // scale and bias variants of the groups this half row covers
+                // (64 columns: one group, two for GS = 32, half of one for 128)
+                constexpr int NG = GS < 64 ? 2 : 1;
+                const int gi = ((ks % RG::SPB) * kPfKS + hf * (kPfKS / 2)) / GS;
+                uint32_t sp[NG][3], b2[NG];
+#pragma unroll
+                for (int gg = 0; gg < NG; ++gg) {
+                    const int q = gi + gg;
+                    const uint32_t sw = (q & 4) ? ((q & 2) ? sreg.w : sreg.z) : ((q & 2) ? sreg.y : sreg.x);
+                    const uint32_t bw = (q & 4) ? ((q & 2) ? breg.w : breg.z) : ((q & 2) ? breg.y : breg.x);
+                    const int sh = (q & 1) * 16;
+                    const uint32_t s16 = (sw >> sh) & 0xFFFFu, bb16 = (bw >> sh) & 0xFFFFu;
                     b2[gg] = bb16 | (bb16 << 16);
+                    sp[gg][0] = s16 | (s16 << 16);
                     if constexpr (C::kPrescale) {
                         sp[gg][1] = P::fma2(sp[gg][0], P::kQuarter, P::kNegZero);
                         sp[gg][2] = P::fma2(sp[gg][0], P::kSixteenth, P::kNegZero);
@@ -529,44 +679,49 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const PfArgs a) 
                         sp[gg][1] = sp[gg][2] = sp[gg][0];
                     }
                 }
-                uint32_t words[NW];
-                const uint32_t csrc = ring_t + (uint32_t)((g % RG::RS) * RG::CB);
+                uint32_t pr[32];
 #pragma unroll
-                for (int i = 0; i < NW / 4; ++i) {
-                    const uint4 v = lds128(csrc + 16 * i);
-                    words[4 * i] = v.x;
-                    words[4 * i + 1] = v.y;
-                    words[4 * i + 2] = v.z;
-                    words[4 * i + 3] = v.w;
-                }
-                uint32_t pr[NPAIR];
-#pragma unroll
-                for (int u = 0; u < NW; ++u) {
-                    const int gg = (GS < kPfKS) ? (u * CPW) / GS : 0;
+                for (int u = 0; u < HW; ++u) {
+                    const int gg = NG == 2 ? (u * CPW) / GS : 0;
                     const typename C::W w = C::prep(words[u]);
 #pragma unroll
                     for (int m = 0; m < C::kPairs; ++m)
                         pr[u * C::kPairs + m] = P::fma2(C::q(w, m), sp[gg][C::pexp(m)], b2[gg]);
                 }
-                const uint32_t adst = arow + (uint32_t)(s * kPfStageBytes);
-#pragma unroll
-                for (int j = 0; j < 8; ++j)
-                    sts128(adst + (uint32_t)((j ^ r7) << 4), pr[4 * j], pr[4 * j + 1], pr[4 * j + 2], pr[4 * j + 3]);
-                // generic-proxy writes -> visible to the tensor core (async proxy)
+                const uint32_t adst = arow + (uint32_t)(s * 128);
+                tmem_st16(adst, *reinterpret_cast<const uint32_t(*)[16]>(&pr[0]));
+                tmem_st16(adst + 16u, *reinterpret_cast<const uint32_t(*)[16]>(&pr[16]));
+                tmem_wait_st();
+                // the generic-proxy reads of the code and scale slots must be
+                // ordered before their TMA refills (without this fence a refill
+                // could land before those reads, measured on B200)
                 fence_proxy_async();
+                tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&full_a[s]);
+                if (lane == 0) {
+                    mbar_arrive(&full_a[s]);
+                    mbar_arrive(&code_empty[cs]);
+                    if (ks % RG::SPB == 0) mbar_arrive(&sc_empty[(nb - 1) & 1]);
+                }
             }
         }
         if (!ok) {
             *abort_flag = 1;
             set_error(a.err, -4);
         }
-        cp_wait<0>();
     } else {
         // ---------------------------------------------------- epilogue
-        const int q4 = warp & 3;  // TMEM lanes 32*q4 .. 32*q4+31 (a warp reaches its own quarter)
+        // Copies the item's accumulators out of TMEM into shared memory,
+        // rounded to the activation dtype (the first operation of both
+        // epilogues), frees TMEM for the next item, then finishes the item
+        // from shared memory while the next item's MMAs run.  Thread = row r
+        // (TMEM lane; a warp reaches its own quarter): staging row r holds
+        // 32 chunks of 8 values (accumulator 0 in chunks 0-15, 1 in 16-31),
+        // chunk c at position c ^ (r & 31).
+        const int q4 = warp & 3;
         const int r = q4 * 32 + lane;
+        const uint32_t srow_e = stg + (uint32_t)(r * 512);
+        const int rx = r & 31;
         int it = 0;
         bool ok = true;
         for (int item = blockIdx.x; item < items; item += gridDim.x, ++it) {
@@ -574,29 +729,55 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const PfArgs a) 
             const int c = item / a.rbn, rb = item - c * a.rbn;
             const Chunk ch = a.chunks[c];
             const int N = (ch.ntok + 15) & ~15;
-            const int b = it & 1;
-            if (!mbar_wait(&acc_full[b], (it >> 1) & 1)) {
+            if (!pf_wait(acc_full, it & 1)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            const uint32_t t0 = tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(b * 256);
+            const uint32_t t0 = tmem + ((uint32_t)(q4 * 32) << 16);
+            for (int j0 = 0; j0 < N; j0 += 16) {
+                uint32_t v0[16], v1[16];
+                tmem_ld16(t0 + (uint32_t)j0, v0);
+                tmem_ld16(t0 + 128u + (uint32_t)j0, v1);
+                tmem_wait_ld(v0);
+                tmem_wait_ld(v1);
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int cc = (j0 >> 3) + h;
+                    const uint32_t *u0 = v0 + 8 * h, *u1 = v1 + 8 * h;
+                    sts128v(srow_e + (uint32_t)(((cc) ^ rx) << 4),
+                            Act<TA>::pack2(__uint_as_float(u0[0]), __uint_as_float(u0[1])),
+                            Act<TA>::pack2(__uint_as_float(u0[2]), __uint_as_float(u0[3])),
+                            Act<TA>::pack2(__uint_as_float(u0[4]), __uint_as_float(u0[5])),
+                            Act<TA>::pack2(__uint_as_float(u0[6]), __uint_as_float(u0[7])));
+                    sts128v(srow_e + (uint32_t)(((16 + cc) ^ rx) << 4),
+                            Act<TA>::pack2(__uint_as_float(u1[0]), __uint_as_float(u1[1])),
+                            Act<TA>::pack2(__uint_as_float(u1[2]), __uint_as_float(u1[3])),
+                            Act<TA>::pack2(__uint_as_float(u1[4]), __uint_as_float(u1[5])),
+                            Act<TA>::pack2(__uint_as_float(u1[6]), __uint_as_float(u1[7])));
+                }
+            }
+            // TMEM is free for the next item's MMAs
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty);
             if constexpr (MODE == PF_GATEUP) {
                 const int f = rb * kPfM + r;
                 const int kp = pf_perm_pos(f, a.hbits);
                 const int pbase = pf_row_base(ch.route_start, c);
-                for (int j0 = 0; j0 < N; j0 += 16) {
-                    uint32_t gv[16], uv[16];
-                    tmem_ld16(t0 + (uint32_t)j0, gv);
-                    tmem_ld16(t0 + 128u + (uint32_t)j0, uv);
-                    tmem_wait_ld(gv);
-                    tmem_wait_ld(uv);
+                for (int j0 = 0; j0 < N; j0 += 8) {
+                    const uint4 gq = lds128(srow_e + (uint32_t)(((j0 >> 3) ^ rx) << 4));
+                    const uint4 uq = lds128(srow_e + (uint32_t)(((16 + (j0 >> 3)) ^ rx) << 4));
+                    const uint32_t gw[4] = {gq.x, gq.y, gq.z, gq.w}, uw[4] = {uq.x, uq.y, uq.z, uq.w};
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) {
+                    for (int i = 0; i < 8; ++i) {
                         const int j = j0 + i;
                         float h = 0.0f;
-                        if (j < ch.ntok)
-                            h = swiglu_h<TA>(__uint_as_float(gv[i]), __uint_as_float(uv[i]), a.limit, a.swiglu_mode);
+                        if (j < ch.ntok) {
+                            const float gv = Act<TA>::to_f((uint16_t)(i & 1 ? gw[i >> 1] >> 16 : gw[i >> 1] & 0xFFFFu));
+                            const float uv = Act<TA>::to_f((uint16_t)(i & 1 ? uw[i >> 1] >> 16 : uw[i >> 1] & 0xFFFFu));
+                            h = swiglu_h<TA>(gv, uv, a.limit, a.swiglu_mode);
+                        }
                         *reinterpret_cast<uint16_t *>(a.hpanel + pf_panel_off(pbase + j, kp, a.hprow)) =
                             Act<TA>::from_f(h);
                     }
@@ -605,33 +786,29 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const PfArgs a) 
 #pragma unroll 1
                 for (int pp = 0; pp < 2; ++pp) {
                     const int f = rb * 2 * kPfM + pp * kPfM + r;
-                    for (int j0 = 0; j0 < N; j0 += 16) {
-                        uint32_t yv[16];
-                        tmem_ld16(t0 + (uint32_t)(pp * 128 + j0), yv);
-                        // route and combine weight of column j0 + (lane & 15)
-                        const int jl = j0 + (lane & 15);
+                    for (int j0 = 0; j0 < N; j0 += 8) {
+                        // route and combine weight of column j0 + (lane & 7)
+                        const int jl = j0 + (lane & 7);
                         int my_route = 0;
                         float my_w = 0.0f;
                         if (jl < ch.ntok) {
                             my_route = a.sorted_routes[ch.route_start + jl];
                             my_w = a.route_w[my_route];
                         }
-                        tmem_wait_ld(yv);
+                        const uint4 yq = lds128(srow_e + (uint32_t)(((pp * 16 + (j0 >> 3)) ^ rx) << 4));
+                        const uint32_t yw4[4] = {yq.x, yq.y, yq.z, yq.w};
 #pragma unroll
-                        for (int i = 0; i < 16; ++i) {
+                        for (int i = 0; i < 8; ++i) {
                             const int route = __shfl_sync(0xffffffffu, my_route, i);
                             const float wv = __shfl_sync(0xffffffffu, my_w, i);
                             if (j0 + i < ch.ntok) {
-                                const float y = Act<TA>::round(__uint_as_float(yv[i]));
+                                const float y = Act<TA>::to_f((uint16_t)(i & 1 ? yw4[i >> 1] >> 16 : yw4[i >> 1] & 0xFFFFu));
                                 a.yw[(size_t)route * a.H + f] = Act<TA>::from_f(y * Act<TA>::round(wv));
                             }
                         }
                     }
                 }
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&acc_empty[b]);
         }
         if (!ok) {
             *abort_flag = 1;
@@ -687,13 +864,56 @@ cudaError_t launch_pf_bits(int bits, int gs, const PfArgs &a, cudaStream_t st) {
 
 }  // namespace
 
+namespace {
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+cudaError_t map2d(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint64_t dim0, uint64_t dim1,
+                  uint64_t stride1, uint32_t box0, uint32_t box1) {
+    if (!g_encode) {
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+        if (e != cudaSuccess) return e;
+        if (q != cudaDriverEntryPointSuccess || !fn) return cudaErrorNotSupported;
+        g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    const cuuint64_t dims[2] = {dim0, dim1};
+    const cuuint64_t strides[1] = {stride1};
+    const cuuint32_t box[2] = {box0, box1};
+    const cuuint32_t es[2] = {1, 1};
+    const CUresult r = g_encode(m, dt, 2, const_cast<void *>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+}  // namespace
+
+cudaError_t pf_prepare(PfArgs &a, int mode, const QView &q0, const QView &q1, int bits, int gs, int n_slots) {
+    (void)gs;
+    const QView *qs[2] = {&q0, mode == PF_GATEUP ? &q1 : &q0};
+    for (int p = 0; p < 2; ++p) {
+        const QView &q = *qs[p];
+        const uint64_t rows = (uint64_t)n_slots * (uint64_t)q.rows;
+        const uint64_t row_bytes = (uint64_t)q.words_per_row * 4u, G = (uint64_t)q.groups_per_row;
+        cudaError_t e = map2d(&a.tm_code[p], CU_TENSOR_MAP_DATA_TYPE_UINT8, q.w, row_bytes, rows, row_bytes,
+                              (uint32_t)(kPfKS * bits / 8), (uint32_t)kPfM);
+        if (e == cudaSuccess)
+            e = map2d(&a.tm_scale[p], CU_TENSOR_MAP_DATA_TYPE_UINT16, q.s, G, rows, G * 2u, 8u, (uint32_t)kPfM);
+        if (e == cudaSuccess)
+            e = map2d(&a.tm_bias[p], CU_TENSOR_MAP_DATA_TYPE_UINT16, q.b, G, rows, G * 2u, 8u, (uint32_t)kPfM);
+        if (e != cudaSuccess) return e;
+    }
+    a.wrows = q0.rows;
+    return cudaSuccess;
+}
+
 // K a multiple of 64 and of 8 groups (16-byte scale blocks), rows a multiple
 // of 128 (gate/up) or 256 (down), and a compiled (bits, group) pair.
 bool pf_supported(int K, int rows, int bits, int gs, int mode) {
     const bool bg = (bits == 2 && (gs == 64 || gs == 128)) ||
                     ((bits == 4 || bits == 8) && (gs == 32 || gs == 64 || gs == 128));
     if (!bg) return false;
-    if (K <= 0 || K % kPfKS != 0 || K % (8 * gs) != 0) return false;
+    if (K <= 0 || K % kPfKS != 0 || K % (8 * gs) != 0) return false;  // (kPfKS = 128)
     return rows > 0 && rows % (mode == PF_GATEUP ? kPfM : 2 * kPfM) == 0;
 }
 

@@ -625,6 +625,211 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
     dispatch_block(a.din, a.dout, a.err, s_disp);
 }
 
+// Router logits for many tokens on the tensor cores (bf16 activations, the
+// prefill regime): logits[t][e] = sum_k x[t][k] * Wg[e][k].  bf16 x bf16
+// products are exact in fp32 and accumulate in fp32, the arithmetic of the
+// per-token path above in another summation order.  Block: 64 tokens x 128
+// experts; 8 warps as 2 x 4, each 32 tokens x 32 experts with mma.sync
+// m16n8k16; K in stages of 64 columns through a 3-stage cp.async pipeline
+// (128-byte rows, 16-byte chunks XOR-swizzled by row for ldmatrix).  Writes
+// the logits and, for the element-wise scorings, (score, score + bias); the
+// top-k runs in topk_kernel.
+constexpr int kRlBM = 64, kRlBN = 128, kRlBK = 64, kRlStages = 3;
+constexpr int kRlABytes = kRlBM * 128, kRlStage = (kRlBM + kRlBN) * 128;
+constexpr int kRlSmem = kRlStages * kRlStage;
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void cp16_zfill(uint32_t dst, const void *src, bool ok) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(ok ? 16 : 0)
+                 : "memory");
+}
+
+__global__ void __launch_bounds__(256) router_logits_mma_kernel(RouterArgs a) {
+    extern __shared__ __align__(128) uint8_t rl_smem[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int t0 = blockIdx.x * kRlBM, e0 = blockIdx.y * kRlBN;
+    const int wm = warp >> 2, wn = warp & 3;
+    const uint32_t sb = smem_u32(rl_smem);
+    const int KT = a.H / kRlBK;
+    pdl_wait();
+    pdl_trigger();
+    if (a.zero) {
+        const int nb = gridDim.x * gridDim.y;
+        for (int i = (blockIdx.y * gridDim.x + blockIdx.x) * blockDim.x + tid; i < a.zero_words; i += nb * blockDim.x)
+            a.zero[i] = 0u;
+    }
+    auto load_stage = [&](int kt) {
+        const int kc = kt * kRlBK;
+        const uint32_t base = sb + (uint32_t)((kt % kRlStages) * kRlStage);
+        for (int i = tid; i < (kRlBM + kRlBN) * 8; i += 256) {
+            const int row = i >> 3, ch = i & 7;
+            if (row < kRlBM) {
+                const int t = t0 + row;
+                const uint16_t *src = a.x + (size_t)min(t, a.T - 1) * a.H + kc + ch * 8;
+                cp16_zfill(base + row * 128 + ((ch ^ (row & 7)) << 4), src, t < a.T);
+            } else {
+                const int r = row - kRlBM, e = e0 + r;
+                const uint16_t *src = a.wg + (size_t)min(e, a.E - 1) * a.H + kc + ch * 8;
+                cp16_zfill(base + kRlABytes + r * 128 + ((ch ^ (r & 7)) << 4), src, e < a.E);
+            }
+        }
+    };
+    for (int s = 0; s < kRlStages - 1; ++s) {
+        if (s < KT) load_stage(s);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    }
+    float acc[2][4][4];
+#pragma unroll
+    for (int mi = 0; mi < 2; ++mi)
+#pragma unroll
+        for (int ni = 0; ni < 4; ++ni)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[mi][ni][e] = 0.0f;
+    for (int kt = 0; kt < KT; ++kt) {
+        asm volatile("cp.async.wait_group %0;" ::"n"(kRlStages - 2) : "memory");
+        __syncthreads();  // stage kt landed for every thread; stage kt-1 is free
+        if (kt + kRlStages - 1 < KT) load_stage(kt + kRlStages - 1);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        const uint32_t As = sb + (uint32_t)((kt % kRlStages) * kRlStage), Bs = As + kRlABytes;
+#pragma unroll
+        for (int kk = 0; kk < kRlBK / 16; ++kk) {
+            uint32_t af[2][4], bf[4][2];
+#pragma unroll
+            for (int mi = 0; mi < 2; ++mi) {
+                const int row = wm * 32 + mi * 16 + (lane & 15);
+                const int ch = kk * 2 + (lane >> 4);
+                ldsm_x4(af[mi], As + row * 128 + ((ch ^ (row & 7)) << 4));
+            }
+#pragma unroll
+            for (int nj = 0; nj < 2; ++nj) {
+                const int row = wn * 32 + nj * 16 + (lane & 7) + ((lane >> 4) << 3);
+                const int ch = kk * 2 + ((lane >> 3) & 1);
+                uint32_t r[4];
+                ldsm_x4(r, Bs + row * 128 + ((ch ^ (row & 7)) << 4));
+                bf[2 * nj][0] = r[0];
+                bf[2 * nj][1] = r[1];
+                bf[2 * nj + 1][0] = r[2];
+                bf[2 * nj + 1][1] = r[3];
+            }
+#pragma unroll
+            for (int mi = 0; mi < 2; ++mi)
+#pragma unroll
+                for (int ni = 0; ni < 4; ++ni)
+                    Act<__nv_bfloat16>::mma(acc[mi][ni], af[mi][0], af[mi][1], af[mi][2], af[mi][3], bf[ni][0],
+                                            bf[ni][1]);
+        }
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    const int g = lane >> 2, tq = lane & 3;
+#pragma unroll
+    for (int mi = 0; mi < 2; ++mi)
+#pragma unroll
+        for (int ni = 0; ni < 4; ++ni)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int t = t0 + wm * 32 + mi * 16 + g + 8 * (e >> 1);
+                const int ex = e0 + wn * 32 + ni * 8 + 2 * tq + (e & 1);
+                if (t >= a.T || ex >= a.E) continue;
+                const float v = acc[mi][ni][e];
+                a.partial[(size_t)t * a.E + ex] = v;
+                if (a.scores) {
+                    const float sc = score_fn(v, a.scoring);
+                    a.scores[(size_t)t * a.E + ex] = make_float2(sc, sc + (a.bias ? a.bias[ex] : 0.0f));
+                }
+            }
+}
+
+// ------------------------------------------------------------ large dispatch
+// Deterministic counting sort for many routes (the prefill regime), stable in
+// route order like the single-block dispatch.  Pass 1: each 256-route block
+// counts its routes per bucket.  Pass 2 (one block): per bucket, the totals
+// and each block's starting position; the bucket offsets (exclusive scan).
+// Pass 3: each block scatters its routes (rank inside the block from per-warp
+// counts and __match_any_sync).  dispatch_chunks_kernel then cuts the chunks.
+__device__ __forceinline__ int dispatch_bucket(const DispatchIn &din, int r, int32_t *err) {
+    const int id = din.idx[r];
+    if (id < 0 || id >= din.n_experts) {
+        set_error(err, -3);
+        return din.n_experts;
+    }
+    return id;
+}
+
+__global__ void __launch_bounds__(256) dispatch_count_kernel(DispatchIn din, DispatchOut dout, int32_t *err) {
+    __shared__ int s_cnt[kDispatchSmallMaxBuckets + 1];
+    pdl_wait();
+    pdl_trigger();
+    const int NBk = din.n_experts + 1;
+    for (int i = threadIdx.x; i < NBk; i += blockDim.x) s_cnt[i] = 0;
+    __syncthreads();
+    const int r = blockIdx.x * 256 + threadIdx.x;
+    if (r < din.R) atomicAdd(&s_cnt[dispatch_bucket(din, r, err)], 1);
+    __syncthreads();
+    for (int i = threadIdx.x; i < NBk; i += blockDim.x) dout.blk[(size_t)blockIdx.x * NBk + i] = s_cnt[i];
+}
+
+__global__ void __launch_bounds__(256) dispatch_scan_kernel(DispatchIn din, DispatchOut dout, int nblk) {
+    __shared__ int s_tmp[9];
+    pdl_wait();
+    pdl_trigger();
+    const int NBk = din.n_experts + 1;
+    const int per = (NBk + 255) >> 8;
+    int tot[4] = {0, 0, 0, 0};  // NBk <= 1024
+    for (int q = 0; q < per; ++q) {
+        const int b = threadIdx.x * per + q;
+        if (b >= NBk) continue;
+        int run = 0;
+        for (int k = 0; k < nblk; ++k) {
+            int *c = dout.blk + (size_t)k * NBk + b;
+            const int v = *c;
+            *c = run;  // exclusive within the bucket
+            run += v;
+        }
+        tot[q] = run;
+    }
+    int lsum = 0;
+    for (int q = 0; q < per; ++q) lsum += tot[q];
+    int total;
+    int off = block_scan_256(lsum, s_tmp, &total);
+    for (int q = 0; q < per; ++q) {
+        const int b = threadIdx.x * per + q;
+        if (b >= NBk) continue;
+        dout.counts[b] = tot[q];
+        dout.route_off[b] = off;
+        for (int k = 0; k < nblk; ++k) dout.blk[(size_t)k * NBk + b] += off;
+        off += tot[q];
+    }
+}
+
+__global__ void __launch_bounds__(256) dispatch_scatter_kernel(DispatchIn din, DispatchOut dout) {
+    __shared__ int s_wcnt[8][kDispatchSmallMaxBuckets + 1];
+    pdl_wait();
+    pdl_trigger();
+    const int NBk = din.n_experts + 1;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int i = lane; i < NBk; i += 32) s_wcnt[warp][i] = 0;
+    __syncwarp();
+    const int r = blockIdx.x * 256 + threadIdx.x;
+    int b = 0x7fffffff;
+    if (r < din.R) {
+        const int id = din.idx[r];
+        b = (id < 0 || id >= din.n_experts) ? din.n_experts : id;
+    }
+    const unsigned same = __match_any_sync(LMOE_FULL, b);
+    const int rank = __popc(same & ((1u << lane) - 1u));
+    if (r < din.R && rank == 0) s_wcnt[warp][b] = __popc(same);
+    __syncthreads();
+    if (r < din.R) {
+        int pos = dout.blk[(size_t)blockIdx.x * NBk + b] + rank;
+        for (int w = 0; w < warp; ++w) pos += s_wcnt[w][b];
+        dout.sorted_routes[pos] = r;
+    }
+}
+
 __global__ void __launch_bounds__(256) topk_kernel(TopkArgs a) {
     pdl_wait();
     pdl_trigger();
@@ -697,9 +902,29 @@ cudaError_t launch_dispatch_small(const DispatchIn &din, const DispatchOut &dout
 
 cudaError_t launch_dispatch_large(const DispatchIn &din, const DispatchOut &dout, int32_t *err,
                                   cudaStream_t st) {
-    cudaError_t e = launch_pdl(dispatch_rank_kernel, dim3(din.n_experts + 1), dim3(256), 0, st, din, dout, err);
+    cudaError_t e;
+    if (dout.blk && din.n_experts + 1 <= kDispatchSmallMaxBuckets) {
+        const int nblk = (din.R + 255) / 256;
+        e = launch_pdl(dispatch_count_kernel, dim3(nblk), dim3(256), 0, st, din, dout, err);
+        if (e == cudaSuccess) e = launch_pdl(dispatch_scan_kernel, dim3(1), dim3(256), 0, st, din, dout, nblk);
+        if (e == cudaSuccess) e = launch_pdl(dispatch_scatter_kernel, dim3(nblk), dim3(256), 0, st, din, dout);
+    } else {
+        e = launch_pdl(dispatch_rank_kernel, dim3(din.n_experts + 1), dim3(256), 0, st, din, dout, err);
+    }
     if (e != cudaSuccess) return e;
     return launch_pdl(dispatch_chunks_kernel, dim3(1), dim3(256), 0, st, din, dout, err);
+}
+
+cudaError_t launch_router_logits_mma(const RouterArgs &a, cudaStream_t st) {
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(router_logits_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             kRlSmem);
+        if (e != cudaSuccess) return e;
+        configured = true;
+    }
+    dim3 grid((a.T + kRlBM - 1) / kRlBM, (a.E + kRlBN - 1) / kRlBN, 1);
+    return launch_pdl(router_logits_mma_kernel, grid, dim3(256), kRlSmem, st, a);
 }
 
 cudaError_t launch_panel(const PanelArgs &a, cudaStream_t st) {
