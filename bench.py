@@ -48,6 +48,7 @@ METRIC = "routed-MoE layer tokens/s + % HBM roofline (decode)"
 UNIT = "tokens/s"
 L2_BYTES = 126 * 1024 * 1024
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1400.0  # sustained under the power cap
 
 
 def parse():
@@ -65,6 +66,8 @@ def parse():
     p.add_argument("--kernel-steps", type=int, default=200)
     p.add_argument("--cpu-sample", type=int, default=24, help="decode steps timed for the CPU baseline")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--prefill-steps", type=int, default=20,
+                   help="timed C3 prefill steps reported in the line's 'prefill' object (0 = skip; N=1 only)")
     p.add_argument("--ep", action="store_true",
                    help="expert-parallel layer (experts sharded over the ranks, NCCL all-to-all dispatch/combine)")
     p.add_argument("--layout", choices=["tiled", "rowmajor"], default="tiled",
@@ -86,6 +89,16 @@ def measured_peak():
         d = json.loads(f.read_text())
         return float(d["hbm_gbs"]), "measured"
     return FALLBACK_HBM_GBS, "fallback"
+
+
+def measured_tensor_peak():
+    """Sustained cuBLAS bf16 TFLOP/s (the prefill kernels run inside a long step)."""
+    f = ROOT / "MEASURED_PEAKS.json"
+    if f.exists():
+        d = json.loads(f.read_text())
+        if "bf16_tflops_sustained" in d:
+            return float(d["bf16_tflops_sustained"]), "measured sustained"
+    return FALLBACK_BF16_TFLOPS, "fallback"
 
 
 class ClockSampler:
@@ -335,6 +348,9 @@ def run_ours(args):
     e2e = None
     if args.e2e_steps > 0:
         e2e = run_e2e(args, cfg, layers, n_layers, dev)
+    prefill = None
+    if world == 1 and args.prefill_steps > 0:
+        prefill = run_prefill(args, dev)
 
     if rank != 0:
         if world > 1:
@@ -365,11 +381,65 @@ def run_ours(args):
         "clocks": clocks.summary(),
         "e2e": e2e,
         "cpu_baseline": cpu,
+        "prefill": prefill,
     }
     print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
+
+
+def run_prefill(args, dev):
+    """C3: the prefill grouped GEMM on the config-1 layer (4096 tokens, uniform
+    routing, 2-bit g64).  Tokens/s of the whole layer step (inputs in HBM,
+    CUDA events), and the tensor roofline of the gate/up kernel (gate + up
+    FLOPs of the routes / its mean duration)."""
+    from locali_b200 import ops, synth
+
+    cfg = synth.config("c3")
+    T = cfg.tokens
+    layer = synth.make_layer(cfg, seed=5, device=dev)
+    kern = ops.MoEKernel(layer.router, layer.experts, layer.expert_slot, cfg.swiglu_limit, path="prefill")
+    K, W = args.prefill_steps, 3
+    g = torch.Generator(device=dev).manual_seed(99)
+    xs = torch.randn((2, T, cfg.hidden), generator=g, device=dev).to(torch.bfloat16)  # 2 x 32 MB, cycled
+    out = torch.empty_like(xs[0])
+    for i in range(W):
+        kern(xs[i % 2], out=out)
+    torch.cuda.synchronize()
+    kern.ws.check()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for i in range(K):
+        kern(xs[i % 2], out=out)
+    end.record()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / K
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(K)]
+    for i in range(K):
+        ev[i][0].record()
+        kern.staged(xs[i % 2], out, ev[i][1], ev[i][2])
+        ev[i][3].record()
+    torch.cuda.synchronize()
+    gu_ms = sum(e[1].elapsed_time(e[2]) for e in ev) / K
+    dn_ms = sum(e[2].elapsed_time(e[3]) for e in ev) / K
+    rt_ms = sum(e[0].elapsed_time(e[1]) for e in ev) / K
+    R = T * cfg.top_k
+    gu_flops = R * 2 * 2 * cfg.hidden * cfg.inter
+    all_flops = R * 3 * 2 * cfg.hidden * cfg.inter
+    peak, kind = measured_tensor_peak()
+    achieved = gu_flops / (gu_ms / 1e3) / 1e12
+    return {
+        "workload": f"c3 prefill: {T} tokens, hidden {cfg.hidden}, {cfg.n_experts} experts top-{cfg.top_k} "
+                    f"(uniform routing), inter {cfg.inter}, 2-bit affine g{cfg.group_size}",
+        "value": T / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms, "steps": K, "warmup": W,
+        "layer_tflops": all_flops / (ms / 1e3) / 1e12,
+        "kernels_us": {"router_dispatch": 1e3 * rt_ms, "gateup_swiglu": 1e3 * gu_ms, "down_combine": 1e3 * dn_ms},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "peak_source": f"{kind} (MEASURED_PEAKS.json bf16_tflops_sustained)",
+                     "kernel": "pf_gemm_kernel<bf16, 2, 64, gate/up> (tcgen05)",
+                     "algorithmic_flops_per_launch": gu_flops},
+    }
 
 
 def run_e2e(args, cfg, layers, n_layers, dev):

@@ -45,8 +45,8 @@ constexpr int kPfM = 128;        // weight rows per accumulator (MMA M)
 constexpr int kPfKS = 128;       // K columns per stage: two 128-byte swizzle atoms of 16-bit values
 constexpr int kPfSS = 2;         // stages in flight: operand A in tensor memory, operand B in shared memory
 constexpr int kPfDeqWarps = 16;  // 512 threads: one (accumulator, row, K half) each
-constexpr int kPfEpiWarps = 4;
-constexpr int kPfDeq0 = 3;       // warps: 0 operand B, 1 MMA, 2 weights, 3..18 dequantisation, 19..22 epilogue
+constexpr int kPfEpiWarps = 8;   // two per TMEM lane quarter, alternate 16-column chunks
+constexpr int kPfDeq0 = 3;       // warps: 0 operand B, 1 MMA, 2 weights, 3..18 dequantisation, 19..26 epilogue
 constexpr int kPfThreads = (kPfDeq0 + kPfDeqWarps + kPfEpiWarps) * 32;
 constexpr int kPfBAtom = kPfNmax * 128;              // one 64-column atom of B: 16 KB
 constexpr int kPfBTile = 2 * kPfBAtom;               // B slot: 2 atoms, 32 KB
@@ -159,6 +159,11 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
         "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
         "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
         : "memory");
+}
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
+                 "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+                 : "memory");
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row atoms of
@@ -679,18 +684,19 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
                         sp[gg][1] = sp[gg][2] = sp[gg][0];
                     }
                 }
-                uint32_t pr[32];
-#pragma unroll
-                for (int u = 0; u < HW; ++u) {
-                    const int gg = NG == 2 ? (u * CPW) / GS : 0;
-                    const typename C::W w = C::prep(words[u]);
-#pragma unroll
-                    for (int m = 0; m < C::kPairs; ++m)
-                        pr[u * C::kPairs + m] = P::fma2(C::q(w, m), sp[gg][C::pexp(m)], b2[gg]);
-                }
+                // 32 packed pairs in 4 stores of 8 TMEM columns
                 const uint32_t adst = arow + (uint32_t)(s * 128);
-                tmem_st16(adst, *reinterpret_cast<const uint32_t(*)[16]>(&pr[0]));
-                tmem_st16(adst + 16u, *reinterpret_cast<const uint32_t(*)[16]>(&pr[16]));
+#pragma unroll
+                for (int blk = 0; blk < 4; ++blk) {
+                    uint32_t pr[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const int pi = blk * 8 + i, u = pi / C::kPairs, m = pi % C::kPairs;
+                        const int gg = NG == 2 ? (u * CPW) / GS : 0;
+                        pr[i] = P::fma2(C::q(C::prep(words[u]), m), sp[gg][C::pexp(m)], b2[gg]);
+                    }
+                    tmem_st8(adst + (uint32_t)(8 * blk), pr);
+                }
                 tmem_wait_st();
                 // the generic-proxy reads of the code and scale slots must be
                 // ordered before their TMA refills (without this fence a refill
@@ -719,6 +725,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
         // 32 chunks of 8 values (accumulator 0 in chunks 0-15, 1 in 16-31),
         // chunk c at position c ^ (r & 31).
         const int q4 = warp & 3;
+        const int hc = (warp - kPfDeq0 - kPfDeqWarps) >> 2;  // this warp's 16-column chunks: (j0 / 16) % 2 == hc
         const int r = q4 * 32 + lane;
         const uint32_t srow_e = stg + (uint32_t)(r * 512);
         const int rx = r & 31;
@@ -735,7 +742,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
             }
             tc_fence_after();
             const uint32_t t0 = tmem + ((uint32_t)(q4 * 32) << 16);
-            for (int j0 = 0; j0 < N; j0 += 16) {
+            for (int j0 = 16 * hc; j0 < N; j0 += 32) {
                 uint32_t v0[16], v1[16];
                 tmem_ld16(t0 + (uint32_t)j0, v0);
                 tmem_ld16(t0 + 128u + (uint32_t)j0, v1);
@@ -765,7 +772,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
                 const int f = rb * kPfM + r;
                 const int kp = pf_perm_pos(f, a.hbits);
                 const int pbase = pf_row_base(ch.route_start, c);
-                for (int j0 = 0; j0 < N; j0 += 8) {
+                for (int j0 = 16 * hc; j0 < N; j0 += (j0 & 8) ? 24 : 8) {
                     const uint4 gq = lds128(srow_e + (uint32_t)(((j0 >> 3) ^ rx) << 4));
                     const uint4 uq = lds128(srow_e + (uint32_t)(((16 + (j0 >> 3)) ^ rx) << 4));
                     const uint32_t gw[4] = {gq.x, gq.y, gq.z, gq.w}, uw[4] = {uq.x, uq.y, uq.z, uq.w};
@@ -786,7 +793,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
 #pragma unroll 1
                 for (int pp = 0; pp < 2; ++pp) {
                     const int f = rb * 2 * kPfM + pp * kPfM + r;
-                    for (int j0 = 0; j0 < N; j0 += 8) {
+                    for (int j0 = 16 * hc; j0 < N; j0 += (j0 & 8) ? 24 : 8) {
                         // route and combine weight of column j0 + (lane & 7)
                         const int jl = j0 + (lane & 7);
                         int my_route = 0;

@@ -772,36 +772,63 @@ __global__ void __launch_bounds__(256) dispatch_count_kernel(DispatchIn din, Dis
     for (int i = threadIdx.x; i < NBk; i += blockDim.x) dout.blk[(size_t)blockIdx.x * NBk + i] = s_cnt[i];
 }
 
-__global__ void __launch_bounds__(256) dispatch_scan_kernel(DispatchIn din, DispatchOut dout, int nblk) {
-    __shared__ int s_tmp[9];
+// Pass 2, one block of 1024 threads: a warp per bucket turns that bucket's
+// per-block counts into exclusive per-block offsets (within the bucket) and
+// totals it; then the bucket offsets are an exclusive scan of the totals.
+__global__ void __launch_bounds__(1024) dispatch_scan_kernel(DispatchIn din, DispatchOut dout, int nblk) {
+    __shared__ int s_tot[kDispatchSmallMaxBuckets + 1];
+    __shared__ int s_wsum[32];
     pdl_wait();
     pdl_trigger();
     const int NBk = din.n_experts + 1;
-    const int per = (NBk + 255) >> 8;
-    int tot[4] = {0, 0, 0, 0};  // NBk <= 1024
-    for (int q = 0; q < per; ++q) {
-        const int b = threadIdx.x * per + q;
-        if (b >= NBk) continue;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int b = warp; b < NBk; b += 32) {
         int run = 0;
-        for (int k = 0; k < nblk; ++k) {
+        for (int k0 = 0; k0 < nblk; k0 += 32) {
+            const int k = k0 + lane;
             int *c = dout.blk + (size_t)k * NBk + b;
-            const int v = *c;
-            *c = run;  // exclusive within the bucket
-            run += v;
+            const int v = k < nblk ? *c : 0;
+            int incl = v;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int n = __shfl_up_sync(LMOE_FULL, incl, o);
+                if (lane >= o) incl += n;
+            }
+            if (k < nblk) *c = run + incl - v;
+            run += __shfl_sync(LMOE_FULL, incl, 31);
         }
-        tot[q] = run;
+        if (lane == 0) s_tot[b] = run;
     }
-    int lsum = 0;
-    for (int q = 0; q < per; ++q) lsum += tot[q];
-    int total;
-    int off = block_scan_256(lsum, s_tmp, &total);
-    for (int q = 0; q < per; ++q) {
-        const int b = threadIdx.x * per + q;
-        if (b >= NBk) continue;
-        dout.counts[b] = tot[q];
-        dout.route_off[b] = off;
-        for (int k = 0; k < nblk; ++k) dout.blk[(size_t)k * NBk + b] += off;
-        off += tot[q];
+    __syncthreads();
+    // exclusive scan of the totals: thread t owns buckets 2t, 2t+1
+    const int b0 = 2 * threadIdx.x;
+    const int t0 = b0 < NBk ? s_tot[b0] : 0, t1 = b0 + 1 < NBk ? s_tot[b0 + 1] : 0;
+    int incl = t0 + t1;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(LMOE_FULL, incl, o);
+        if (lane >= o) incl += n;
+    }
+    if (lane == 31) s_wsum[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        int w = s_wsum[lane], wi = w;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int n = __shfl_up_sync(LMOE_FULL, wi, o);
+            if (lane >= o) wi += n;
+        }
+        s_wsum[lane] = wi - w;
+    }
+    __syncthreads();
+    const int ex = s_wsum[warp] + incl - (t0 + t1);
+    if (b0 < NBk) {
+        dout.counts[b0] = t0;
+        dout.route_off[b0] = ex;
+    }
+    if (b0 + 1 < NBk) {
+        dout.counts[b0 + 1] = t1;
+        dout.route_off[b0 + 1] = ex + t0;
     }
 }
 
@@ -824,7 +851,7 @@ __global__ void __launch_bounds__(256) dispatch_scatter_kernel(DispatchIn din, D
     if (r < din.R && rank == 0) s_wcnt[warp][b] = __popc(same);
     __syncthreads();
     if (r < din.R) {
-        int pos = dout.blk[(size_t)blockIdx.x * NBk + b] + rank;
+        int pos = dout.route_off[b] + dout.blk[(size_t)blockIdx.x * NBk + b] + rank;
         for (int w = 0; w < warp; ++w) pos += s_wcnt[w][b];
         dout.sorted_routes[pos] = r;
     }
@@ -906,7 +933,7 @@ cudaError_t launch_dispatch_large(const DispatchIn &din, const DispatchOut &dout
     if (dout.blk && din.n_experts + 1 <= kDispatchSmallMaxBuckets) {
         const int nblk = (din.R + 255) / 256;
         e = launch_pdl(dispatch_count_kernel, dim3(nblk), dim3(256), 0, st, din, dout, err);
-        if (e == cudaSuccess) e = launch_pdl(dispatch_scan_kernel, dim3(1), dim3(256), 0, st, din, dout, nblk);
+        if (e == cudaSuccess) e = launch_pdl(dispatch_scan_kernel, dim3(1), dim3(1024), 0, st, din, dout, nblk);
         if (e == cudaSuccess) e = launch_pdl(dispatch_scatter_kernel, dim3(nblk), dim3(256), 0, st, din, dout);
     } else {
         e = launch_pdl(dispatch_rank_kernel, dim3(din.n_experts + 1), dim3(256), 0, st, din, dout, err);
