@@ -130,6 +130,18 @@ int lmoe_route(const lmoe_router *router, int32_t hidden, int32_t dtype,
                const void *x, int32_t tokens, int32_t *idx, float *w,
                void *workspace, size_t ws_bytes, void *stream);
 
+/* lmoe_route for a layer with token-id hash routing (the first layers of the
+ * V4 gate, dsv4_arena.py:149-152): the experts of token t are given,
+ * hash_idx[t * top_k + j] (the checkpoint's token-id -> expert table gathered
+ * at the token ids, on the device); w receives their scores normalised and
+ * routed-scaled as for a scored layer.  The V4 MoEGate that defines the
+ * reference arithmetic is not part of the reference repository; this follows
+ * the scored layers' weight computation. */
+int lmoe_route_hashed(const lmoe_router *router, int32_t hidden, int32_t dtype,
+                      const void *x, int32_t tokens, const int32_t *hash_idx,
+                      int32_t *idx, float *w, void *workspace, size_t ws_bytes,
+                      void *stream);
+
 /* Workspace bytes for lmoe_route with up to max_tokens tokens. */
 size_t lmoe_workspace_size_route(const lmoe_router *router, int32_t hidden,
                                  int32_t max_tokens);
@@ -175,6 +187,13 @@ int lmoe_moe_layer_path(const lmoe_layer *layer, const void *x, int32_t tokens,
                         void *out, int32_t *idx, float *w, void *workspace,
                         size_t ws_bytes, void *stream, int32_t path,
                         void *ev_routed, void *ev_gateup);
+
+/* lmoe_moe_layer_path with token-id hash routing (see lmoe_route_hashed);
+ * same workspace as lmoe_moe_layer_path. */
+int lmoe_moe_layer_hashed(const lmoe_layer *layer, const void *x, int32_t tokens,
+                          const int32_t *hash_idx, void *out, int32_t *idx,
+                          float *w, void *workspace, size_t ws_bytes,
+                          void *stream, int32_t path);
 
 /* Workspace bytes for lmoe_moe_layer_path calls of up to max_tokens tokens
  * on `path` (0 when the path is unavailable).  lmoe_workspace_size equals

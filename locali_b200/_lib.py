@@ -95,6 +95,10 @@ _SIGS = {
     "lmoe_route": ([ctypes.POINTER(Router), ctypes.c_int32, ctypes.c_int32, _VP, ctypes.c_int32, _VP, _VP, _VP,
                     ctypes.c_size_t, _VP], ctypes.c_int),
     "lmoe_workspace_size_route": ([ctypes.POINTER(Router), ctypes.c_int32, ctypes.c_int32], ctypes.c_size_t),
+    "lmoe_route_hashed": ([ctypes.POINTER(Router), ctypes.c_int32, ctypes.c_int32, _VP, ctypes.c_int32, _VP, _VP, _VP,
+                           _VP, ctypes.c_size_t, _VP], ctypes.c_int),
+    "lmoe_moe_layer_hashed": ([ctypes.POINTER(Layer), _VP, ctypes.c_int32, _VP, _VP, _VP, _VP, _VP, ctypes.c_size_t,
+                               _VP, ctypes.c_int32], ctypes.c_int),
     "lmoe_moe_layer": ([ctypes.POINTER(Layer), _VP, ctypes.c_int32, _VP, _VP, _VP, _VP, ctypes.c_size_t,
                         _VP], ctypes.c_int),
     "lmoe_moe_layer_staged": ([ctypes.POINTER(Layer), _VP, ctypes.c_int32, _VP, _VP, _VP, _VP, ctypes.c_size_t,

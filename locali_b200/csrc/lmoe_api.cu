@@ -398,7 +398,8 @@ int lmoe_workspace_status(void *workspace, void *stream) {
 // Router (+ top-k, + dispatch when `l` is given).  In the decode regime the
 // router kernel's last block runs top-k (and dispatch) itself: one launch.
 static int route_impl(const lmoe_router &r, int H, int dtype, const lmoe_layer *l, const Layout &L, const void *x,
-                      int T, int32_t *idx_user, float *w_user, void *ws, cudaStream_t st) {
+                      int T, int32_t *idx_user, float *w_user, void *ws, cudaStream_t st,
+                      const int32_t *hash_idx = nullptr) {
     const int k = r.top_k;
     const int R = T * k;
     const int ksplit = 1;
@@ -434,6 +435,7 @@ static int route_impl(const lmoe_router &r, int H, int dtype, const lmoe_layer *
         }
     }
     a.act_f16 = dtype == LMOE_F16;
+    a.hash_idx = hash_idx;
     a.counter = at<uint32_t>(ws, L.status) + 1;
     a.idx_ws = at<int32_t>(ws, L.idx);
     a.w_ws = at<float>(ws, L.w);
@@ -496,6 +498,7 @@ static int route_impl(const lmoe_router &r, int H, int dtype, const lmoe_layer *
         tk.w_ws = a.w_ws;
         tk.idx_user = idx_user;
         tk.w_user = w_user;
+        tk.hash_idx = hash_idx;
         rc = cuda_rc(launch_topk(tk, st));
         if (rc) return rc;
     }
@@ -519,8 +522,9 @@ size_t lmoe_workspace_size_route(const lmoe_router *router, int32_t hidden, int3
                        1, 0).total;
 }
 
-int lmoe_route(const lmoe_router *router, int32_t hidden, int32_t dtype, const void *x, int32_t tokens,
-               int32_t *idx, float *w, void *workspace, size_t ws_bytes, void *stream) {
+static int route_entry(const lmoe_router *router, int32_t hidden, int32_t dtype, const void *x, int32_t tokens,
+                       const int32_t *hash_idx, int32_t *idx, float *w, void *workspace, size_t ws_bytes,
+                       void *stream) {
     int rc = check_router(router, hidden);
     if (rc) return rc;
     if (dtype != LMOE_BF16 && dtype != LMOE_F16) return LMOE_EUNSUPPORTED;
@@ -530,12 +534,24 @@ int lmoe_route(const lmoe_router *router, int32_t hidden, int32_t dtype, const v
                                  router->n_experts, 1, 0);
     if (ws_bytes < L.total) return LMOE_EWORKSPACE;
     return route_impl(*router, hidden, dtype, nullptr, L, x, tokens, idx, w, workspace,
-                      static_cast<cudaStream_t>(stream));
+                      static_cast<cudaStream_t>(stream), hash_idx);
 }
 
-int lmoe_moe_layer_path(const lmoe_layer *layer, const void *x, int32_t tokens, void *out, int32_t *idx, float *w,
-                        void *workspace, size_t ws_bytes, void *stream, int32_t path, void *ev_routed,
-                        void *ev_gateup) {
+int lmoe_route_hashed(const lmoe_router *router, int32_t hidden, int32_t dtype, const void *x, int32_t tokens,
+                      const int32_t *hash_idx, int32_t *idx, float *w, void *workspace, size_t ws_bytes,
+                      void *stream) {
+    if (tokens > 0 && !hash_idx) return LMOE_EINVAL;
+    return route_entry(router, hidden, dtype, x, tokens, hash_idx, idx, w, workspace, ws_bytes, stream);
+}
+
+int lmoe_route(const lmoe_router *router, int32_t hidden, int32_t dtype, const void *x, int32_t tokens,
+               int32_t *idx, float *w, void *workspace, size_t ws_bytes, void *stream) {
+    return route_entry(router, hidden, dtype, x, tokens, nullptr, idx, w, workspace, ws_bytes, stream);
+}
+
+static int layer_entry(const lmoe_layer *layer, const void *x, int32_t tokens, const int32_t *hash_idx, void *out,
+                       int32_t *idx, float *w, void *workspace, size_t ws_bytes, void *stream, int32_t path,
+                       void *ev_routed, void *ev_gateup) {
     int rc = check_layer(layer);
     if (rc) return rc;
     if (tokens < 0 || (tokens > 0 && (!x || !out || !workspace))) return LMOE_EINVAL;
@@ -547,12 +563,27 @@ int lmoe_moe_layer_path(const lmoe_layer *layer, const void *x, int32_t tokens, 
     if (ws_bytes < L.total) return LMOE_EWORKSPACE;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     rc = route_impl(layer->router, layer->experts.hidden, layer->experts.dtype, layer, L, x, tokens, idx, w,
-                    workspace, st);
+                    workspace, st, hash_idx);
     if (rc) return rc;
     if (ev_routed && cudaEventRecord(static_cast<cudaEvent_t>(ev_routed), st) != cudaSuccess) return LMOE_ECUDA;
     const float *rw = at<float>(workspace, L.w);
     if (pf) return run_experts_pf(layer, L, workspace, x, tokens, rw, out, st, static_cast<cudaEvent_t>(ev_gateup));
     return run_experts(layer, L, workspace, tokens, rw, out, st, static_cast<cudaEvent_t>(ev_gateup));
+}
+
+int lmoe_moe_layer_path(const lmoe_layer *layer, const void *x, int32_t tokens, void *out, int32_t *idx, float *w,
+                        void *workspace, size_t ws_bytes, void *stream, int32_t path, void *ev_routed,
+                        void *ev_gateup) {
+    return layer_entry(layer, x, tokens, nullptr, out, idx, w, workspace, ws_bytes, stream, path, ev_routed,
+                       ev_gateup);
+}
+
+int lmoe_moe_layer_hashed(const lmoe_layer *layer, const void *x, int32_t tokens, const int32_t *hash_idx,
+                          void *out, int32_t *idx, float *w, void *workspace, size_t ws_bytes, void *stream,
+                          int32_t path) {
+    if (tokens > 0 && !hash_idx) return LMOE_EINVAL;
+    return layer_entry(layer, x, tokens, hash_idx, out, idx, w, workspace, ws_bytes, stream, path, nullptr,
+                       nullptr);
 }
 
 size_t lmoe_workspace_size_path(const lmoe_layer *layer, int32_t max_tokens, int32_t path) {

@@ -112,6 +112,8 @@ struct RouterArgs {
     // combine counters of this call, zeroed by the router blocks
     uint32_t *zero;
     int32_t zero_words;
+    // token-id hash routing: [T, top_k] expert ids replacing the top-k search, or nullptr
+    const int32_t *hash_idx;
 };
 
 struct TopkArgs {
@@ -124,6 +126,7 @@ struct TopkArgs {
     float *w_ws;
     int32_t *idx_user;
     float *w_user;
+    const int32_t *hash_idx;  // as RouterArgs::hash_idx
 };
 
 struct PanelArgs {

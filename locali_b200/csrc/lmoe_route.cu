@@ -277,7 +277,7 @@ __device__ __forceinline__ float score_fn(float lg, int scoring) {
 __device__ void topk_token(const float *partial, const float2 *scores, int ksplit, int T, int E, int tok,
                            const float *bias, int scoring, int top_k, int norm, float scaling,
                            int32_t *idx_ws, float *w_ws, int32_t *idx_user, float *w_user,
-                           int *s_idx = nullptr) {
+                           int *s_idx = nullptr, const int32_t *hash_idx = nullptr) {
     const int lane = threadIdx.x & 31;
     float sc[kRouterMaxEPL], bs[kRouterMaxEPL];
     if (scores) {
@@ -332,6 +332,28 @@ __device__ void topk_token(const float *partial, const float2 *scores, int kspli
             bs[i] = (e < E) ? sc[i] + (bias ? bias[e] : 0.0f) : -INFINITY;
         }
     }
+    int my_e = -1;
+    float my_s = 0.0f;
+    if (hash_idx) {
+        // token-id hash routing: the experts are given (tid2eid[input_ids]);
+        // the weights are their scores, normalised and scaled as below.  An
+        // id outside [0, E) keeps score 0 (dispatch sends it to the zero slot).
+        const int e_l = lane < top_k ? hash_idx[(size_t)tok * top_k + lane] : -1;
+#pragma unroll 1
+        for (int j = 0; j < top_k; ++j) {
+            const int e = __shfl_sync(LMOE_FULL, e_l, j);
+            const bool ok = e >= 0 && e < E;
+            float v = 0.0f;
+#pragma unroll
+            for (int i = 0; i < kRouterMaxEPL; ++i)
+                if (ok && i == (e >> 5)) v = sc[i];
+            const float sv = __shfl_sync(LMOE_FULL, v, ok ? (e & 31) : 0);
+            if (lane == j) {
+                my_e = e;
+                my_s = ok ? sv : 0.0f;
+            }
+        }
+    } else {
     // Each lane keeps its own best candidate; a round takes the warp-wide
     // best and only the winning lane rescans its candidates.  Lane j keeps
     // the j-th winner.
@@ -344,8 +366,6 @@ __device__ void topk_token(const float *partial, const float2 *scores, int kspli
             lbe = lane + 32 * i;
             lbs = sc[i];
         }
-    int my_e = -1;
-    float my_s = 0.0f;
 #pragma unroll 1
     for (int j = 0; j < top_k; ++j) {
         float bv = lbv;
@@ -377,6 +397,7 @@ __device__ void topk_token(const float *partial, const float2 *scores, int kspli
                 }
             }
         }
+    }
     }
     float ssum = 0.0f;  // fp32, in selection order
 #pragma unroll 1
@@ -613,7 +634,7 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
         for (int e = tid; e < a.E; e += blockDim.x) s_slot[e] = a.din.expert_slot ? a.din.expert_slot[e] : e;
     for (int tok = warp; tok < a.T; tok += 8)
         topk_token(a.partial, a.scores, 1, a.T, a.E, tok, a.bias, a.scoring, a.top_k, a.norm_topk, a.scaling,
-                   a.idx_ws, a.w_ws, a.idx_user, a.w_user, warp_disp ? s_idx : nullptr);
+                   a.idx_ws, a.w_ws, a.idx_user, a.w_user, warp_disp ? s_idx : nullptr, a.hash_idx);
     if (!a.do_dispatch) return;
     if (warp_disp) {
         __syncthreads();
@@ -864,7 +885,7 @@ __global__ void __launch_bounds__(256) topk_kernel(TopkArgs a) {
     const int tok = blockIdx.x * 8 + warp;
     if (tok >= a.T) return;
     topk_token(a.partial, a.scores, a.ksplit, a.T, a.E, tok, a.bias, a.scoring, a.top_k, a.norm_topk,
-               a.scaling, a.idx_ws, a.w_ws, a.idx_user, a.w_user);
+               a.scaling, a.idx_ws, a.w_ws, a.idx_user, a.w_user, nullptr, a.hash_idx);
 }
 
 // ============================================================ activation panel

@@ -209,7 +209,7 @@ class V4ArenaMoE(ArenaMoE):
         direct = (self._resident and isinstance(self.gate, V4Gate) and self.nxt is None and self.nxt2 is None)
         if direct:
             self.store.sync_table()
-            out = self.kernel(tier)(flat).reshape(shape)
+            out = self.kernel(tier)(flat, hash_idx=self.gate.hash_idx(input_ids)).reshape(shape)
             return out if out.dtype == x.dtype else out.to(x.dtype)
         inds, gates = self.route(x, input_ids)
         ii = inds.reshape(-1, self.top_k)

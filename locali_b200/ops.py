@@ -244,12 +244,20 @@ class MoEKernel:
         return x.reshape(-1, x.shape[-1]).contiguous()
 
     def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None, idx: torch.Tensor | None = None,
-                 w: torch.Tensor | None = None) -> torch.Tensor:
+                 w: torch.Tensor | None = None, hash_idx: torch.Tensor | None = None) -> torch.Tensor:
+        """The whole layer.  ``hash_idx`` [T, top_k] selects the experts of
+        each token (token-id hash routing) instead of the router's top-k."""
         flat = self._x(x)
         T = flat.shape[0]
         if out is None:
             out = torch.empty_like(flat)
         self.ws.ensure(self.workspace_bytes(T))
+        h = _hash(hash_idx, T, self.router.top_k)
+        if h is not None:
+            check(lmoe().lmoe_moe_layer_hashed(ctypes.byref(self.desc), flat.data_ptr(), T, h.data_ptr(),
+                                               out.data_ptr(), _ptr(idx), _ptr(w), self.ws.ptr(), self.ws.nbytes,
+                                               _stream(), _lib.PATH[self.path]), "lmoe_moe_layer_hashed")
+            return out.reshape(x.shape)
         check(lmoe().lmoe_moe_layer_path(ctypes.byref(self.desc), flat.data_ptr(), T, out.data_ptr(), _ptr(idx),
                                          _ptr(w), self.ws.ptr(), self.ws.nbytes, _stream(), _lib.PATH[self.path],
                                          None, None), "lmoe_moe_layer")
@@ -300,8 +308,22 @@ class MoEKernel:
         return out.reshape(x.shape)
 
 
-def route(x: torch.Tensor, router: RouterArrays, ws: Workspace | None = None) -> tuple[torch.Tensor, torch.Tensor]:
-    """Router kernel only: x [T, hidden] -> (idx int32 [T, k], w fp32 [T, k])."""
+def _hash(hash_idx: torch.Tensor | None, T: int, k: int) -> torch.Tensor | None:
+    if hash_idx is None:
+        return None
+    _need_cuda(hash_idx)
+    h = hash_idx.reshape(T, -1)
+    if h.shape[1] != k:
+        raise ValueError(f"hash_idx must hold top_k={k} experts per token")
+    return h.to(torch.int32).contiguous()
+
+
+def route(x: torch.Tensor, router: RouterArrays, ws: Workspace | None = None,
+          hash_idx: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Router kernel only: x [T, hidden] -> (idx int32 [T, k], w fp32 [T, k]).
+
+    ``hash_idx`` [T, k] (token-id hash routing): the experts are given; the
+    weights are their normalised, routed-scaled scores."""
     _need_cuda(x, router.weight)
     if x.dtype not in _ACT:
         raise ValueError(f"unsupported activation dtype {x.dtype}")
@@ -315,8 +337,14 @@ def route(x: torch.Tensor, router: RouterArrays, ws: Workspace | None = None) ->
     if n == 0:
         raise _lib.LmoeError(_lib.LMOE_EUNSUPPORTED, "router descriptor")
     ws = (ws or Workspace(flat.device)).ensure(int(n))
-    check(lmoe().lmoe_route(ctypes.byref(desc), H, _ACT[flat.dtype], flat.data_ptr(), T, idx.data_ptr(),
-                            w.data_ptr(), ws.ptr(), ws.nbytes, _stream()), "lmoe_route")
+    h = _hash(hash_idx, T, k)
+    if h is None:
+        check(lmoe().lmoe_route(ctypes.byref(desc), H, _ACT[flat.dtype], flat.data_ptr(), T, idx.data_ptr(),
+                                w.data_ptr(), ws.ptr(), ws.nbytes, _stream()), "lmoe_route")
+    else:
+        check(lmoe().lmoe_route_hashed(ctypes.byref(desc), H, _ACT[flat.dtype], flat.data_ptr(), T, h.data_ptr(),
+                                       idx.data_ptr(), w.data_ptr(), ws.ptr(), ws.nbytes, _stream()),
+              "lmoe_route_hashed")
     return idx, w
 
 

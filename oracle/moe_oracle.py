@@ -273,12 +273,18 @@ def _score(logits: np.ndarray, scoring: str) -> np.ndarray:
 
 
 def router(x: np.ndarray, weight: np.ndarray, bias: np.ndarray | None, top_k: int,
-           scoring: str = "sigmoid", routed_scaling: float = 1.0, norm_topk: bool = True):
+           scoring: str = "sigmoid", routed_scaling: float = 1.0, norm_topk: bool = True,
+           hash_idx: np.ndarray | None = None):
     """``ArenaMoE.route`` (``arena.py:501-506``) plus V4 routed scaling.
 
     x [T, H] values, weight [E, H] values (bf16 numbers).  Returns
     (idx [T,k] int32 ordered by biased score desc, w [T,k] float32,
     scores [T,E] float32, biased [T,E] float32).
+
+    ``hash_idx`` [T, k]: token-id hash routing (the V4 gate's first layers,
+    ``dsv4_arena.py:149-152``; the gate itself is not in the reference
+    repository): the experts are given and weighted by their scores,
+    normalised and scaled as for scored layers (ids outside [0, E) score 0).
     """
     x64 = np.asarray(x, np.float64)
     w64 = np.asarray(weight, np.float64)
@@ -286,10 +292,15 @@ def router(x: np.ndarray, weight: np.ndarray, bias: np.ndarray | None, top_k: in
     scores = _score(logits, scoring)
     biased = scores if bias is None else (scores + np.asarray(bias, np.float32)).astype(np.float32)
     T, E = scores.shape
-    # stable descending order: ties -> lower expert id first
-    order = np.argsort(-biased, axis=-1, kind="stable")
-    idx = order[:, :top_k].astype(np.int32)
-    g = np.take_along_axis(scores, idx, axis=-1).astype(np.float32)
+    if hash_idx is not None:
+        idx = np.asarray(hash_idx).reshape(T, top_k).astype(np.int32)
+        ok = (idx >= 0) & (idx < E)
+        g = np.where(ok, np.take_along_axis(scores, np.clip(idx, 0, E - 1), axis=-1), 0).astype(np.float32)
+    else:
+        # stable descending order: ties -> lower expert id first
+        order = np.argsort(-biased, axis=-1, kind="stable")
+        idx = order[:, :top_k].astype(np.int32)
+        g = np.take_along_axis(scores, idx, axis=-1).astype(np.float32)
     if norm_topk:
         w = g / (g.sum(-1, keepdims=True, dtype=np.float32) + np.float32(1e-20))
     else:

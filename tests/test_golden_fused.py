@@ -84,3 +84,15 @@ def test_kernel_matches_reference_kernel(built, case, tiled):
     got = h.float().cpu().numpy()
     ref = _to_f32(bits, dtype)
     _check(got, ref)
+
+
+def test_oracle_hash_router_weights():
+    """The hash-routed oracle takes the given experts and normalises their scores."""
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((3, 64)).astype(np.float32)
+    wg = (rng.standard_normal((8, 64)) * 0.1).astype(np.float32)
+    hidx = np.array([[0, 1], [7, 3], [5, 5]], dtype=np.int32)
+    idx, w, scores, _ = O.router(x, wg, None, 2, "sigmoid", 2.0, True, hash_idx=hidx)
+    assert np.array_equal(idx, hidx)
+    g = np.take_along_axis(scores, hidx, axis=-1)
+    np.testing.assert_allclose(w, 2.0 * g / (g.sum(-1, keepdims=True) + 1e-20), rtol=1e-6)
