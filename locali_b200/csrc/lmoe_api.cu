@@ -10,10 +10,14 @@ using namespace lmoe;
 
 namespace {
 
+// bit widths and group sizes of the decode GEMVs
 bool gemv_ok(int bits, int gs) {
     return (bits == 2 && (gs == 64 || gs == 128)) ||
            ((bits == 4 || bits == 8) && (gs == 32 || gs == 64 || gs == 128));
 }
+// ... and of the arena arrays a layer accepts: 3-bit projections run on the
+// prefill (tcgen05) kernels at every token count
+bool quant_ok(int bits, int gs) { return gemv_ok(bits, gs) || (bits == 3 && (gs == 32 || gs == 64 || gs == 128)); }
 
 size_t al(size_t v) { return (v + 255) & ~size_t(255); }
 
@@ -133,7 +137,7 @@ int check_proj(const lmoe_qproj &p, int rows, int cols) {
     } else if (!p.weight || !p.scales || !p.biases) {
         return LMOE_EINVAL;
     }
-    if (!gemv_ok(p.bits, p.group_size)) return LMOE_EUNSUPPORTED;
+    if (!quant_ok(p.bits, p.group_size)) return LMOE_EUNSUPPORTED;
     if (rows % 16 != 0 || cols % p.group_size != 0) return LMOE_EUNSUPPORTED;
     return LMOE_OK;
 }
@@ -331,12 +335,20 @@ bool layer_pf_ok(const lmoe_layer *l) {
            pf_supported(ex.inter, ex.hidden, ex.down.bits, ex.down.group_size, PF_DOWN);
 }
 
+bool layer_gemv_ok(const lmoe_layer *l) {
+    const lmoe_experts &ex = l->experts;
+    return gemv_ok(ex.gate.bits, ex.gate.group_size) && gemv_ok(ex.up.bits, ex.up.group_size) &&
+           gemv_ok(ex.down.bits, ex.down.group_size);
+}
+
 // 1 = prefill grouped GEMM, 0 = decode GEMVs, -1 = the requested path is unavailable
 int choose_path(const lmoe_layer *l, int T, int path) {
-    if (path == LMOE_PATH_DECODE) return 0;
+    const bool dec = layer_gemv_ok(l);
+    if (path == LMOE_PATH_DECODE) return dec ? 0 : -1;
     const bool ok = layer_pf_ok(l);
     if (path == LMOE_PATH_PREFILL) return ok ? 1 : -1;
     if (path != LMOE_PATH_AUTO) return -1;
+    if (!dec) return ok ? 1 : -1;
     return ok && (long)T * l->router.top_k >= (long)LMOE_PREFILL_MIN_ROUTES_PER_EXPERT * l->router.n_experts;
 }
 
@@ -680,6 +692,7 @@ int lmoe_moe_routed(const lmoe_layer *layer, const void *x, int32_t tokens, cons
                     const float *w, void *out, void *workspace, size_t ws_bytes, void *stream) {
     int rc = check_layer(layer);
     if (rc) return rc;
+    if (!layer_gemv_ok(layer)) return LMOE_EUNSUPPORTED;  // the decode GEMVs (2/4/8-bit)
     if (tokens < 0 || (tokens > 0 && (!x || !idx || !w || !out || !workspace))) return LMOE_EINVAL;
     if (tokens == 0) return LMOE_OK;
     const Layout L = layer_layout(layer, tokens);
@@ -718,6 +731,7 @@ int lmoe_gateup_swiglu(const lmoe_experts *experts, const void *x, int32_t token
     int rc = check_proj(experts->gate, experts->inter, experts->hidden);
     if (!rc) rc = check_proj(experts->up, experts->inter, experts->hidden);
     if (rc) return rc;
+    if (!gemv_ok(experts->gate.bits, experts->gate.group_size)) return LMOE_EUNSUPPORTED;
     if (experts->gate.bits != experts->up.bits || experts->gate.group_size != experts->up.group_size)
         return LMOE_EUNSUPPORTED;
     if (tokens < 0 || top_k < 1) return LMOE_EINVAL;
@@ -767,6 +781,7 @@ int lmoe_gather_qmm(const lmoe_qproj *proj, int32_t n_slots, int32_t rows, int32
     if (!proj || n_slots < 1 || rows <= 0 || cols <= 0 || routes < 0) return LMOE_EINVAL;
     if (dtype != LMOE_BF16 && dtype != LMOE_F16) return LMOE_EUNSUPPORTED;
     int rc = check_proj(*proj, rows, cols);
+    if (!rc && !gemv_ok(proj->bits, proj->group_size)) rc = LMOE_EUNSUPPORTED;
     if (rc) return rc;
     if (routes == 0) return LMOE_OK;
     if (!x || !slots || !y || !workspace) return LMOE_EINVAL;

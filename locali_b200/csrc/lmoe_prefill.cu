@@ -259,7 +259,7 @@ struct Pf2<__half> {
 // other widths shift each pair down first (p = 0).
 template <typename TA, int BITS>
 struct PfCodes {
-    static constexpr int kPairs = 16 / BITS;
+    static constexpr int kPairs = BITS == 3 ? 16 : 16 / BITS;  // pairs per word (3-bit: per 3-word span)
     static constexpr bool kPrescale = (BITS == 2) && std::is_same<TA, __nv_bfloat16>::value;
     struct W {
         uint32_t w0, w6, w12;
@@ -292,6 +292,28 @@ struct PfCodes {
     }
 };
 
+// Exact codes of packed pair pi of a half stage row (64 codes in `words`).
+// Positions (2 pi, 2 pi + 1) hold (c_m, c_{m + n/2}) of the pi-th span of n
+// columns: one word of 32/bits codes, or for 3-bit (a continuous LSB-first
+// bit stream, 8 codes per 3 bytes) a 3-word span of 32 codes, whose codes
+// are cut out with funnel shifts.
+template <typename TA, int BITS, int HW>
+__device__ __forceinline__ uint32_t pf_pair(const uint32_t (&words)[HW], int pi) {
+    using C = PfCodes<TA, BITS>;
+    using P = Pf2<TA>;
+    if constexpr (BITS == 3) {
+        const int sp = pi >> 4, m = pi & 15;
+        const uint32_t w0 = words[3 * sp], w1 = words[3 * sp + 1], w2 = words[3 * sp + 2];
+        const int bl = 3 * m, bh = 3 * m + 48;
+        const uint32_t lo = bl < 32 ? __funnelshift_r(w0, w1, bl) : __funnelshift_r(w1, w2, bl - 32);
+        const uint32_t hi = bh < 64 ? __funnelshift_r(w1, w2, bh - 32) : (w2 >> (bh - 64));
+        const uint32_t v = (lo & 7u) | ((hi & 7u) << 16) | P::kMagic;
+        return P::fma2(v, P::kOne, P::kNegMagic);
+    } else {
+        return C::q(C::prep(words[pi / C::kPairs]), pi % C::kPairs);
+    }
+}
+
 // Weight stream of one block: the producer warp moves the codes of both
 // 128-row blocks, stage by stage, into a ring of CR stages, and their scales
 // and biases, 8 groups at a time, into a ring of 2 blocks (2-D TMA copies,
@@ -301,7 +323,7 @@ template <int BITS, int GS>
 struct PfRing {
     static constexpr int CB = 16 * BITS;  // code bytes of one row per stage
     static constexpr int SPB = GS / 16;   // stages per block of 8 groups
-    static constexpr int RING = BITS == 2 ? 32 * 1024 : (BITS == 4 ? 48 * 1024 : 64 * 1024);
+    static constexpr int RING = BITS == 2 ? 32 * 1024 : (BITS == 8 ? 64 * 1024 : 48 * 1024);
     static constexpr int CR = RING / (2 * kPfM * CB);
     static_assert(CR >= 2 && SPB >= 2, "rings");
 };
@@ -313,7 +335,7 @@ constexpr int pf_smem_bytes() {
 
 // Panel position of column f for a projection quantised with `bits`.
 __host__ __device__ __forceinline__ int pf_perm_pos(int f, int bits) {
-    const int n = 32 / bits, h = n >> 1;
+    const int n = bits == 3 ? 32 : 32 / bits, h = n >> 1;
     const int base = f - f % n, c = f % n;
     return c < h ? base + 2 * c : base + 2 * (c - h) + 1;
 }
@@ -338,6 +360,15 @@ __device__ __forceinline__ uint4 pf_perm_chunk(const uint16_t *row64, int h) {
         o.y = __byte_perm(l0, h0, 0x7632);
         o.z = __byte_perm(l1, h1, 0x5410);
         o.w = __byte_perm(l1, h1, 0x7632);
+    } else if constexpr (BITS == 3) {
+        // span of 32: (2m, 2m+1) <- (m, m + 16); chunk h holds m = 4 (h % 4) .. + 3
+        const uint16_t *sp = row64 + (h >> 2) * 32 + (h & 3) * 4;
+        const uint2 lo = *reinterpret_cast<const uint2 *>(sp);
+        const uint2 hi = *reinterpret_cast<const uint2 *>(sp + 16);
+        o.x = __byte_perm(lo.x, hi.x, 0x5410);
+        o.y = __byte_perm(lo.x, hi.x, 0x7632);
+        o.z = __byte_perm(lo.y, hi.y, 0x5410);
+        o.w = __byte_perm(lo.y, hi.y, 0x7632);
     } else if constexpr (BITS == 4) {
         // span of 8: (2m, 2m+1) <- (m, m + 4)
         const uint4 v = *reinterpret_cast<const uint4 *>(row64 + h * 8);
@@ -423,7 +454,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
     using P = Pf2<TA>;
     constexpr int HW = RG::CB / 8;           // code words of half a row per stage (64 weights)
     constexpr int CPW = 32 / BITS;           // codes per word
-    static_assert(HW * C::kPairs == 32, "half a stage row is 64 weights");
+    static_assert(HW * 32 / BITS == 64, "half a stage row is 64 weights");
     constexpr bool kF16 = std::is_same<TA, __half>::value;
     constexpr int CSTAGE = 2 * kPfM * RG::CB;  // code bytes of one ring stage
 
@@ -649,13 +680,22 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
                     break;
                 }
                 uint32_t words[HW];
+                if constexpr (HW % 4 == 0) {
 #pragma unroll
-                for (int i = 0; i < HW / 4; ++i) {
-                    const uint4 v = lds128(crow + (uint32_t)(cs * CSTAGE + 16 * i));
-                    words[4 * i] = v.x;
-                    words[4 * i + 1] = v.y;
-                    words[4 * i + 2] = v.z;
-                    words[4 * i + 3] = v.w;
+                    for (int i = 0; i < HW / 4; ++i) {
+                        const uint4 v = lds128(crow + (uint32_t)(cs * CSTAGE + 16 * i));
+                        words[4 * i] = v.x;
+                        words[4 * i + 1] = v.y;
+                        words[4 * i + 2] = v.z;
+                        words[4 * i + 3] = v.w;
+                    }
+                } else {  // 3-bit: 24 bytes
+#pragma unroll
+                    for (int i = 0; i < HW / 2; ++i) {
+                        const uint2 v = lds64(crow + (uint32_t)(cs * CSTAGE + 8 * i));
+                        words[2 * i] = v.x;
+                        words[2 * i + 1] = v.y;
+                    }
                 }
                 const int s = g % kPfSS;
                 if (!pf_wait(&empty[s], ((g / kPfSS) & 1) ^ 1)) {
@@ -691,9 +731,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
                     uint32_t pr[8];
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
-                        const int pi = blk * 8 + i, u = pi / C::kPairs, m = pi % C::kPairs;
-                        const int gg = NG == 2 ? (u * CPW) / GS : 0;
-                        pr[i] = P::fma2(C::q(C::prep(words[u]), m), sp[gg][C::pexp(m)], b2[gg]);
+                        // span of the pair: one word (3-bit: 3 words of 32 codes)
+                        constexpr int SC = BITS == 3 ? 32 : CPW;
+                        const int pi = blk * 8 + i;
+                        const int gg = NG == 2 ? ((pi / (SC / 2)) * SC) / GS : 0;
+                        pr[i] = P::fma2(pf_pair<TA, BITS, HW>(words, pi), sp[gg][C::pexp(pi % C::kPairs)], b2[gg]);
                     }
                     tmem_st8(adst + (uint32_t)(8 * blk), pr);
                 }
@@ -858,6 +900,9 @@ cudaError_t launch_pf_bits(int bits, int gs, const PfArgs &a, cudaStream_t st) {
 #define LMOE_PF_CASE(B, G) \
     if (bits == B && gs == G) return launch_pf_t<TA, B, G, MODE>(a, st);
     LMOE_PF_CASE(2, 64)
+    LMOE_PF_CASE(3, 32)
+    LMOE_PF_CASE(3, 64)
+    LMOE_PF_CASE(3, 128)
     LMOE_PF_CASE(2, 128)
     LMOE_PF_CASE(4, 32)
     LMOE_PF_CASE(4, 64)
@@ -917,7 +962,7 @@ cudaError_t pf_prepare(PfArgs &a, int mode, const QView &q0, const QView &q1, in
 // K a multiple of 64 and of 8 groups (16-byte scale blocks), rows a multiple
 // of 128 (gate/up) or 256 (down), and a compiled (bits, group) pair.
 bool pf_supported(int K, int rows, int bits, int gs, int mode) {
-    const bool bg = (bits == 2 && (gs == 64 || gs == 128)) ||
+    const bool bg = (bits == 2 && (gs == 64 || gs == 128)) || (bits == 3 && (gs == 32 || gs == 64 || gs == 128)) ||
                     ((bits == 4 || bits == 8) && (gs == 32 || gs == 64 || gs == 128));
     if (!bg) return false;
     if (K <= 0 || K % kPfKS != 0 || K % (8 * gs) != 0) return false;  // (kPfKS = 128)
@@ -929,6 +974,7 @@ cudaError_t launch_pf_panel(const PfPanelArgs &a, int max_chunks, cudaStream_t s
     const int atoms = a.K / 64;
     dim3 grid(static_cast<unsigned>(max_chunks), static_cast<unsigned>((atoms + kPfPanelAtoms - 1) / kPfPanelAtoms));
     if (a.bits == 2) return launch_pdl(pf_panel_kernel<2>, grid, dim3(256), 0, st, a);
+    if (a.bits == 3) return launch_pdl(pf_panel_kernel<3>, grid, dim3(256), 0, st, a);
     if (a.bits == 4) return launch_pdl(pf_panel_kernel<4>, grid, dim3(256), 0, st, a);
     if (a.bits == 8) return launch_pdl(pf_panel_kernel<8>, grid, dim3(256), 0, st, a);
     return cudaErrorInvalidValue;

@@ -136,9 +136,13 @@ class ExpertArrays:
         return self.gate.scales.dtype
 
     def pack_tiles(self, slot_begin: int = 0, slot_count: int | None = None) -> "ExpertArrays":
-        """Pre-tile all three projections (see :meth:`QProjArrays.pack_tiles`)."""
+        """Pre-tile the projections that have a tile layout (see
+        :meth:`QProjArrays.pack_tiles`; 3-bit rows have none: those
+        projections run on the prefill kernels, which read the row-major
+        arrays)."""
         for q in (self.gate, self.up, self.down):
-            q.pack_tiles(slot_begin, slot_count)
+            if q.tile_bytes():
+                q.pack_tiles(slot_begin, slot_count)
         return self
 
     def ctype(self) -> _lib.Experts:

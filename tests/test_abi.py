@@ -48,7 +48,7 @@ def test_workspace_size_and_validation(built):
     n64 = lib.lmoe_workspace_size(ctypes.byref(L), 64)
     assert 0 < n1 < n64
     # unsupported bit width / group size
-    assert lib.lmoe_workspace_size(ctypes.byref(_layer(bits=3)), 1) == 0
+    assert lib.lmoe_workspace_size(ctypes.byref(_layer(bits=5)), 1) == 0
     assert lib.lmoe_workspace_size(ctypes.byref(_layer(bits=2, gs=32)), 1) == 0
     # top_k > n_experts
     assert lib.lmoe_workspace_size(ctypes.byref(_layer(E=4, k=6)), 1) == 0
@@ -129,3 +129,18 @@ def test_prefill_path_selection(built):
     rc = lib.lmoe_moe_layer_path(ctypes.byref(L), 256, 512, 256, None, None, 256, small, None, P["prefill"], None,
                                  None)
     assert rc == _lib.LMOE_EWORKSPACE
+
+
+def test_three_bit_layers_take_the_prefill_path(built):
+    """3-bit projections have no decode GEMV: AUTO sizes (and takes) the
+    prefill path at any token count; DECODE reports them unsupported."""
+    lib = _lib.lmoe()
+    P = _lib.PATH
+    L3 = _layer(bits=3)
+    ws = lambda layer, T, p: lib.lmoe_workspace_size_path(ctypes.byref(layer), T, P[p])  # noqa: E731
+    assert ws(L3, 1, "decode") == 0
+    assert ws(L3, 1, "auto") >= ws(L3, 1, "prefill") > 0
+    big = 1 << 40
+    rc = lib.lmoe_moe_layer_path(ctypes.byref(L3), 256, 1, 256, None, None, 256, big, None, P["decode"], None, None)
+    assert rc == _lib.LMOE_EUNSUPPORTED
+    assert lib.lmoe_tile_bytes(2048, 4096, 3, 64) == 0  # no tile layout for 3-bit rows

@@ -96,3 +96,16 @@ def test_oracle_hash_router_weights():
     assert np.array_equal(idx, hidx)
     g = np.take_along_axis(scores, hidx, axis=-1)
     np.testing.assert_allclose(w, 2.0 * g / (g.sum(-1, keepdims=True) + 1e-20), rtol=1e-6)
+
+
+def test_oracle_three_bit_stream_layout():
+    """3-bit rows are one LSB-first bit stream (MLX packs 8 codes per 3 bytes):
+    element j at bits [3j, 3j+3) of the row's little-endian bytes."""
+    rng = np.random.default_rng(1)
+    c = rng.integers(0, 8, (4, 96)).astype(np.uint8)
+    w = O.pack_codes(c, 3)
+    assert w.shape == (4, 9)
+    assert np.array_equal(O.unpack_codes(w, 3, 96), c)
+    bits = np.unpackbits(w.view(np.uint8).reshape(4, -1), axis=1, bitorder="little")
+    for j in (0, 10, 11, 21, 31, 95):
+        assert int(bits[2, 3 * j] + 2 * bits[2, 3 * j + 1] + 4 * bits[2, 3 * j + 2]) == c[2, j]

@@ -66,7 +66,8 @@ def _check(cfg, T, seed=0, dtype=torch.bfloat16, tokens=None):
     return err_r, err_e
 
 
-@pytest.mark.parametrize("bits,gs", [(2, 64), (2, 128), (4, 32), (4, 64), (4, 128), (8, 32), (8, 64), (8, 128)])
+@pytest.mark.parametrize("bits,gs", [(2, 64), (2, 128), (3, 32), (3, 64), (3, 128), (4, 32), (4, 64), (4, 128),
+                                     (8, 32), (8, 64), (8, 128)])
 def test_prefill_layer_bits(built, bits, gs):
     # the prefill kernels stream scales in blocks of 8 groups: K % (8 * gs) == 0
     inter = 1024 if gs == 128 else 512
@@ -160,3 +161,33 @@ def test_prefill_c3_sampled_tokens(built):
     kernels, 4 tokens checked against the oracle."""
     cfg = synth.config("c3")
     _check(cfg, cfg.tokens, seed=0, tokens=[0, 1111, 2222, 4095])
+
+
+@pytest.mark.parametrize("T", [1, 5])
+def test_three_bit_layer_any_batch(built, T):
+    """3-bit codes (MLX's continuous LSB-first bit stream, 8 codes per 3 bytes)
+    run on the tcgen05 kernels at every token count: AUTO takes that path even
+    for decode batches, and the decode path reports them unsupported."""
+    cfg = synth.config("c0", bits_gate=3, bits_up=3, bits_down=3)
+    layer = synth.make_layer(cfg, seed=40 + T, device="cuda")
+    x = synth.make_tokens(cfg, T, seed=50 + T, device="cuda")
+    kern = ops.MoEKernel(layer.router, layer.experts, layer.expert_slot, cfg.swiglu_limit, "fused")
+    idx = torch.empty((T, cfg.top_k), dtype=torch.int32, device="cuda")
+    w = torch.empty((T, cfg.top_k), dtype=torch.float32, device="cuda")
+    out = kern(x, idx=idx, w=w)
+    torch.cuda.synchronize()
+    kern.ws.check()
+    L = layer_np(layer)
+    gi, gw = t2np(idx).astype(np.int64), t2np(w)
+    ref_r = O.moe_layer(t2np(x), L, idx=gi, w=gw, weights="rounded")["out"]
+    ref_e = O.moe_layer(t2np(x), L, idx=gi, w=gw, weights="exact")["out"]
+    assert O.rel_l2(t2np(out), ref_r) < ROUNDED_TOL
+    assert O.rel_l2(t2np(out), ref_e) < LAYER_TOL
+    dec = ops.MoEKernel(layer.router, layer.experts, layer.expert_slot, cfg.swiglu_limit, "fused", path="decode")
+    with pytest.raises(Exception):
+        dec(x)
+
+
+def test_three_bit_mixed_with_four_bit_down(built):
+    cfg = synth.config("c0", bits_gate=3, bits_up=3, bits_down=4, zipf=True)
+    _check(cfg, 72, seed=61)
