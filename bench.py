@@ -66,6 +66,8 @@ def parse():
     p.add_argument("--kernel-steps", type=int, default=200)
     p.add_argument("--cpu-sample", type=int, default=24, help="decode steps timed for the CPU baseline")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--path", choices=["auto", "decode", "prefill"], default="auto",
+                   help="expert-product path of the main workload (lmoe_moe_layer_path)")
     p.add_argument("--prefill-steps", type=int, default=20,
                    help="timed C3 prefill steps reported in the line's 'prefill' object (0 = skip; N=1 only)")
     p.add_argument("--ep", action="store_true",
@@ -270,7 +272,7 @@ def run_ours(args):
     if args.layout == "tiled":
         for l in layers:
             l.experts.pack_tiles()
-    kerns = [ops.MoEKernel(l.router, l.experts, l.expert_slot, cfg.swiglu_limit) for l in layers]
+    kerns = [ops.MoEKernel(l.router, l.experts, l.expert_slot, cfg.swiglu_limit, path=args.path) for l in layers]
     K, W = args.steps, args.warmup
     g = torch.Generator(device=dev).manual_seed(77 + rank)
     xs = torch.randn((K + W, T, cfg.hidden), generator=g, device=dev).to(torch.bfloat16)
