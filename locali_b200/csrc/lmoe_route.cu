@@ -414,6 +414,121 @@ __device__ void topk_token(const float *partial, const float2 *scores, int kspli
     }
 }
 
+// Routing of a single token by the whole 256-thread block (decode batch 1),
+// from precomputed (score, score + bias).  Selection: the top_k-th largest of
+// the 8 warp maxima (top_k <= 8; otherwise -inf) is a threshold that at least
+// top_k experts reach, so every winner is at or above it.  The experts there
+// are gathered in shared memory and each counts the candidates that beat it
+// (biased score higher, ties to the lower id): that count is its position in
+// topk_token's selection order, so the winners, their order, the fp32 weight
+// sum in that order and the weights are topk_token's bit for bit.
+// With `disp` the block also writes dispatch_warp's output for these top_k
+// distinct experts: routes sorted by expert id, one chunk of one route each.
+__device__ void route_one_token(const RouterArgs &a, const int *s_slot, bool disp) {
+    constexpr int kMaxE = 512;
+    __shared__ float s_wmax[8];
+    __shared__ float s_cb[kMaxE], s_cs[kMaxE];
+    __shared__ int s_ce[kMaxE];
+    __shared__ int s_nc;
+    __shared__ float s_ws[16];
+    __shared__ int s_we[16];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int E = a.E, top_k = a.top_k;
+    float bs[2], sc[2];
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+        const int e = tid + 256 * q;
+        bs[q] = -INFINITY;
+        sc[q] = 0.0f;
+        if (e < E) {
+            const float2 v = __ldcg(a.scores + e);
+            sc[q] = v.x;
+            bs[q] = v.y;
+        }
+    }
+    if (tid == 0) s_nc = 0;
+    if (tid < 16) s_we[tid] = -1;
+    float m = fmaxf(bs[0], bs[1]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(LMOE_FULL, m, o));
+    if (lane == 0) s_wmax[warp] = m;
+    __syncthreads();
+    float tau = -INFINITY;
+    if (top_k <= 8) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float wi = s_wmax[i];
+            int ge = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) ge += s_wmax[j] >= wi;
+            if (ge >= top_k) tau = fmaxf(tau, wi);
+        }
+    }
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+        const int e = tid + 256 * q;
+        const bool cand = e < E && bs[q] >= tau;
+        const unsigned bal = __ballot_sync(LMOE_FULL, cand);
+        int base = 0;
+        if (lane == 0 && bal) base = atomicAdd(&s_nc, __popc(bal));
+        base = __shfl_sync(LMOE_FULL, base, 0);
+        if (cand) {
+            const int pos = base + __popc(bal & ((1u << lane) - 1u));
+            s_cb[pos] = bs[q];
+            s_cs[pos] = sc[q];
+            s_ce[pos] = e;
+        }
+    }
+    __syncthreads();
+    const int nc = s_nc;
+    for (int c = tid; c < nc; c += blockDim.x) {
+        const float mb = s_cb[c];
+        const int me = s_ce[c];
+        int r = 0;
+        for (int i = 0; i < nc; ++i) {
+            const float ob = s_cb[i];
+            r += (ob > mb) || (ob == mb && s_ce[i] < me);
+        }
+        if (r < top_k) {
+            s_ws[r] = s_cs[c];
+            s_we[r] = me;
+        }
+    }
+    __syncthreads();
+    if (warp != 0 || lane >= top_k) return;
+    float ssum = 0.0f;  // fp32, in selection order
+    for (int j = 0; j < top_k; ++j) ssum += s_ws[j];
+    const float my_s = s_ws[lane];
+    const int my_e = s_we[lane];
+    float wv = a.norm_topk ? my_s / (ssum + 1e-20f) : my_s;
+    wv *= a.scaling;
+    a.idx_ws[lane] = my_e;
+    a.w_ws[lane] = wv;
+    if (a.idx_user) a.idx_user[lane] = my_e;
+    if (a.w_user) a.w_user[lane] = wv;
+    if (!disp) return;
+    int pos = 0;
+    for (int j = 0; j < top_k; ++j) pos += s_we[j] < my_e;
+    int slot = 0;
+    if (my_e < 0 || my_e >= E) {
+        set_error(a.err, -3);
+    } else {
+        slot = s_slot[my_e];
+        if (slot < 0 || slot >= a.din.n_slots) {
+            set_error(a.err, -3);
+            slot = 0;
+        }
+    }
+    a.dout.sorted_routes[pos] = lane;
+    Chunk ch;
+    ch.slot = slot;
+    ch.route_start = pos;
+    ch.ntok = 1;
+    ch.expert = my_e;
+    a.dout.chunks[pos] = ch;
+    if (lane == 0) *a.dout.n_chunks = top_k;
+}
+
 template <typename TA>
 __device__ __forceinline__ float act_to_f(uint16_t v) {
     return Act<TA>::to_f(v);
@@ -463,6 +578,17 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
     // the preceding kernels
     pdl_wait();
     pdl_trigger();
+    // the expert -> slot table for the finishing block's small dispatch
+    // (every block loads it; one uses it)
+    const bool warp_disp = a.finish && a.do_dispatch && a.din.R <= 32 && a.E <= kDispatchSmallMaxRoutes;
+    int slot_pre[2] = {0, 0};
+    if (warp_disp) {
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+            const int e = tid + 256 * q;
+            if (e < a.E) slot_pre[q] = a.din.expert_slot ? __ldg(a.din.expert_slot + e) : e;
+        }
+    }
     if (a.zero) {
         const int nb = gridDim.x * gridDim.y;
         for (int i = (blockIdx.y * gridDim.x + blockIdx.x) * blockDim.x + tid; i < a.zero_words; i += nb * blockDim.x)
@@ -625,13 +751,19 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
     if (!s_last) return;
     __threadfence();
     if (tid == 0) *a.counter = 0u;
-    // small dispatch: the winners and the expert -> slot table go through
-    // shared memory (the slot table load overlaps the top-k)
-    const bool warp_disp = a.do_dispatch && a.din.R <= 32 && a.E <= kDispatchSmallMaxRoutes;
+    // small dispatch: the winners and the expert -> slot table (loaded at
+    // the kernel start) go through shared memory
     int *s_idx = s_disp;                              // [32]
     int *s_slot = s_disp + 32;                        // [E]
-    if (warp_disp)
-        for (int e = tid; e < a.E; e += blockDim.x) s_slot[e] = a.din.expert_slot ? a.din.expert_slot[e] : e;
+    if (warp_disp) {
+        if (tid < a.E) s_slot[tid] = slot_pre[0];
+        if (tid + 256 < a.E) s_slot[tid + 256] = slot_pre[1];
+        __syncthreads();
+    }
+    if (a.T == 1 && a.scores && !a.hash_idx && a.E <= 512 && a.top_k <= 16) {
+        route_one_token(a, s_slot, warp_disp);
+        return;
+    }
     for (int tok = warp; tok < a.T; tok += 8)
         topk_token(a.partial, a.scores, 1, a.T, a.E, tok, a.bias, a.scoring, a.top_k, a.norm_topk, a.scaling,
                    a.idx_ws, a.w_ws, a.idx_user, a.w_user, warp_disp ? s_idx : nullptr, a.hash_idx);
