@@ -261,8 +261,13 @@ int run_experts(const lmoe_layer *l, const Layout &L, void *ws, int T, const flo
     dn.top_k = k;
     dn.counters = at<uint32_t>(ws, L.cnt);
     dn.combined = static_cast<uint16_t *>(out);
-    return cuda_rc(launch_gemv(MODE_DOWN, ex.dtype == LMOE_F16, ex.down.bits, ex.down.group_size, dn,
-                               L.max_chunks, st));
+    dn.n_tok = T;
+    // Few tokens: blocks own row pairs and combine locally (no device-wide
+    // counters or fences at the tail).  More tokens: row tiles spread over
+    // every SM and the counter-based combine.
+    const int mode = (T <= kDown2MaxTokens && H % 32 == 0 && down2_grid(H / 32) > 0) ? MODE_DOWN2 : MODE_DOWN;
+    if (mode == MODE_DOWN2) dn.q1 = dn.q0;
+    return cuda_rc(launch_gemv(mode, ex.dtype == LMOE_F16, ex.down.bits, ex.down.group_size, dn, L.max_chunks, st));
 }
 
 // Prefill path over an already dispatched layer (chunks of at most kPfNmax

@@ -96,7 +96,10 @@ __device__ __forceinline__ void trace_point(const GemvArgs &a, int it, int point
 template <typename TA, int BITS, int GS, int MODE>
 __global__ void __launch_bounds__(kGemvMaxThreads, 1) gemv_kernel(const GemvArgs a, const GemvCfg c) {
     using Gm = Geo<BITS, GS>;
-    constexpr bool PAIR = (MODE == MODE_GATEUP);
+    // MODE_DOWN2: a unit is two adjacent row tiles of one projection, held
+    // as the two matrices of the paired layout
+    constexpr bool PAIRT = (MODE == MODE_DOWN2);
+    constexpr bool PAIR = (MODE == MODE_GATEUP) || PAIRT;
     constexpr int NM = PAIR ? 2 : 1;
     constexpr int NROW = 2 * NM;
     constexpr int WPS = Gm::kWps;
@@ -117,6 +120,7 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) gemv_kernel(const GemvArgs
     const int K = a.q0.cols;
     const int rows = a.q0.rows;
     const int RT = rows >> 4;
+    const int UT = PAIRT ? RT / 2 : RT;  // row positions of a chunk's units
     const int GT = K / GS;
 
     if (threadIdx.x == 0) {
@@ -149,7 +153,7 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) gemv_kernel(const GemvArgs
     pdl_wait();
     pdl_trigger();
     const int nch = *a.n_chunks;
-    const int units = nch * RT;
+    const int units = nch * UT;
 
     if (warp == c.ncw || warp == c.ncw + 1) {
         // ===================================================== producers
@@ -177,7 +181,7 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) gemv_kernel(const GemvArgs
                     m_w[n] = 0.0f;
                 }
                 if (uj < units) {
-                    const Chunk chj = a.chunks[uj / RT];
+                    const Chunk chj = a.chunks[uj / UT];
                     m_slot = chj.slot;
                     if (m_slot < 0 || m_slot >= a.n_slots) {
                         set_error(a.err, -3);
@@ -207,7 +211,7 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) gemv_kernel(const GemvArgs
                 }
                 break;
             }
-            const int rt = u % RT;  // units run row-tile fastest: a block's consecutive units share a chunk
+            const int rt = u % UT;  // units run row-tile fastest: a block's consecutive units share a chunk
             if (pw == 0) trace_point(a, it, 0);
             const int src = it & 31;
             const int slot = __shfl_sync(LMOE_FULL, m_slot, src);
@@ -262,11 +266,12 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) gemv_kernel(const GemvArgs
                          &full[st]);
             }
             if (pw == 0 && lane == 8 && tiled0)
-                bulk_g2s(sb + c.off_codes, a.q0.tiles + (size_t)slot * a.q0.tile_slot_stride + (size_t)rt * c.TBp,
+                bulk_g2s(sb + c.off_codes,
+                         a.q0.tiles + (size_t)slot * a.q0.tile_slot_stride + (size_t)(PAIRT ? 2 * rt : rt) * c.TBp,
                          static_cast<uint32_t>(c.TBp), &full[st]);
             if (pw == 0 && lane == 9 && tiled1)
                 bulk_g2s(sb + c.off_codes + c.TBp,
-                         a.q1.tiles + (size_t)slot * a.q1.tile_slot_stride + (size_t)rt * c.TBp,
+                         a.q1.tiles + (size_t)slot * a.q1.tile_slot_stride + (size_t)(PAIRT ? 2 * rt + 1 : rt) * c.TBp,
                          static_cast<uint32_t>(c.TBp), &full[st]);
             if (pw == 0) trace_point(a, it, 5);
             // codes: a matrix's 16 rows are one contiguous block of the slot;
@@ -278,7 +283,7 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) gemv_kernel(const GemvArgs
                 const QView &q = m ? a.q1 : a.q0;
                 if (q.tiles) continue;
                 const uint8_t *src = reinterpret_cast<const uint8_t *>(
-                    q.w + (size_t)slot * q.w_slot_stride + (size_t)(rt * 16) * q.words_per_row);
+                    q.w + (size_t)slot * q.w_slot_stride + (size_t)((PAIRT ? 2 * rt + m : rt) * 16) * q.words_per_row);
                 uint8_t *dst = sb + c.off_codes + m * c.TBp;
 #pragma unroll 4
                 for (int i = lane + 32 * pw; i < n16c; i += 64) {
@@ -295,7 +300,8 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) gemv_kernel(const GemvArgs
                 const QView &q = m ? a.q1 : a.q0;
                 if (q.tiles) continue;
                 const uint8_t *src = reinterpret_cast<const uint8_t *>(
-                    (kind ? q.b : q.s) + (size_t)slot * q.sb_slot_stride + (size_t)(rt * 16) * q.groups_per_row);
+                    (kind ? q.b : q.s) + (size_t)slot * q.sb_slot_stride +
+                    (size_t)((PAIRT ? 2 * rt + m : rt) * 16) * q.groups_per_row);
                 uint8_t *dst = sb + (kind ? c.off_b : c.off_s) + m * c.TBp;
                 for (int i = lane; i < n16s; i += 32) {
                     const int o = i << 4;
@@ -448,6 +454,29 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) gemv_kernel(const GemvArgs
                             *reinterpret_cast<float2 *>(a.out_sum16 + ((size_t)r1 * RT + rt) * 2) = make_float2(s1, p1);
                     }
                 }
+            } else if constexpr (MODE == MODE_DOWN2) {
+                // y*w of both row tiles; the block sums each token's k rows
+                // after its last unit (it owns every chunk of these rows)
+#pragma unroll
+                for (int m = 0; m < 2; ++m)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int n = 2 * t + (e & 1);
+                        const int row = (2 * rt + m) * 16 + g + 8 * (e >> 1);
+                        if (n < ntok) {
+                            int route = rr[0];
+                            float wr = rw[0];
+#pragma unroll
+                            for (int q = 0; q < 8; ++q)
+                                if (q == n) {
+                                    route = rr[q];
+                                    wr = rw[q];
+                                }
+                            const float y = Act<TA>::round(fin[m][e]);
+                            const float wv = Act<TA>::round(wr);
+                            a.out[(size_t)route * rows + row] = Act<TA>::from_f(y * wv);
+                        }
+                    }
             } else if constexpr (MODE == MODE_DOWN) {
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
@@ -494,6 +523,31 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) gemv_kernel(const GemvArgs
         }
         if constexpr (MODE == MODE_DOWN) {
             if (list_n > 0) flush();
+        }
+        if constexpr (MODE == MODE_DOWN2) {
+            // Weighted combine of the row pairs this block owns (u = chunk *
+            // UT + pair with gridDim.x dividing UT, so the block ran every
+            // chunk of pairs blockIdx.x + j * gridDim.x): each token's k y*w
+            // rows summed in route order in fp32 and rounded once, the
+            // arithmetic of the MODE_DOWN combine.  Rows written by the other
+            // epilogue warps are read back from L2 after the named barrier.
+            __threadfence_block();
+            asm volatile("bar.sync 1, %0;" ::"r"(kGemvEpi * 32) : "memory");
+            if (!aborted(abort_flag)) {
+                const int own = (UT - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
+                                static_cast<int>(gridDim.x);
+                const int items = own * 32 * a.n_tok;
+                for (int i = ew * 32 + lane; i < items; i += kGemvEpi * 32) {
+                    const int ri = i & 31, rest = i >> 5;
+                    const int tok = rest % a.n_tok, j = rest / a.n_tok;
+                    const int row = (static_cast<int>(blockIdx.x) + j * static_cast<int>(gridDim.x)) * 32 + ri;
+                    float sacc = 0.0f;
+                    for (int r = 0; r < a.top_k; ++r)
+                        sacc += Act<TA>::to_f(__ldcg(reinterpret_cast<const unsigned short *>(
+                            a.out + ((size_t)tok * a.top_k + r) * rows + row)));
+                    a.combined[(size_t)tok * rows + row] = Act<TA>::from_f(sacc);
+                }
+            }
         }
         return;
     }
@@ -791,7 +845,7 @@ static int num_sms() {
 }
 
 bool gemv_config(int mode, int bits, int gs, int K, int ntok_max, GemvCfg *out) {
-    const int NM = mode == MODE_GATEUP ? 2 : 1;
+    const int NM = (mode == MODE_GATEUP || mode == MODE_DOWN2) ? 2 : 1;
     GemvCfg c;
     std::memset(&c, 0, sizeof(c));
     const int GT = K / gs;
@@ -893,6 +947,18 @@ cudaError_t launch_tile_pack(const QView &q, int bits, int gs, int slot_begin, i
     return cudaGetLastError();
 }
 
+// Blocks of a MODE_DOWN2 launch for `pairs` row pairs: the largest divisor of
+// pairs not above the SM count, or 0 when that leaves more than half the SMs
+// idle (the caller then uses MODE_DOWN).
+int down2_grid(int pairs) {
+    const int sms = num_sms();
+    if (pairs < 1) return 0;
+    int g = pairs < sms ? pairs : sms;
+    while (g > 1 && pairs % g != 0) --g;
+    const int want = pairs < sms ? pairs : sms;
+    return 2 * g >= want ? g : 0;
+}
+
 template <typename TA, int BITS, int GS, int MODE>
 static cudaError_t launch_gemv_t(const GemvArgs &a, int max_chunks, cudaStream_t st) {
     GemvCfg c;
@@ -904,10 +970,17 @@ static cudaError_t launch_gemv_t(const GemvArgs &a, int max_chunks, cudaStream_t
         if (e != cudaSuccess) return e;
         configured = c.smem;
     }
-    const long units_max = (long)max_chunks * (a.q0.rows / 16);
     long grid = num_sms();
-    if (grid > units_max) grid = units_max;
-    if (grid < 1) grid = 1;
+    if (MODE == MODE_DOWN2) {
+        // every block owns whole row pairs: the grid divides their number
+        const int pairs = a.q0.rows / 32;
+        grid = down2_grid(pairs);
+        if (grid < 1 || (a.q0.rows & 31) != 0) return cudaErrorInvalidValue;
+    } else {
+        const long units_max = (long)max_chunks * (a.q0.rows / 16);
+        if (grid > units_max) grid = units_max;
+        if (grid < 1) grid = 1;
+    }
     return launch_pdl(kern, dim3(static_cast<unsigned>(grid)), dim3((c.ncw + 2 + kGemvEpi) * 32), c.smem, st, a, c);
 }
 
@@ -932,10 +1005,12 @@ cudaError_t launch_gemv(int mode, int act_f16, int bits, int gs, const GemvArgs 
     if (act_f16) {
         if (mode == MODE_GATEUP) return launch_gemv_bits<__half, MODE_GATEUP>(bits, gs, a, max_chunks, st);
         if (mode == MODE_DOWN) return launch_gemv_bits<__half, MODE_DOWN>(bits, gs, a, max_chunks, st);
+        if (mode == MODE_DOWN2) return launch_gemv_bits<__half, MODE_DOWN2>(bits, gs, a, max_chunks, st);
         return launch_gemv_bits<__half, MODE_QMM>(bits, gs, a, max_chunks, st);
     }
     if (mode == MODE_GATEUP) return launch_gemv_bits<__nv_bfloat16, MODE_GATEUP>(bits, gs, a, max_chunks, st);
     if (mode == MODE_DOWN) return launch_gemv_bits<__nv_bfloat16, MODE_DOWN>(bits, gs, a, max_chunks, st);
+    if (mode == MODE_DOWN2) return launch_gemv_bits<__nv_bfloat16, MODE_DOWN2>(bits, gs, a, max_chunks, st);
     return launch_gemv_bits<__nv_bfloat16, MODE_QMM>(bits, gs, a, max_chunks, st);
 }
 

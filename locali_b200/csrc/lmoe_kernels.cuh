@@ -8,7 +8,9 @@
 
 namespace lmoe {
 
-enum GemvMode { MODE_GATEUP = 0, MODE_DOWN = 1, MODE_QMM = 2 };
+// MODE_DOWN2: down + weighted combine over pairs of row tiles, each block
+// owning whole pairs for every chunk (block-local combine, decode layers)
+enum GemvMode { MODE_GATEUP = 0, MODE_DOWN = 1, MODE_QMM = 2, MODE_DOWN2 = 3 };
 
 // Geometry of one 16-row weight tile as the GEMV consumers read it from
 // shared memory: [codes 16 x RB][scales 16 x SB][biases 16 x SB], padded to
@@ -157,6 +159,7 @@ struct GemvArgs {
     int32_t swiglu_mode;
     const float *route_w;
     int32_t top_k;
+    int32_t n_tok;  // tokens of the layer (MODE_DOWN2 combine)
     uint32_t *counters;
     uint16_t *combined;
     int32_t *err;
@@ -224,6 +227,10 @@ cudaError_t launch_panel(const PanelArgs &a, cudaStream_t st);
 // returns cudaErrorInvalidValue for an unsupported (bits, gs)
 cudaError_t launch_gemv(int mode, int act_f16, int bits, int gs, const GemvArgs &a,
                         int max_chunks, cudaStream_t st);
+// blocks of a MODE_DOWN2 launch over `pairs` row pairs (0: use MODE_DOWN)
+int down2_grid(int pairs);
+// MODE_DOWN2 serves layers of at most this many tokens
+constexpr int kDown2MaxTokens = 16;
 // row-major slots [slot_begin, slot_begin + slot_count) of q -> tiles
 cudaError_t launch_tile_pack(const QView &q, int bits, int gs, int slot_begin, int slot_count, uint8_t *tiles,
                              cudaStream_t st);
