@@ -24,7 +24,8 @@ def _ptr(t: torch.Tensor | None) -> int | None:
 
 
 def _stream() -> int:
-    return torch.cuda.current_stream().cuda_stream
+    """Raw cudaStream_t of the current device's current stream."""
+    return torch._C._cuda_getCurrentRawStream(torch.cuda.current_device())
 
 
 def _event(ev: torch.cuda.Event | None) -> int | None:
@@ -230,6 +231,11 @@ class MoEKernel:
                                self.swiglu_limit, _lib.SWIGLU_MODE[swiglu_mode])
         self.act_dtype = experts.dtype
         self.ws = Workspace(expert_slot.device)
+        # per-call fast path of __call__: the bound entry point, the
+        # descriptor reference, and the (workspace, tokens) last sized for
+        self._layer_fn = lmoe().lmoe_moe_layer_path
+        self._desc_ref = ctypes.byref(self.desc)
+        self._ready: tuple | None = None
 
     def workspace_bytes(self, tokens: int) -> int:
         cache = self.__dict__.setdefault("_ws_bytes", {})
@@ -251,6 +257,22 @@ class MoEKernel:
                  w: torch.Tensor | None = None, hash_idx: torch.Tensor | None = None) -> torch.Tensor:
         """The whole layer.  ``hash_idx`` [T, top_k] selects the experts of
         each token (token-id hash routing) instead of the router's top-k."""
+        if (out is None and idx is None and w is None and hash_idx is None and x.dtype is self.act_dtype
+                and x.dim() == 2 and x.is_cuda and x.is_contiguous()):
+            # steady-state decode call: no reshapes or casts, the workspace
+            # already sized for this token count
+            T = x.shape[0]
+            ready = self._ready
+            if ready is None or ready[0] is not self.ws or ready[1] != T:
+                self.ws.ensure(self.workspace_bytes(T))
+                self._ready = (self.ws, T)
+            buf = self.ws.buf
+            out = torch.empty_like(x)
+            rc = self._layer_fn(self._desc_ref, x.data_ptr(), T, out.data_ptr(), None, None, buf.data_ptr(),
+                                buf.numel(), _stream(), _lib.PATH[self.path], None, None)
+            if rc != _lib.LMOE_OK:
+                check(rc, "lmoe_moe_layer")
+            return out
         flat = self._x(x)
         T = flat.shape[0]
         if out is None:
