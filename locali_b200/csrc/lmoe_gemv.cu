@@ -215,6 +215,32 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) gemv_kernel(const GemvArgs
             if (pw == 0) trace_point(a, it, 0);
             const int src = it & 31;
             const int slot = __shfl_sync(LMOE_FULL, m_slot, src);
+            uint8_t *sb = smem + c.off_stage + (size_t)st * c.stage_bytes;
+            const bool tiled0 = a.q0.tiles != nullptr;
+            const bool tiled1 = NM > 1 && a.q1.tiles != nullptr;
+            // Pre-tiled weight tiles go first: they need only the slot, and
+            // they are most of the stage's bytes.  Their bytes are added to
+            // the stage's transaction count without an arrival, so the stage
+            // cannot complete before the header and activation rows below.
+            // The proxy fence orders the consumers' reads of this slot's last
+            // unit (observed through the empty barrier) before the copies.
+            const uint32_t tile_bytes = static_cast<uint32_t>(((tiled0 ? 1 : 0) + (tiled1 ? 1 : 0)) * c.TBp);
+            if (pw == 0 && tile_bytes) {
+                if (lane == 0) {
+                    fence_proxy_async();
+                    mbar_add_tx(&full[st], tile_bytes);
+                }
+                __syncwarp();
+                if (lane == 8 && tiled0)
+                    bulk_g2s(sb + c.off_codes,
+                             a.q0.tiles + (size_t)slot * a.q0.tile_slot_stride + (size_t)(PAIRT ? 2 * rt : rt) * c.TBp,
+                             static_cast<uint32_t>(c.TBp), &full[st]);
+                if (lane == 9 && tiled1)
+                    bulk_g2s(sb + c.off_codes + c.TBp,
+                             a.q1.tiles + (size_t)slot * a.q1.tile_slot_stride +
+                                 (size_t)(PAIRT ? 2 * rt + 1 : rt) * c.TBp,
+                             static_cast<uint32_t>(c.TBp), &full[st]);
+            }
             const int ntok = __shfl_sync(LMOE_FULL, m_ntok, src);
             int rr[8];
             float ww[8];
@@ -226,24 +252,19 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) gemv_kernel(const GemvArgs
                 if (lane == n) route = rr[n];
             }
             int *hdr = reinterpret_cast<int *>(smem + c.off_shdr + st * kHdrBytes);
-            uint8_t *sb = smem + c.off_stage + (size_t)st * c.stage_bytes;
             // Bulk (TMA) copies for the per-route activation rows (two per
-            // route) and, for pre-tiled projections, one per weight tile;
-            // projections in the plain row-major layout go through 16-byte
-            // cp.async, swizzled into the tile layout on the way.
+            // route); projections in the plain row-major layout go through
+            // 16-byte cp.async, swizzled into the tile layout on the way.
             // The activation rows already in this stage (from its previous
             // unit) are reused when the new unit needs the same rows in the
             // same order: in decode every unit of a chunk reads one row.
-            const bool tiled0 = a.q0.tiles != nullptr;
-            const bool tiled1 = NM > 1 && a.q1.tiles != nullptr;
             const int prow = route >= 0 ? route / a.route_div : -1;
             bool reuse = false;
             if (pw == 0) {
                 const bool same = lane >= ntok || lane >= 8 || hdr[kHdrPanel + lane] == prow;
                 reuse = __all_sync(LMOE_FULL, same) && hdr[kHdrPanelN] == ntok;
             }
-            const uint32_t bulk_bytes = static_cast<uint32_t>((reuse ? 0 : ntok * (c.PB + K / 2)) +
-                                                              ((tiled0 ? 1 : 0) + (tiled1 ? 1 : 0)) * c.TBp);
+            const uint32_t bulk_bytes = static_cast<uint32_t>(reuse ? 0 : ntok * (c.PB + K / 2));
             if (pw == 0 && lane == 0) {
                 hdr[0] = ntok;
                 hdr[1] = rt;
@@ -265,14 +286,6 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) gemv_kernel(const GemvArgs
                 bulk_g2s(sb + c.off_sum + lane * c.S16B, a.sum16 + (size_t)prow * (K / 8), static_cast<uint32_t>(K / 2),
                          &full[st]);
             }
-            if (pw == 0 && lane == 8 && tiled0)
-                bulk_g2s(sb + c.off_codes,
-                         a.q0.tiles + (size_t)slot * a.q0.tile_slot_stride + (size_t)(PAIRT ? 2 * rt : rt) * c.TBp,
-                         static_cast<uint32_t>(c.TBp), &full[st]);
-            if (pw == 0 && lane == 9 && tiled1)
-                bulk_g2s(sb + c.off_codes + c.TBp,
-                         a.q1.tiles + (size_t)slot * a.q1.tile_slot_stride + (size_t)(PAIRT ? 2 * rt + 1 : rt) * c.TBp,
-                         static_cast<uint32_t>(c.TBp), &full[st]);
             if (pw == 0) trace_point(a, it, 5);
             // codes: a matrix's 16 rows are one contiguous block of the slot;
             // consecutive lanes copy consecutive 16-byte chunks (coalesced),
