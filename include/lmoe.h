@@ -172,14 +172,17 @@ int lmoe_moe_layer_staged(const lmoe_layer *layer, const void *x, int32_t tokens
  * weight, as a tensor-core operand) and contracted on the 5th-generation
  * tensor cores; it needs hidden % 256 == 0, inter % 128 == 0, both a multiple
  * of 8 quantisation groups, and row-major arena arrays.  AUTO takes the
- * prefill path when tokens * top_k >= LMOE_PREFILL_MIN_ROUTES_PER_EXPERT *
- * n_experts and the geometry allows it.  No counterpart in the reference's
- * own code; MLX's gather_qmm (dsv4_arena.py:198-221) also changes kernels
- * with the batch size. */
+ * prefill path when the geometry allows it and the routes (tokens * top_k)
+ * reach both LMOE_PREFILL_MIN_ROUTES and LMOE_PREFILL_ROUTES_PER_4_EXPERTS /
+ * 4 * n_experts (measured crossover on B200 at 256 experts, top-6: the two
+ * paths tie at 48 tokens, and the prefill path leads from 64).  No
+ * counterpart in the reference's own code; MLX's gather_qmm
+ * (dsv4_arena.py:198-221) also changes kernels with the batch size. */
 #define LMOE_PATH_AUTO 0
 #define LMOE_PATH_DECODE 1
 #define LMOE_PATH_PREFILL 2
-#define LMOE_PREFILL_MIN_ROUTES_PER_EXPERT 16
+#define LMOE_PREFILL_MIN_ROUTES 256
+#define LMOE_PREFILL_ROUTES_PER_4_EXPERTS 5
 
 /* lmoe_moe_layer_staged on an explicit path (LMOE_PATH_*); LMOE_EUNSUPPORTED
  * when the layer's geometry does not allow the requested path. */

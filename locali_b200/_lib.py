@@ -29,7 +29,14 @@ SCORING = {"sigmoid": 0, "softmax": 1, "sqrtsoftplus": 2}
 SWIGLU_MODE = {"fused": 0, "stock": 1}
 # expert-product path of a layer call (LMOE_PATH_*)
 PATH = {"auto": 0, "decode": 1, "prefill": 2}
-PREFILL_MIN_ROUTES_PER_EXPERT = 16
+PREFILL_MIN_ROUTES = 256
+PREFILL_ROUTES_PER_4_EXPERTS = 5
+
+
+def auto_takes_prefill(tokens: int, top_k: int, n_experts: int) -> bool:
+    """LMOE_PATH_AUTO's choice for a layer where both paths are available."""
+    routes = tokens * top_k
+    return routes >= PREFILL_MIN_ROUTES and 4 * routes >= PREFILL_ROUTES_PER_4_EXPERTS * n_experts
 
 
 class QProj(ctypes.Structure):

@@ -354,7 +354,9 @@ int choose_path(const lmoe_layer *l, int T, int path) {
     if (path == LMOE_PATH_PREFILL) return ok ? 1 : -1;
     if (path != LMOE_PATH_AUTO) return -1;
     if (!dec) return ok ? 1 : -1;
-    return ok && (long)T * l->router.top_k >= (long)LMOE_PREFILL_MIN_ROUTES_PER_EXPERT * l->router.n_experts;
+    const long routes = (long)T * l->router.top_k;
+    return ok && routes >= LMOE_PREFILL_MIN_ROUTES &&
+           4 * routes >= (long)LMOE_PREFILL_ROUTES_PER_4_EXPERTS * l->router.n_experts;
 }
 
 }  // namespace

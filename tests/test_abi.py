@@ -110,8 +110,8 @@ def test_prefill_path_selection(built):
     dec, pre, auto = ws(L, 4096, "decode"), ws(L, 4096, "prefill"), ws(L, 4096, "auto")
     assert dec > 0 and pre > 0 and auto == max(dec, pre)
     assert lib.lmoe_workspace_size(ctypes.byref(L), 4096) == auto
-    # below the AUTO threshold (tokens * top_k < 16 * n_experts) AUTO sizes the decode path
-    assert 8 * 6 < _lib.PREFILL_MIN_ROUTES_PER_EXPERT * 16
+    # below the AUTO threshold AUTO sizes the decode path
+    assert not _lib.auto_takes_prefill(8, 6, 16)
     assert ws(L, 8, "auto") == ws(L, 8, "decode")
     # inter not a multiple of 128: no prefill path, AUTO falls back to decode
     odd = _layer(inter=320)

@@ -17,7 +17,7 @@ import numpy as np
 import pytest
 import torch
 
-from locali_b200 import ops, synth
+from locali_b200 import _lib, ops, synth
 from oracle import moe_oracle as O
 from oracle.bridge import layer_np, t2np
 
@@ -129,7 +129,7 @@ def test_prefill_and_decode_agree(built):
 
 
 def test_prefill_auto_switch_and_workspace_reuse(built):
-    """AUTO takes the prefill path once tokens * top_k >= 16 * n_experts; one
+    """AUTO takes the prefill path once the routes reach its threshold; one
     workspace serves both paths in any order."""
     cfg = synth.config("c0")
     layer = synth.make_layer(cfg, seed=31, device="cuda")
@@ -137,7 +137,7 @@ def test_prefill_auto_switch_and_workspace_reuse(built):
     for T in (4, 96, 1, 300, 8):
         x = synth.make_tokens(cfg, T, seed=40 + T, device="cuda")
         got = auto(x).clone()
-        want_path = "prefill" if T * cfg.top_k >= 16 * cfg.n_experts else "decode"
+        want_path = "prefill" if _lib.auto_takes_prefill(T, cfg.top_k, cfg.n_experts) else "decode"
         fresh = ops.MoEKernel(layer.router, layer.experts, layer.expert_slot, cfg.swiglu_limit, "fused",
                               path=want_path)
         want = fresh(x)

@@ -45,7 +45,8 @@ def test_static_entry_rejects_oversize_without_launching(built):
     assert cap == 8 << 20
     cfg = synth.config("c1")
     layer = synth.make_layer(cfg, seed=1, device="cuda")
-    kern = ops.MoEKernel(layer.router, layer.experts, layer.expert_slot, cfg.swiglu_limit)
+    # the allocation-free entry always runs the decode path: size with it
+    kern = ops.MoEKernel(layer.router, layer.experts, layer.expert_slot, cfg.swiglu_limit, path="decode")
     big = 1
     while kern.workspace_bytes(big) <= cap:
         big *= 2
