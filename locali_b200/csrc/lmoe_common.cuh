@@ -374,6 +374,25 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
     }
 }
 
+// Bulk copy global -> shared with an L2 cache policy (streamed weights use
+// evict-first, so the layer's small hot data keeps its L2 lines).
+__device__ __forceinline__ void bulk_g2s_hint(void *dst, const void *src, uint32_t bytes, uint64_t *bar,
+                                              uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::
+            "r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+// 16-byte read-only global load with an L2 cache policy.
+__device__ __forceinline__ uint4 ldg_u128_hint(const void *p, uint64_t policy) {
+    uint4 v;
+    asm volatile("ld.global.nc.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p), "l"(policy));
+    return v;
+}
+
 // XOR swizzle of 16-byte chunks inside each 128-byte line of a shared-memory
 // tile: rows stay contiguous (so 16-byte cp.async of a row writes whole lines)
 // while the consumers' per-row reads land in distinct bank groups.

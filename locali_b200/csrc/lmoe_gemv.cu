@@ -232,14 +232,15 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) gemv_kernel(const GemvArgs
                 }
                 __syncwarp();
                 if (lane == 8 && tiled0)
-                    bulk_g2s(sb + c.off_codes,
-                             a.q0.tiles + (size_t)slot * a.q0.tile_slot_stride + (size_t)(PAIRT ? 2 * rt : rt) * c.TBp,
-                             static_cast<uint32_t>(c.TBp), &full[st]);
+                    bulk_g2s_hint(sb + c.off_codes,
+                                  a.q0.tiles + (size_t)slot * a.q0.tile_slot_stride +
+                                      (size_t)(PAIRT ? 2 * rt : rt) * c.TBp,
+                                  static_cast<uint32_t>(c.TBp), &full[st], pol);
                 if (lane == 9 && tiled1)
-                    bulk_g2s(sb + c.off_codes + c.TBp,
-                             a.q1.tiles + (size_t)slot * a.q1.tile_slot_stride +
-                                 (size_t)(PAIRT ? 2 * rt + 1 : rt) * c.TBp,
-                             static_cast<uint32_t>(c.TBp), &full[st]);
+                    bulk_g2s_hint(sb + c.off_codes + c.TBp,
+                                  a.q1.tiles + (size_t)slot * a.q1.tile_slot_stride +
+                                      (size_t)(PAIRT ? 2 * rt + 1 : rt) * c.TBp,
+                                  static_cast<uint32_t>(c.TBp), &full[st], pol);
             }
             const int ntok = __shfl_sync(LMOE_FULL, m_ntok, src);
             int rr[8];

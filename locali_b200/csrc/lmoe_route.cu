@@ -558,6 +558,8 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
     const int nchunk = a.H / kRouterKS;
     __shared__ float s_bias[EPB];
     if (tid < EPB) s_bias[tid] = (a.bias && e0 + tid < a.E) ? a.bias[e0 + tid] : 0.0f;
+    // Router weights are read once per layer call: evict-first in L2.
+    const uint64_t wpol = evict_first_policy();
     // Decode (one pass of at most 8 tokens): this warp's first two weight
     // chunks are requested before the panel work so their latency overlaps it.
     const bool one_pass = (tend - tbeg) <= 8;
@@ -569,8 +571,8 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
         for (int i = 0; i < EPB; ++i) {
             wpre[j][i] = make_uint4(0, 0, 0, 0);
             if (one_pass && ch < nchunk && e0 + i < a.E)
-                wpre[j][i] = __ldg(reinterpret_cast<const uint4 *>(a.wg + (size_t)(e0 + i) * a.H + ch * kRouterKS +
-                                                                   lane * 8));
+                wpre[j][i] = ldg_u128_hint(
+                    reinterpret_cast<const uint4 *>(a.wg + (size_t)(e0 + i) * a.H + ch * kRouterKS + lane * 8), wpol);
         }
     }
 
@@ -673,7 +675,7 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
                 } else {
                     wv[i] = make_uint4(0, 0, 0, 0);
                     if (e0 + i < a.E)
-                        wv[i] = __ldg(reinterpret_cast<const uint4 *>(a.wg + (size_t)(e0 + i) * a.H + col));
+                        wv[i] = ldg_u128_hint(reinterpret_cast<const uint4 *>(a.wg + (size_t)(e0 + i) * a.H + col), wpol);
                 }
             }
             uint4 xv[8];
