@@ -265,7 +265,11 @@ int run_experts(const lmoe_layer *l, const Layout &L, void *ws, int T, const flo
     // Few tokens: blocks own row pairs and combine locally (no device-wide
     // counters or fences at the tail).  More tokens: row tiles spread over
     // every SM and the counter-based combine.
-    const int mode = (T <= kDown2MaxTokens && H % 32 == 0 && down2_grid(H / 32) > 0) ? MODE_DOWN2 : MODE_DOWN;
+    GemvCfg d2;
+    const int mode = (T <= kDown2MaxTokens && H % 32 == 0 && down2_grid(H / 32) > 0 &&
+                      gemv_config(MODE_DOWN2, ex.down.bits, ex.down.group_size, I, ntok_max, &d2))
+                         ? MODE_DOWN2
+                         : MODE_DOWN;
     if (mode == MODE_DOWN2) dn.q1 = dn.q0;
     return cuda_rc(launch_gemv(mode, ex.dtype == LMOE_F16, ex.down.bits, ex.down.group_size, dn, L.max_chunks, st));
 }
@@ -340,10 +344,13 @@ bool layer_pf_ok(const lmoe_layer *l) {
            pf_supported(ex.inter, ex.hidden, ex.down.bits, ex.down.group_size, PF_DOWN);
 }
 
+// The decode GEMVs need supported bit widths and, for both projections, a
+// shared-memory plan with at least two stages of one route (the tile layout
+// needs a power-of-two number of 16-byte chunks per code row).
 bool layer_gemv_ok(const lmoe_layer *l) {
     const lmoe_experts &ex = l->experts;
     return gemv_ok(ex.gate.bits, ex.gate.group_size) && gemv_ok(ex.up.bits, ex.up.group_size) &&
-           gemv_ok(ex.down.bits, ex.down.group_size);
+           gemv_ok(ex.down.bits, ex.down.group_size) && layer_chunk(l, 1) >= 1;
 }
 
 // 1 = prefill grouped GEMM, 0 = decode GEMVs, -1 = the requested path is unavailable

@@ -120,6 +120,12 @@ def test_prefill_path_selection(built):
     big = 1 << 40
     rc = lib.lmoe_moe_layer_path(ctypes.byref(odd), 256, 4, 256, None, None, 256, big, None, P["prefill"], None, None)
     assert rc == _lib.LMOE_EUNSUPPORTED
+    # code rows the decode GEMVs cannot stage (7168 x 2 bits: 112 16-byte
+    # chunks; 8192: two stages do not fit): decode unavailable, AUTO = prefill
+    for hidden in (7168, 8192):
+        wide = _layer(hidden=hidden)
+        assert ws(wide, 1, "decode") == 0
+        assert ws(wide, 1, "auto") == ws(wide, 1, "prefill") > 0
     # unknown path value
     assert lib.lmoe_moe_layer_path(ctypes.byref(L), 256, 4, 256, None, None, 256, big, None, 9, None, None) == \
         _lib.LMOE_EUNSUPPORTED

@@ -191,3 +191,27 @@ def test_three_bit_layer_any_batch(built, T):
 def test_three_bit_mixed_with_four_bit_down(built):
     cfg = synth.config("c0", bits_gate=3, bits_up=3, bits_down=4, zipf=True)
     _check(cfg, 72, seed=61)
+
+
+@pytest.mark.parametrize("T", [1, 3])
+def test_wide_hidden_decode_batches_take_tcgen05_path(built, T):
+    """Hidden 7168 (DeepSeek-V3 width): its 2-bit code rows are 112 16-byte
+    chunks, not a power of two, so the decode GEMVs cannot stage them; AUTO
+    runs such layers on the tcgen05 kernels at every token count, and the
+    decode path reports them unsupported."""
+    cfg = synth.config("c0", hidden=7168, inter=512, n_experts=8, bits_gate=2, bits_up=2, bits_down=2)
+    layer = synth.make_layer(cfg, seed=70 + T, device="cuda")
+    x = synth.make_tokens(cfg, T, seed=80 + T, device="cuda")
+    kern = ops.MoEKernel(layer.router, layer.experts, layer.expert_slot, cfg.swiglu_limit, "fused")
+    idx = torch.empty((T, cfg.top_k), dtype=torch.int32, device="cuda")
+    w = torch.empty((T, cfg.top_k), dtype=torch.float32, device="cuda")
+    out = kern(x, idx=idx, w=w)
+    torch.cuda.synchronize()
+    kern.ws.check()
+    L = layer_np(layer)
+    gi, gw = t2np(idx).astype(np.int64), t2np(w)
+    assert O.rel_l2(t2np(out), O.moe_layer(t2np(x), L, idx=gi, w=gw, weights="rounded")["out"]) < ROUNDED_TOL
+    assert O.rel_l2(t2np(out), O.moe_layer(t2np(x), L, idx=gi, w=gw, weights="exact")["out"]) < LAYER_TOL
+    dec = ops.MoEKernel(layer.router, layer.experts, layer.expert_slot, cfg.swiglu_limit, "fused", path="decode")
+    with pytest.raises(Exception):
+        dec(x)
