@@ -192,7 +192,8 @@ def workload_config(cfg, T, world, n_layers, layout):
         "global_batch": T * world, "parallelism": f"replicas{world}" if world > 1 else "single",
         "layers_cycled": n_layers,
         "l2": f"{n_layers} distinct layers cycled; >{4 * 126} MB of expert bytes touched between reuses",
-        "weights": f"{cfg.bits_gate}-bit affine g{cfg.group_size} (uint32 codes, bf16 scales/biases)",
+        "weights": f"gate/up/down {cfg.bits_gate}/{cfg.bits_up}/{cfg.bits_down}-bit affine g{cfg.group_size} "
+                   "(uint32 codes, bf16 scales/biases)",
         "layout": layout,
     }
 
@@ -258,7 +259,7 @@ def run_ours(args):
         torch.cuda.set_device(0)
     dev = torch.device("cuda", torch.cuda.current_device())
 
-    from locali_b200 import ops, synth
+    from locali_b200 import _lib, ops, synth
 
     over = {}
     if args.tokens is not None:
@@ -345,6 +346,12 @@ def run_ours(args):
     layer_bytes = (sum(d * cfg.expert_bytes() for d in distinct) / nk + cfg.router_bytes()
                    + 2 * T * cfg.hidden * 2)
     layer_ms = ms / K
+    # the gate/up kernel the layer ran (AUTO picks by the routes per step)
+    path = args.path
+    if path == "auto":
+        path = "prefill" if _lib.auto_takes_prefill(T, cfg.top_k, cfg.n_experts) else "decode"
+    gu_kernel = ("gemv_kernel<bf16, gate/up>" if path == "decode"
+                 else f"pf_gemm_kernel<bf16, {cfg.bits_gate}, {cfg.group_size}, gate/up> (tcgen05)")
 
     # ---- e2e through the public module API with host buffers
     e2e = None
@@ -374,7 +381,7 @@ def run_ours(args):
         "config": workload_config(cfg, T, world, n_layers, args.layout),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": traffic, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
-                     "kernel": "gemv_kernel<bf16, gate/up>", "algorithmic_bytes_per_launch": gu_bytes},
+                     "kernel": gu_kernel, "algorithmic_bytes_per_launch": gu_bytes},
         "layer_roofline": {"bytes_per_step": layer_bytes, "achieved_gbs": layer_bytes / (layer_ms / 1e3) / 1e9,
                            "frac": layer_bytes / (layer_ms / 1e3) / 1e9 / peak},
         "kernels_us": {"router_dispatch": 1e3 * sum(t_router) / nk, "gateup_swiglu": 1e3 * gu_ms,
