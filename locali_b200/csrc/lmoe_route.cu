@@ -453,16 +453,19 @@ __device__ void route_one_token(const RouterArgs &a, const int *s_slot, bool dis
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(LMOE_FULL, m, o));
     if (lane == 0) s_wmax[warp] = m;
     __syncthreads();
+    // lane i & 7 tests warp maximum i; a max over each group of 8 lanes
+    // gives every lane the threshold (short code: it runs once per layer,
+    // with its instructions fetched cold)
     float tau = -INFINITY;
     if (top_k <= 8) {
+        const float wi = s_wmax[lane & 7];
+        int ge = 0;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const float wi = s_wmax[i];
-            int ge = 0;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) ge += s_wmax[j] >= wi;
-            if (ge >= top_k) tau = fmaxf(tau, wi);
-        }
+        for (int j = 0; j < 8; ++j) ge += s_wmax[j] >= wi;
+        tau = ge >= top_k ? wi : -INFINITY;
+        tau = fmaxf(tau, __shfl_xor_sync(LMOE_FULL, tau, 1));
+        tau = fmaxf(tau, __shfl_xor_sync(LMOE_FULL, tau, 2));
+        tau = fmaxf(tau, __shfl_xor_sync(LMOE_FULL, tau, 4));
     }
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
