@@ -85,19 +85,24 @@ def expert_partials(recv_rows: torch.Tensor, recv_meta: torch.Tensor, k: int,
                     local_fn: Callable[[torch.Tensor, torch.Tensor, torch.Tensor], torch.Tensor]) -> torch.Tensor:
     """Step 4: each received row's routes through the local experts, summed in
     route order in fp32.  ``local_fn(x [R,H], idx [R,1], w [R,1])`` returns the
-    rounded per-route products ``T(T(y)*T(w))`` [R, H]."""
+    rounded per-route products ``T(T(y)*T(w))`` [R, H].  Every local (row,
+    route) pair goes through one ``local_fn`` call; the products are placed
+    at their route position and summed over the routes in order 0..k-1
+    (absent routes add exact zeros)."""
     n, H = recv_rows.shape
     out = torch.zeros((n, H), dtype=torch.float32, device=recv_rows.device)
     if n == 0:
         return out
     loc = recv_meta[:, :k]
     wr = recv_meta[:, k:].contiguous().view(torch.float32)
+    rows, js = (loc >= 0).nonzero(as_tuple=True)
+    if rows.numel() == 0:
+        return out
+    y = local_fn(recv_rows[rows], loc[rows, js].unsqueeze(1), wr[rows, js].unsqueeze(1))
+    per_route = torch.zeros((n, k, H), dtype=torch.float32, device=recv_rows.device)
+    per_route[rows, js] = y.float()
     for j in range(k):  # route order j = 0..k-1, fp32
-        rows = (loc[:, j] >= 0).nonzero(as_tuple=True)[0]
-        if rows.numel() == 0:
-            continue
-        y = local_fn(recv_rows[rows], loc[rows, j].unsqueeze(1), wr[rows, j].unsqueeze(1))
-        out[rows] += y.float()
+        out += per_route[:, j]
     return out
 
 
