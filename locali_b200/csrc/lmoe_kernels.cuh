@@ -180,9 +180,10 @@ struct GemvCfg {
     int32_t off_panel, off_sum, stage_bytes;
     int32_t off_bars, off_shdr, off_rhdr, off_red, off_xs, off_list, off_ptab, off_stage, smem, list_cap;
 };
-// Consumer warps per block: two per SM sub-partition.  Legacy mma.sync
-// throughput per sub-partition falls to less than half when four warps
-// interleave MMAs with the code-extraction ALU work (measured on B200).
+// Consumer warps per block: two per SM sub-partition.  Sixteen (four per
+// sub-partition, register cap 80) made the C1 gate/up GEMV slower on B200
+// (30.5 against 26.7 us): a unit's consumers start together and each warp's
+// mma.sync stream with its code extraction is latency-bound.
 constexpr int kGemvMaxConsumers = 8;
 constexpr int kGemvEpi = 4;  // epilogue warps
 constexpr int kGemvMaxThreads = (kGemvMaxConsumers + 2 + kGemvEpi) * 32;  // + 2 producer warps
