@@ -9,9 +9,9 @@ One layer step:
    of its experts, with its local expert ids there and their combine weights
    (``-1`` / 0 for routes owned elsewhere);
 3. exchange counts, token rows and route metadata (all-to-all);
-4. run the received routes through the local experts (``lmoe_moe_routed``,
-   one route per row) and sum each received row's routes in route order in
-   fp32;
+4. run the received routes through the local experts (one
+   ``lmoe_moe_routed`` call, one route per entry) and sum each received row's
+   routes in route order in fp32;
 5. send the fp32 partial rows home (all-to-all) and add them per token in
    rank order, then round once.
 
@@ -81,21 +81,53 @@ def plan_dispatch(x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, n_experts
     return DispatchPlan(tok, counts, x[tok], meta)
 
 
+def dispatch_counts(idx: torch.Tensor, n_experts: int, world: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per destination rank: the token rows it receives from this rank and
+    the routes those rows carry, as one int64 [world, 2] tensor on the
+    device, together with the token x destination hit mask."""
+    per = n_experts // world
+    owner = idx.to(torch.int64) // per                                            # [T, k]
+    own = owner.unsqueeze(-1) == torch.arange(world, device=idx.device)           # [T, k, world]
+    hits = own.any(1)                                                             # [T, world]
+    return torch.stack([hits.sum(0), own.sum((0, 1))], 1), hits
+
+
+def plan_dispatch_sized(x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, n_experts: int, world: int,
+                        hits: torch.Tensor, send_counts: list[int]) -> DispatchPlan:
+    """plan_dispatch with the per-destination row counts already on the host
+    (no host wait)."""
+    T, k = idx.shape
+    per = n_experts // world
+    idx = idx.to(torch.int64)
+    owner = idx // per
+    dst, tok = torch.nonzero_static(hits.t(), size=sum(send_counts)).unbind(1)
+    own = owner[tok] == dst.unsqueeze(1)
+    local = torch.where(own, idx[tok] - dst.unsqueeze(1) * per, torch.full_like(idx[tok], -1))
+    wsel = torch.where(own, w[tok].to(torch.float32), torch.zeros_like(w[tok], dtype=torch.float32))
+    meta = torch.cat([local.to(torch.int32), wsel.view(torch.int32)], dim=1)
+    return DispatchPlan(tok, list(send_counts), x[tok], meta)
+
+
 def expert_partials(recv_rows: torch.Tensor, recv_meta: torch.Tensor, k: int,
-                    local_fn: Callable[[torch.Tensor, torch.Tensor, torch.Tensor], torch.Tensor]) -> torch.Tensor:
+                    local_fn: Callable[[torch.Tensor, torch.Tensor, torch.Tensor], torch.Tensor],
+                    n_routes: int | None = None) -> torch.Tensor:
     """Step 4: each received row's routes through the local experts, summed in
     route order in fp32.  ``local_fn(x [R,H], idx [R,1], w [R,1])`` returns the
     rounded per-route products ``T(T(y)*T(w))`` [R, H].  Every local (row,
     route) pair goes through one ``local_fn`` call; the products are placed
     at their route position and summed over the routes in order 0..k-1
-    (absent routes add exact zeros)."""
+    (absent routes add exact zeros).  ``n_routes``, the number of local
+    routes when the caller knows it, saves a host wait."""
     n, H = recv_rows.shape
     out = torch.zeros((n, H), dtype=torch.float32, device=recv_rows.device)
     if n == 0:
         return out
     loc = recv_meta[:, :k]
     wr = recv_meta[:, k:].contiguous().view(torch.float32)
-    rows, js = (loc >= 0).nonzero(as_tuple=True)
+    if n_routes is None:
+        rows, js = (loc >= 0).nonzero(as_tuple=True)
+    else:
+        rows, js = torch.nonzero_static(loc >= 0, size=n_routes).unbind(1)
     if rows.numel() == 0:
         return out
     y = local_fn(recv_rows[rows], loc[rows, js].unsqueeze(1), wr[rows, js].unsqueeze(1))
@@ -156,16 +188,21 @@ class ExpertParallelMoE:
         T, H = flat.shape
         idx, w = self.r.route(flat)
         k = idx.shape[1]
-        plan = plan_dispatch(flat, idx, w, self.r.n_experts, self.r.world)
-        send_counts = torch.tensor(plan.send_counts, dtype=torch.int64, device=flat.device)
-        recv_counts = torch.empty_like(send_counts)
-        dist.all_to_all_single(recv_counts, send_counts, group=self.group)
-        rc = recv_counts.tolist()
+        world = self.r.world
+        # rows and routes per destination, exchanged as one [world, 2] tensor;
+        # one host wait then gives every split size of the step
+        cnt, hits = dispatch_counts(idx, self.r.n_experts, world)
+        recv_cnt = torch.empty_like(cnt)
+        dist.all_to_all_single(recv_cnt, cnt, group=self.group)
+        host = torch.cat([cnt.reshape(-1), recv_cnt.reshape(-1)]).tolist()
+        send_counts, rc = host[0:2 * world:2], host[2 * world::2]
+        n_routes = sum(host[2 * world + 1::2])
+        plan = plan_dispatch_sized(flat, idx, w, self.r.n_experts, world, hits, send_counts)
         recv_rows = flat.new_empty((sum(rc), H))
         dist.all_to_all_single(recv_rows, plan.rows, rc, plan.send_counts, group=self.group)
         recv_meta = plan.meta.new_empty((sum(rc), 2 * k))
         dist.all_to_all_single(recv_meta, plan.meta, rc, plan.send_counts, group=self.group)
-        part = expert_partials(recv_rows, recv_meta, k, self.r.local_fn)
+        part = expert_partials(recv_rows, recv_meta, k, self.r.local_fn, n_routes)
         back = part.new_empty((sum(plan.send_counts), H))
         dist.all_to_all_single(back, part, plan.send_counts, rc, group=self.group)
         return combine_home(T, H, plan.tok, back, plan.send_counts, flat.dtype).reshape(x.shape)
