@@ -86,6 +86,31 @@ def test_plan_dispatch_dedupes_tokens_per_rank():
     assert wr[0].tolist() == pytest.approx([0.5, 0.0, 0.2])
 
 
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_sized_plan_equals_plan(world):
+    """The one-wait planner (device-side counts, nonzero_static) builds the
+    same plan as plan_dispatch: rows, their order, metadata and counts; the
+    route counts add up to the local routes each destination receives."""
+    g = torch.Generator().manual_seed(world)
+    E, T, k = 32, 23, 6
+    # at 8 ranks only experts 0..15 are chosen: ranks 4..7 receive no rows
+    pool = 16 if world == 8 else E
+    idx = torch.stack([torch.randperm(pool, generator=g)[:k] for _ in range(T)]).to(torch.int32)
+    w = torch.rand((T, k), generator=g)
+    x = torch.randn((T, 8), generator=g)
+    want = ep.plan_dispatch(x, idx, w, E, world)
+    cnt, hits = ep.dispatch_counts(idx, E, world)
+    send = cnt[:, 0].tolist()
+    got = ep.plan_dispatch_sized(x, idx, w, E, world, hits, send)
+    assert send == want.send_counts
+    assert torch.equal(got.tok, want.tok)
+    assert torch.equal(got.rows, want.rows)
+    assert torch.equal(got.meta, want.meta)
+    per = E // world
+    for d in range(world):
+        assert int(cnt[d, 1]) == int(((idx.long() // per) == d).sum())
+
+
 def test_loopback_matches_distributed_plan():
     cfg, layer = _layer()
     L = layer_np(layer)
