@@ -149,6 +149,34 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) gemv_kernel(const GemvArgs
         }
     }
     __syncthreads();
+    // MODE_DOWN2 with pre-tiled weights: the chunk table was written by the
+    // router, two launches back (the gate/up kernel, which precedes this one,
+    // allowed this launch only after its own wait on the router), and the
+    // weight tiles are static.  So the producer requests the weight tiles of
+    // its first stages before waiting on the gate/up kernel, whose output
+    // (the activation rows) is copied only after the wait.
+    int npre = 0;
+    if constexpr (MODE == MODE_DOWN2) {
+        if (warp == c.ncw && a.q0.tiles) {
+            const int u = static_cast<int>(blockIdx.x) + lane * static_cast<int>(gridDim.x);
+            const bool pre = lane < c.nst && u < *a.n_chunks * UT;
+            if (pre) {
+                int slot = a.chunks[u / UT].slot;
+                if (slot < 0 || slot >= a.n_slots) {
+                    set_error(a.err, -3);
+                    slot = 0;
+                }
+                const int rt = u % UT;
+                uint8_t *sb = smem + c.off_stage + (size_t)lane * c.stage_bytes;
+                const uint8_t *src = a.q0.tiles + (size_t)slot * a.q0.tile_slot_stride + (size_t)(2 * rt) * c.TBp;
+                mbar_add_tx(&full[lane], static_cast<uint32_t>(2 * c.TBp));
+                const uint64_t pol = evict_first_policy();
+                bulk_g2s_hint(sb + c.off_codes, src, static_cast<uint32_t>(c.TBp), &full[lane], pol);
+                bulk_g2s_hint(sb + c.off_codes + c.TBp, src + c.TBp, static_cast<uint32_t>(c.TBp), &full[lane], pol);
+            }
+            npre = __popc(__ballot_sync(LMOE_FULL, pre));
+        }
+    }
     // the chunk table and activations come from the preceding kernels
     pdl_wait();
     pdl_trigger();
@@ -225,7 +253,7 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) gemv_kernel(const GemvArgs
             // The proxy fence orders the consumers' reads of this slot's last
             // unit (observed through the empty barrier) before the copies.
             const uint32_t tile_bytes = static_cast<uint32_t>(((tiled0 ? 1 : 0) + (tiled1 ? 1 : 0)) * c.TBp);
-            if (pw == 0 && tile_bytes) {
+            if (pw == 0 && tile_bytes && it >= npre) {  // stages below npre: requested before the wait
                 if (lane == 0) {
                     fence_proxy_async();
                     mbar_add_tx(&full[st], tile_bytes);
@@ -327,8 +355,11 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) gemv_kernel(const GemvArgs
             if (pw == 0) trace_point(a, it, 1);
         }
         if (aborted(abort_flag)) {
-            // drain: let copies already issued land before the block exits
-            for (int j = (it > c.nst ? it - c.nst : 0); j < it; ++j) mbar_wait(&full[j % c.nst], (j / c.nst) & 1);
+            // drain: let copies already issued (in the loop, or before the
+            // wait on the preceding kernel) land before the block exits
+            const int issued = it > npre ? it : npre;
+            for (int j = (issued > c.nst ? issued - c.nst : 0); j < issued; ++j)
+                mbar_wait(&full[j % c.nst], (j / c.nst) & 1);
         }
         return;
     }
