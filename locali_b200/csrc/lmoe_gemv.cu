@@ -681,6 +681,24 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) gemv_kernel(const GemvArgs
 #pragma unroll
                 for (int e = 0; e < 4; ++e) d[m][e] = 0.0f;
             const uint8_t *panel0 = sb + c.off_panel;
+            // scales and biases of the lane's two group columns (2t, 2t + 1),
+            // read before the MMA loop so their latency hides behind it
+            uint16_t sbr[NM][2][4];
+            {
+                const bool v0 = 2 * t < ng, v1 = 2 * t + 1 < ng;
+#pragma unroll
+                for (int m = 0; m < NM; ++m)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int r = 2 * m + h;
+                        const int os0 = srow[r] + ((2 * (Gbeg + 2 * t)) ^ sfx[r]);
+                        const int os1 = srow[r] + ((2 * (Gbeg + 2 * t + 1)) ^ sfx[r]);
+                        sbr[m][h][0] = v0 ? *reinterpret_cast<const uint16_t *>(sb + c.off_s + os0) : 0;
+                        sbr[m][h][1] = v0 ? *reinterpret_cast<const uint16_t *>(sb + c.off_b + os0) : 0;
+                        sbr[m][h][2] = v1 ? *reinterpret_cast<const uint16_t *>(sb + c.off_s + os1) : 0;
+                        sbr[m][h][3] = v1 ? *reinterpret_cast<const uint16_t *>(sb + c.off_b + os1) : 0;
+                    }
+            }
             // straight-line over the (at most 2 * WPS) 16-byte chunks of a
             // lane: as a rolled loop the compiler keeps too few values live
             // and the MMA issue rate drops several-fold
@@ -722,23 +740,12 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) gemv_kernel(const GemvArgs
             }
             // epilogue: scale, bias and offset correction per group column,
             // then the row sums over the quad's columns
-            const bool v0 = 2 * t < ng, v1 = 2 * t + 1 < ng;
 #pragma unroll
             for (int m = 0; m < NM; ++m) {
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
-                    const int r = 2 * m + h;
-                    const int os0 = srow[r] + ((2 * (Gbeg + 2 * t)) ^ sfx[r]);
-                    const int os1 = srow[r] + ((2 * (Gbeg + 2 * t + 1)) ^ sfx[r]);
-                    float s0 = 0.0f, b0 = 0.0f, s1 = 0.0f, b1 = 0.0f;
-                    if (v0) {
-                        s0 = Act<TA>::to_f(*reinterpret_cast<const uint16_t *>(sb + c.off_s + os0));
-                        b0 = Act<TA>::to_f(*reinterpret_cast<const uint16_t *>(sb + c.off_b + os0));
-                    }
-                    if (v1) {
-                        s1 = Act<TA>::to_f(*reinterpret_cast<const uint16_t *>(sb + c.off_s + os1));
-                        b1 = Act<TA>::to_f(*reinterpret_cast<const uint16_t *>(sb + c.off_b + os1));
-                    }
+                    const float s0 = Act<TA>::to_f(sbr[m][h][0]), b0 = Act<TA>::to_f(sbr[m][h][1]);
+                    const float s1 = Act<TA>::to_f(sbr[m][h][2]), b1 = Act<TA>::to_f(sbr[m][h][3]);
                     float e0 = d[m][2 * h], e1 = d[m][2 * h + 1];
                     if constexpr (OFFSET) {
                         e0 = fmaf(-kM, P0, e0);
