@@ -667,14 +667,7 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) gemv_kernel(const GemvArgs
                         gx.y += w.y;
                     }
                 }
-                gx.x += __shfl_xor_sync(LMOE_FULL, gx.x, 1);
-                gx.y += __shfl_xor_sync(LMOE_FULL, gx.y, 1);
-                gx.x += __shfl_xor_sync(LMOE_FULL, gx.x, 2);
-                gx.y += __shfl_xor_sync(LMOE_FULL, gx.y, 2);
             }
-            // this lane's D columns are n0 = 2t and n1 = 2t + 1
-            const float X0 = __shfl_sync(LMOE_FULL, gx.x, 8 * t), P0 = __shfl_sync(LMOE_FULL, gx.y, 8 * t);
-            const float X1 = __shfl_sync(LMOE_FULL, gx.x, 8 * t + 4), P1 = __shfl_sync(LMOE_FULL, gx.y, 8 * t + 4);
             float d[NM][4];
 #pragma unroll
             for (int m = 0; m < NM; ++m)
@@ -738,6 +731,14 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) gemv_kernel(const GemvArgs
                     }
                 }
             }
+            // the group sums (loaded before the MMA loop) reduced over each
+            // group's 4 lanes; this lane's D columns are n0 = 2t and n1 = 2t + 1
+            gx.x += __shfl_xor_sync(LMOE_FULL, gx.x, 1);
+            gx.y += __shfl_xor_sync(LMOE_FULL, gx.y, 1);
+            gx.x += __shfl_xor_sync(LMOE_FULL, gx.x, 2);
+            gx.y += __shfl_xor_sync(LMOE_FULL, gx.y, 2);
+            const float X0 = __shfl_sync(LMOE_FULL, gx.x, 8 * t), P0 = __shfl_sync(LMOE_FULL, gx.y, 8 * t);
+            const float X1 = __shfl_sync(LMOE_FULL, gx.x, 8 * t + 4), P1 = __shfl_sync(LMOE_FULL, gx.y, 8 * t + 4);
             // epilogue: scale, bias and offset correction per group column,
             // then the row sums over the quad's columns
 #pragma unroll
