@@ -191,6 +191,20 @@ int lmoe_moe_layer_path(const lmoe_layer *layer, const void *x, int32_t tokens,
                         size_t ws_bytes, void *stream, int32_t path,
                         void *ev_routed, void *ev_gateup);
 
+/* The layer with its input and output in page-locked, mapped host memory
+ * (e.g. torch pin_memory(); cudaHostGetDevicePointer must accept both):
+ * a kernel reads the token rows from host memory into x_stage (device,
+ * tokens * hidden elements, 16-byte aligned, no allocation here) and the
+ * combine writes the result straight into out_host, so the host<->device
+ * transfers are part of the launch chain instead of copy-engine calls
+ * between layers.  Both host buffers are in use until the stream reaches
+ * the end of this call.  LMOE_EINVAL for host memory the device cannot
+ * address.  Same workspace as lmoe_moe_layer_path.  No counterpart in the
+ * reference, whose arrays live in unified memory (MLX on Apple silicon). */
+int lmoe_moe_layer_host(const lmoe_layer *layer, const void *x_host, int32_t tokens,
+                        void *out_host, void *x_stage, void *workspace, size_t ws_bytes,
+                        void *stream, int32_t path);
+
 /* lmoe_moe_layer_path with token-id hash routing (see lmoe_route_hashed);
  * same workspace as lmoe_moe_layer_path. */
 int lmoe_moe_layer_hashed(const lmoe_layer *layer, const void *x, int32_t tokens,

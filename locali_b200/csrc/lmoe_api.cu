@@ -604,6 +604,26 @@ int lmoe_moe_layer_path(const lmoe_layer *layer, const void *x, int32_t tokens, 
                        ev_gateup);
 }
 
+int lmoe_moe_layer_host(const lmoe_layer *layer, const void *x_host, int32_t tokens, void *out_host,
+                        void *x_stage, void *workspace, size_t ws_bytes, void *stream, int32_t path) {
+    int rc = check_layer(layer);
+    if (rc) return rc;
+    if (tokens < 0 || (tokens > 0 && (!x_host || !out_host || !x_stage))) return LMOE_EINVAL;
+    if (tokens == 0) return LMOE_OK;
+    void *xd = nullptr, *od = nullptr;
+    if (cudaHostGetDevicePointer(&xd, const_cast<void *>(x_host), 0) != cudaSuccess ||
+        cudaHostGetDevicePointer(&od, out_host, 0) != cudaSuccess) {
+        (void)cudaGetLastError();  // not page-locked, mapped host memory
+        return LMOE_EINVAL;
+    }
+    if ((reinterpret_cast<uintptr_t>(xd) | reinterpret_cast<uintptr_t>(x_stage)) & 15u) return LMOE_EINVAL;
+    const size_t bytes = (size_t)tokens * layer->experts.hidden * 2;
+    rc = cuda_rc(launch_stage_rows(x_stage, xd, bytes, static_cast<cudaStream_t>(stream)));
+    if (rc) return rc;
+    return layer_entry(layer, x_stage, tokens, nullptr, od, nullptr, nullptr, workspace, ws_bytes, stream, path,
+                       nullptr, nullptr);
+}
+
 int lmoe_moe_layer_hashed(const lmoe_layer *layer, const void *x, int32_t tokens, const int32_t *hash_idx,
                           void *out, int32_t *idx, float *w, void *workspace, size_t ws_bytes, void *stream,
                           int32_t path) {

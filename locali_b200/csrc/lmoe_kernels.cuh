@@ -228,6 +228,8 @@ cudaError_t launch_panel(const PanelArgs &a, cudaStream_t st);
 // returns cudaErrorInvalidValue for an unsupported (bits, gs)
 cudaError_t launch_gemv(int mode, int act_f16, int bits, int gs, const GemvArgs &a,
                         int max_chunks, cudaStream_t st);
+// host rows (device-mapped pointer) -> device buffer; bytes a multiple of 16
+cudaError_t launch_stage_rows(void *dst, const void *src, size_t bytes, cudaStream_t st);
 // blocks of a MODE_DOWN2 launch over `pairs` row pairs (0: use MODE_DOWN)
 int down2_grid(int pairs);
 // MODE_DOWN2 serves layers of at most this many tokens

@@ -532,6 +532,30 @@ __device__ void route_one_token(const RouterArgs &a, const int *s_slot, bool dis
     if (lane == 0) *a.dout.n_chunks = top_k;
 }
 
+// Token rows from host memory the GPU can address (pinned, mapped) into a
+// device buffer.  The host reads are issued before the wait on the preceding
+// kernel, so their PCIe latency overlaps it; the stores follow the wait (an
+// earlier launch may still read the buffer).
+__global__ void __launch_bounds__(256) stage_rows_kernel(uint4 *dst, const uint4 *src, size_t n16) {
+    pdl_trigger();
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (i < n16) v = src[i];
+    pdl_wait();
+    if (i < n16) dst[i] = v;
+    for (i += stride; i < n16; i += stride) dst[i] = src[i];
+}
+
+cudaError_t launch_stage_rows(void *dst, const void *src, size_t bytes, cudaStream_t st) {
+    const size_t n16 = bytes / 16;
+    size_t blocks = (n16 + 255) / 256;
+    if (blocks > 592) blocks = 592;
+    if (blocks < 1) blocks = 1;
+    return launch_pdl(stage_rows_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, st,
+                      static_cast<uint4 *>(dst), static_cast<const uint4 *>(src), n16);
+}
+
 template <typename TA>
 __device__ __forceinline__ float act_to_f(uint16_t v) {
     return Act<TA>::to_f(v);

@@ -236,6 +236,7 @@ class MoEKernel:
         self._layer_fn = lmoe().lmoe_moe_layer_path
         self._desc_ref = ctypes.byref(self.desc)
         self._ready: tuple | None = None
+        self._stage: torch.Tensor | None = None  # device rows for host-buffer calls
 
     def workspace_bytes(self, tokens: int) -> int:
         cache = self.__dict__.setdefault("_ws_bytes", {})
@@ -257,6 +258,27 @@ class MoEKernel:
                  w: torch.Tensor | None = None, hash_idx: torch.Tensor | None = None) -> torch.Tensor:
         """The whole layer.  ``hash_idx`` [T, top_k] selects the experts of
         each token (token-id hash routing) instead of the router's top-k."""
+        if (out is None and idx is None and w is None and hash_idx is None and x.dtype is self.act_dtype
+                and x.dim() == 2 and not x.is_cuda and x.is_contiguous() and x.is_pinned()):
+            # host buffers: the rows are staged on the device by a kernel and
+            # the result is written into pinned host memory by the combine
+            # (returned tensor: filled when the current stream reaches the end
+            # of this call; x must stay unchanged until then)
+            T = x.shape[0]
+            ready = self._ready
+            if ready is None or ready[0] is not self.ws or ready[1] != T:
+                self.ws.ensure(self.workspace_bytes(T))
+                self._ready = (self.ws, T)
+            stage = self._stage
+            if stage is None or stage.numel() < x.numel():
+                self._stage = stage = torch.empty(x.numel(), dtype=x.dtype, device=self.ws.device)
+            buf = self.ws.buf
+            out = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
+            rc = lmoe().lmoe_moe_layer_host(self._desc_ref, x.data_ptr(), T, out.data_ptr(), stage.data_ptr(),
+                                            buf.data_ptr(), buf.numel(), _stream(), _lib.PATH[self.path])
+            if rc != _lib.LMOE_OK:
+                check(rc, "lmoe_moe_layer_host")
+            return out
         if (out is None and idx is None and w is None and hash_idx is None and x.dtype is self.act_dtype
                 and x.dim() == 2 and x.is_cuda and x.is_contiguous()):
             # steady-state decode call: no reshapes or casts, the workspace

@@ -270,3 +270,25 @@ def test_zero_tokens_is_a_noop(built):
     x = torch.empty((0, cfg.hidden), dtype=torch.bfloat16, device="cuda")
     out = kern(x)
     assert out.shape == (0, cfg.hidden)
+
+
+@pytest.mark.parametrize("T", [1, 5])
+def test_host_buffers_match_device_call(built, T):
+    """Pinned host input and output (lmoe_moe_layer_host): rows staged by a
+    kernel, result written into host memory by the combine.  Two calls in a
+    row (the staging buffer is reused) equal the device call bit for bit."""
+    cfg = synth.config("c1", n_experts=32)
+    layer = synth.make_layer(cfg, seed=30 + T, device="cuda")
+    layer.experts.pack_tiles()
+    kern = ops.MoEKernel(layer.router, layer.experts, layer.expert_slot, cfg.swiglu_limit, "fused")
+    xs = [synth.make_tokens(cfg, T, seed=40 + T + i, device="cuda") for i in range(2)]
+    want = [kern(x).clone() for x in xs]
+    hosts = [x.cpu().pin_memory() for x in xs]
+    outs = [kern(h) for h in hosts]
+    torch.cuda.synchronize()
+    kern.ws.check()
+    for o, wv in zip(outs, want):
+        assert not o.is_cuda and o.is_pinned()
+        assert torch.equal(o, wv.cpu())
+    with pytest.raises(Exception):  # pageable host memory: no CPU fallback
+        kern(xs[0].cpu())
