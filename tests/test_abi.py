@@ -56,6 +56,11 @@ def test_workspace_size_and_validation(built):
     assert lib.lmoe_moe_layer(ctypes.byref(L), None, 0, None, None, None, None, 0, None) == _lib.LMOE_OK
     assert lib.lmoe_moe_layer(ctypes.byref(L), None, 4, None, None, None, None, 0, None) == _lib.LMOE_EINVAL
     assert lib.lmoe_moe_layer(None, None, 4, None, None, None, None, 0, None) == _lib.LMOE_EINVAL
+    # host-buffer entry: zero tokens is a no-op; null buffers are rejected
+    # before any CUDA call
+    assert lib.lmoe_moe_layer_host(ctypes.byref(L), None, 0, None, None, None, 0, None, 0) == _lib.LMOE_OK
+    assert lib.lmoe_moe_layer_host(ctypes.byref(L), None, 4, None, None, None, 0, None, 0) == _lib.LMOE_EINVAL
+    assert lib.lmoe_moe_layer_host(ctypes.byref(L), 256, 4, 256, None, 256, 1 << 30, None, 0) == _lib.LMOE_EINVAL
     # too small a workspace is reported before any launch
     rc = lib.lmoe_moe_layer(ctypes.byref(L), 256, 4, 256, None, None, 256, 16, None)
     assert rc == _lib.LMOE_EWORKSPACE
