@@ -618,6 +618,7 @@ int lmoe_moe_layer_host(const lmoe_layer *layer, const void *x_host, int32_t tok
     }
     if ((reinterpret_cast<uintptr_t>(xd) | reinterpret_cast<uintptr_t>(x_stage)) & 15u) return LMOE_EINVAL;
     const size_t bytes = (size_t)tokens * layer->experts.hidden * 2;
+    if (bytes & 15u) return LMOE_EUNSUPPORTED;  // the staging kernel moves 16-byte chunks
     rc = cuda_rc(launch_stage_rows(x_stage, xd, bytes, static_cast<cudaStream_t>(stream)));
     if (rc) return rc;
     return layer_entry(layer, x_stage, tokens, nullptr, od, nullptr, nullptr, workspace, ws_bytes, stream, path,
