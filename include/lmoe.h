@@ -174,15 +174,15 @@ int lmoe_moe_layer_staged(const lmoe_layer *layer, const void *x, int32_t tokens
  * of 8 quantisation groups, and row-major arena arrays.  AUTO takes the
  * prefill path when the geometry allows it and the routes (tokens * top_k)
  * reach both LMOE_PREFILL_MIN_ROUTES and LMOE_PREFILL_ROUTES_PER_4_EXPERTS /
- * 4 * n_experts (measured crossover on B200 at 256 experts, top-6: the two
- * paths tie at 48 tokens, and the prefill path leads from 64).  No
+ * 4 * n_experts (measured crossover on B200 at 256 experts, top-6: the
+ * decode path leads at 64 tokens, the prefill path at 96).  No
  * counterpart in the reference's own code; MLX's gather_qmm
  * (dsv4_arena.py:198-221) also changes kernels with the batch size. */
 #define LMOE_PATH_AUTO 0
 #define LMOE_PATH_DECODE 1
 #define LMOE_PATH_PREFILL 2
 #define LMOE_PREFILL_MIN_ROUTES 256
-#define LMOE_PREFILL_ROUTES_PER_4_EXPERTS 5
+#define LMOE_PREFILL_ROUTES_PER_4_EXPERTS 7
 
 /* lmoe_moe_layer_staged on an explicit path (LMOE_PATH_*); LMOE_EUNSUPPORTED
  * when the layer's geometry does not allow the requested path. */

@@ -30,7 +30,7 @@ SWIGLU_MODE = {"fused": 0, "stock": 1}
 # expert-product path of a layer call (LMOE_PATH_*)
 PATH = {"auto": 0, "decode": 1, "prefill": 2}
 PREFILL_MIN_ROUTES = 256
-PREFILL_ROUTES_PER_4_EXPERTS = 5
+PREFILL_ROUTES_PER_4_EXPERTS = 7
 
 
 def auto_takes_prefill(tokens: int, top_k: int, n_experts: int) -> bool:

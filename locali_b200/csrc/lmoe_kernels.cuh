@@ -232,8 +232,9 @@ cudaError_t launch_gemv(int mode, int act_f16, int bits, int gs, const GemvArgs 
 cudaError_t launch_stage_rows(void *dst, const void *src, size_t bytes, cudaStream_t st);
 // blocks of a MODE_DOWN2 launch over `pairs` row pairs (0: use MODE_DOWN)
 int down2_grid(int pairs);
-// MODE_DOWN2 serves layers of at most this many tokens
-constexpr int kDown2MaxTokens = 16;
+// MODE_DOWN2 serves layers of at most this many tokens (the decode path's
+// range under AUTO at 256 experts, top-6)
+constexpr int kDown2MaxTokens = 64;
 // row-major slots [slot_begin, slot_begin + slot_count) of q -> tiles
 cudaError_t launch_tile_pack(const QView &q, int bits, int gs, int slot_begin, int slot_count, uint8_t *tiles,
                              cudaStream_t st);

@@ -221,7 +221,7 @@ class MoEKernel:
         if path not in _lib.PATH:
             raise ValueError(f"path must be one of {sorted(_lib.PATH)}")
         # "decode": fused dequant GEMVs; "prefill": tcgen05 grouped GEMM;
-        # "auto": prefill once the routes reach 256 and 1.25 * n_experts
+        # "auto": prefill once the routes reach 256 and 1.75 * n_experts
         self.path = path
         if expert_slot.dtype != torch.int32 or not expert_slot.is_contiguous():
             raise ValueError("expert_slot must be contiguous int32")
