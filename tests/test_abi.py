@@ -155,3 +155,19 @@ def test_three_bit_layers_take_the_prefill_path(built):
     rc = lib.lmoe_moe_layer_path(ctypes.byref(L3), 256, 1, 256, None, None, 256, big, None, P["decode"], None, None)
     assert rc == _lib.LMOE_EUNSUPPORTED
     assert lib.lmoe_tile_bytes(2048, 4096, 3, 64) == 0  # no tile layout for 3-bit rows
+
+
+def test_auto_rule_mirror_matches_library(built):
+    """_lib.auto_takes_prefill (used by tests and the bench) is the library's
+    AUTO choice: AUTO sizes the decode layout below the threshold and the
+    larger of both layouts from it on."""
+    lib = _lib.lmoe()
+    P = _lib.PATH
+    for E in (16, 64, 256):
+        L = _layer(E=E, k=6)
+        for T in (1, 8, 42, 43, 64, 74, 75, 96, 300):
+            dec = lib.lmoe_workspace_size_path(ctypes.byref(L), T, P["decode"])
+            pre = lib.lmoe_workspace_size_path(ctypes.byref(L), T, P["prefill"])
+            auto = lib.lmoe_workspace_size_path(ctypes.byref(L), T, P["auto"])
+            want = max(dec, pre) if _lib.auto_takes_prefill(T, 6, E) else dec
+            assert auto == want, (E, T)
