@@ -48,7 +48,7 @@ METRIC = "routed-MoE layer tokens/s + % HBM roofline (decode)"
 UNIT = "tokens/s"
 L2_BYTES = 126 * 1024 * 1024
 FALLBACK_HBM_GBS = 6650.0
-FALLBACK_BF16_TFLOPS = 1400.0  # sustained under the power cap
+FALLBACK_BF16_TFLOPS = 1590.0  # burst figure of the profiling recipe
 
 
 def parse():
@@ -94,12 +94,13 @@ def measured_peak():
 
 
 def measured_tensor_peak():
-    """Sustained cuBLAS bf16 TFLOP/s (the prefill kernels run inside a long step)."""
+    """Burst cuBLAS bf16 TFLOP/s: the prefill kernels are timed over a region
+    of tens of milliseconds, not a seconds-long loop under the power cap."""
     f = ROOT / "MEASURED_PEAKS.json"
     if f.exists():
         d = json.loads(f.read_text())
-        if "bf16_tflops_sustained" in d:
-            return float(d["bf16_tflops_sustained"]), "measured sustained"
+        if "bf16_tflops" in d:
+            return float(d["bf16_tflops"]), "measured burst"
     return FALLBACK_BF16_TFLOPS, "fallback"
 
 
@@ -445,7 +446,7 @@ def run_prefill(args, dev):
         "layer_tflops": all_flops / (ms / 1e3) / 1e12,
         "kernels_us": {"router_dispatch": 1e3 * rt_ms, "gateup_swiglu": 1e3 * gu_ms, "down_combine": 1e3 * dn_ms},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                     "frac": achieved / peak, "peak_source": f"{kind} (MEASURED_PEAKS.json bf16_tflops_sustained)",
+                     "frac": achieved / peak, "peak_source": f"{kind} (MEASURED_PEAKS.json bf16_tflops)",
                      "kernel": "pf_gemm_kernel<bf16, 2, 64, gate/up> (tcgen05)",
                      "algorithmic_flops_per_launch": gu_flops},
     }

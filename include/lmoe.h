@@ -104,12 +104,6 @@ typedef struct lmoe_layer {
 int lmoe_version(void);
 const char *lmoe_strerror(int status);
 
-/* Profiling aid (not part of the reference interface): while buf is non-NULL,
- * every gate/up expert kernel launched by lmoe_moe_layer* records
- * %globaltimer stamps into buf[block][unit][8] (units_per_block units per
- * block; device memory owned by the caller).  Pass NULL to stop. */
-void lmoe_profile_trace(uint64_t *buf, int32_t units_per_block);
-
 /* Bytes of workspace needed for up to max_tokens tokens of this layer. */
 size_t lmoe_workspace_size(const lmoe_layer *layer, int32_t max_tokens);
 
@@ -125,7 +119,8 @@ int lmoe_workspace_status(void *workspace, void *stream);
  * (arena.py:501-506).  x [T, hidden] activations of `dtype`; idx [T, top_k]
  * int32 (ordered by biased score, ties to the lower id); w [T, top_k] fp32
  * combine weights (already multiplied by routed_scaling).  hidden must be a
- * multiple of 256. */
+ * multiple of 64 (LMOE_EUNSUPPORTED otherwise); the layer entry points below
+ * share this rule. */
 int lmoe_route(const lmoe_router *router, int32_t hidden, int32_t dtype,
                const void *x, int32_t tokens, int32_t *idx, float *w,
                void *workspace, size_t ws_bytes, void *stream);
@@ -224,21 +219,37 @@ size_t lmoe_workspace_size_path(const lmoe_layer *layer, int32_t max_tokens,
  * forbids allocation on its request path, a binding without a device
  * allocator).  Scratch lives in a static device array of
  * LMOE_STATIC_WORKSPACE_BYTES (8 MiB), held by every GPU that loads the
- * library until the process exits; layers whose workspace would exceed it
- * (lmoe_workspace_size > 8 MiB, about 80 decode tokens at DeepSeek-V4-Flash
- * shapes) are rejected with LMOE_EWORKSPACE before anything is enqueued.  The
- * first call on a device looks up the array's device address with that
- * device current; make that first call before any stream capture.  The call
- * allocates nothing (no cudaMalloc/cudaFree), zeroes the array's counters on
- * the stream, then runs the same kernels as lmoe_moe_layer.  All calls on a
- * device share the one array and it keeps the last call's contents, so calls
- * that overlap on the GPU (different streams, or concurrent host threads
- * without ordering) race and corrupt each other's results. */
+ * library until the process exits.  The call always runs the decode path
+ * (lmoe_moe_layer_path with LMOE_PATH_DECODE), so:
+ *   - layers that path cannot run (3-bit projections, or widths without a
+ *     decode tile plan such as hidden 7168 at 2 bits) return
+ *     LMOE_EUNSUPPORTED;
+ *   - calls with lmoe_workspace_size_path(layer, tokens, LMOE_PATH_DECODE)
+ *     > LMOE_STATIC_WORKSPACE_BYTES (about 80 tokens at DeepSeek-V4-Flash
+ *     shapes) return LMOE_EWORKSPACE;
+ * both before anything is enqueued.  Where AUTO would take the tcgen05 path
+ * (LMOE_PREFILL_MIN_ROUTES and more), the results follow the decode path's
+ * arithmetic, not lmoe_moe_layer's.  The first call on a device looks up the
+ * array's device address with that device current; make that first call
+ * before any stream capture.  The call allocates nothing (no
+ * cudaMalloc/cudaFree), clears the array's status word and router counter on
+ * the stream, then runs the kernels.  All calls on a device share the one
+ * array and it keeps the last call's contents, so calls that overlap on the
+ * GPU (different streams, or concurrent host threads without ordering) race
+ * and corrupt each other's results. */
 #define LMOE_STATIC_WORKSPACE_BYTES (8u << 20)
 int lmoe_moe_layer_static(const lmoe_layer *layer, const void *x,
                           int32_t tokens, void *out, int32_t *idx, float *w,
                           void *stream);
 size_t lmoe_static_workspace_bytes(void);
+
+/* Device error flag of the most recent lmoe_moe_layer_static call on the
+ * current device (each call clears it when it starts): synchronises the
+ * stream, reads the flag, clears it.  Returns LMOE_OK, LMOE_EINDEX (a bad
+ * expert id or arena slot was met and contributed zeros) or LMOE_ECUDA.  The
+ * lmoe_workspace_status of the static scratch, whose address callers never
+ * see. */
+int lmoe_static_status(void *stream);
 
 /* Same layer with routing supplied by the caller (an external gate, as
  * V4ArenaMoE.route returns it): idx [T, top_k] expert ids, w [T, top_k]

@@ -21,9 +21,12 @@ bool quant_ok(int bits, int gs) { return gemv_ok(bits, gs) || (bits == 3 && (gs 
 
 size_t al(size_t v) { return (v + 255) & ~size_t(255); }
 
-// profiling timeline of the gate/up kernel (lmoe_profile_trace)
+#ifdef LMOE_PROFILE_TRACE
+// profiling timeline of the gate/up kernel (lmoe_profile_trace, profiling
+// builds only)
 uint64_t *g_trace = nullptr;
 int32_t g_trace_units = 0;
+#endif
 
 struct Layout {
     size_t status = 0, partial = 0, idx = 0, w = 0, sorted = 0, counts = 0, roff = 0,
@@ -245,8 +248,10 @@ int run_experts(const lmoe_layer *l, const Layout &L, void *ws, int T, const flo
     gu.out_gs = ex.down.group_size;
     gu.limit = l->swiglu_limit;
     gu.swiglu_mode = l->swiglu_mode;
+#ifdef LMOE_PROFILE_TRACE
     gu.trace = g_trace;
     gu.trace_units = g_trace_units;
+#endif
     int rc = cuda_rc(launch_gemv(MODE_GATEUP, ex.dtype == LMOE_F16, ex.gate.bits, ex.gate.group_size,
                                  gu, L.max_chunks, st));
     if (rc) return rc;
@@ -353,6 +358,10 @@ bool layer_gemv_ok(const lmoe_layer *l) {
            gemv_ok(ex.down.bits, ex.down.group_size) && layer_chunk(l, 1) >= 1;
 }
 
+// Router kernels: 16-byte column loads over 256-column warp chunks (the last
+// may be partial) and 64-column tensor-core stages for many tokens.
+bool router_hidden_ok(int hidden) { return hidden > 0 && hidden % 64 == 0; }
+
 // 1 = prefill grouped GEMM, 0 = decode GEMVs, -1 = the requested path is unavailable
 int choose_path(const lmoe_layer *l, int T, int path) {
     const bool dec = layer_gemv_ok(l);
@@ -372,10 +381,15 @@ extern "C" {
 
 int lmoe_version(void) { return LMOE_ABI_VERSION; }
 
+#ifdef LMOE_PROFILE_TRACE
+// Profiling builds only (not declared in lmoe.h): while buf is non-NULL,
+// every gate/up GEMV records %globaltimer stamps into
+// buf[block][unit][8] (device memory owned by the caller).
 void lmoe_profile_trace(uint64_t *buf, int32_t units_per_block) {
     g_trace = buf;
     g_trace_units = buf ? units_per_block : 0;
 }
+#endif
 
 const char *lmoe_strerror(int status) {
     switch (status) {
@@ -537,7 +551,7 @@ int check_router(const lmoe_router *r, int hidden) {
     if (r->n_experts < 1 || r->top_k < 1 || r->top_k > 16 || r->top_k > r->n_experts) return LMOE_EINVAL;
     if (r->n_experts > 32 * kRouterMaxEPL) return LMOE_EUNSUPPORTED;
     if (r->scoring < 0 || r->scoring > 2) return LMOE_EUNSUPPORTED;
-    if (hidden % kRouterKS) return LMOE_EUNSUPPORTED;
+    if (!router_hidden_ok(hidden)) return LMOE_EUNSUPPORTED;
     return LMOE_OK;
 }
 
@@ -582,7 +596,7 @@ static int layer_entry(const lmoe_layer *layer, const void *x, int32_t tokens, c
     if (rc) return rc;
     if (tokens < 0 || (tokens > 0 && (!x || !out || !workspace))) return LMOE_EINVAL;
     if (tokens == 0) return LMOE_OK;
-    if (layer->experts.hidden % kRouterKS) return LMOE_EUNSUPPORTED;
+    if (!router_hidden_ok(layer->experts.hidden)) return LMOE_EUNSUPPORTED;
     const int pf = choose_path(layer, tokens, path);
     if (pf < 0) return LMOE_EUNSUPPORTED;
     const Layout L = pf ? prefill_layout(layer, tokens) : layer_layout(layer, tokens);
@@ -701,26 +715,32 @@ size_t lmoe_static_workspace_bytes(void) { return LMOE_STATIC_WORKSPACE_BYTES; }
 
 int lmoe_moe_layer_static(const lmoe_layer *layer, const void *x, int32_t tokens, void *out, int32_t *idx,
                           float *w, void *stream) {
+    // every check that can reject the call runs before anything is enqueued
     int rc = check_layer(layer);
     if (rc) return rc;
     if (tokens < 0 || (tokens > 0 && (!x || !out))) return LMOE_EINVAL;
     if (tokens == 0) return LMOE_OK;
-    if (layer->experts.hidden % kRouterKS) return LMOE_EUNSUPPORTED;
+    if (!router_hidden_ok(layer->experts.hidden)) return LMOE_EUNSUPPORTED;
+    if (choose_path(layer, tokens, LMOE_PATH_DECODE) < 0) return LMOE_EUNSUPPORTED;
     const Layout L = layer_layout(layer, tokens);
     if (L.total > LMOE_STATIC_WORKSPACE_BYTES) return LMOE_EWORKSPACE;
     void *ws = nullptr;
     rc = static_workspace(&ws);
     if (rc) return rc;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    // The array keeps whatever the previous call left in it: zero the words
-    // that must start at zero (error flag, router block counter, combine
-    // counters) before this call's kernels run.
-    const size_t cnt_bytes = (size_t)tokens * (layer->experts.hidden / 16) * sizeof(uint32_t);
-    if (cudaMemsetAsync(at<uint8_t>(ws, L.status), 0, 256, st) != cudaSuccess ||
-        cudaMemsetAsync(at<uint8_t>(ws, L.cnt), 0, cnt_bytes, st) != cudaSuccess)
-        return LMOE_ECUDA;
+    // The array keeps whatever the previous call left in it.  The status
+    // word and the router's block counter (the first 256 bytes) must start
+    // at zero; the combine counters are zeroed by the router kernel itself.
+    if (cudaMemsetAsync(at<uint8_t>(ws, L.status), 0, 256, st) != cudaSuccess) return LMOE_ECUDA;
     return lmoe_moe_layer_path(layer, x, tokens, out, idx, w, ws, LMOE_STATIC_WORKSPACE_BYTES, stream,
                                LMOE_PATH_DECODE, nullptr, nullptr);
+}
+
+int lmoe_static_status(void *stream) {
+    void *ws = nullptr;
+    const int rc = static_workspace(&ws);
+    if (rc) return rc;
+    return lmoe_workspace_status(ws, stream);
 }
 
 int lmoe_moe_routed(const lmoe_layer *layer, const void *x, int32_t tokens, const int32_t *idx,

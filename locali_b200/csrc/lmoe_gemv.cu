@@ -87,10 +87,15 @@ __device__ __forceinline__ int code_xor(int row) {
     return row & 7;
 }
 
-// Optional profiling timeline: one globaltimer stamp per (block, unit, point).
+// Profiling builds (-DLMOE_PROFILE_TRACE) record one globaltimer stamp per
+// (block, unit, point); the default build compiles these calls away.
 __device__ __forceinline__ void trace_point(const GemvArgs &a, int it, int point) {
+#ifdef LMOE_PROFILE_TRACE
     if (a.trace && it < a.trace_units && (threadIdx.x & 31) == 0)
         a.trace[((size_t)blockIdx.x * a.trace_units + it) * 8 + point] = globaltimer_ns();
+#else
+    (void)a, (void)it, (void)point;
+#endif
 }
 
 template <typename TA, int BITS, int GS, int MODE>

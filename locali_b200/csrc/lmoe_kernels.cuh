@@ -163,10 +163,12 @@ struct GemvArgs {
     uint32_t *counters;
     uint16_t *combined;
     int32_t *err;
-    // optional per-unit timeline (nanoseconds, %globaltimer) for profiling:
-    // [block][unit slot][8]; nullptr in normal use
+#ifdef LMOE_PROFILE_TRACE
+    // per-unit timeline (nanoseconds, %globaltimer) of a profiling build:
+    // [block][unit slot][8]
     uint64_t *trace;
     int32_t trace_units;
+#endif
 };
 
 // Shared-memory plan of one gemv launch (computed on the host, passed by value).

@@ -533,18 +533,15 @@ __device__ void route_one_token(const RouterArgs &a, const int *s_slot, bool dis
 }
 
 // Token rows from host memory the GPU can address (pinned, mapped) into a
-// device buffer.  The host reads are issued before the wait on the preceding
-// kernel, so their PCIe latency overlaps it; the stores follow the wait (an
-// earlier launch may still read the buffer).
+// device buffer.  Both the host reads and the device stores follow the wait
+// on the preceding kernel: the host rows may be the output of the previous
+// layer call (its combine writes straight into pinned host memory), and an
+// earlier launch may still read the device buffer.
 __global__ void __launch_bounds__(256) stage_rows_kernel(uint4 *dst, const uint4 *src, size_t n16) {
     pdl_trigger();
-    const size_t stride = (size_t)gridDim.x * blockDim.x;
-    size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-    if (i < n16) v = src[i];
     pdl_wait();
-    if (i < n16) dst[i] = v;
-    for (i += stride; i < n16; i += stride) dst[i] = src[i];
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += stride) dst[i] = src[i];
 }
 
 cudaError_t launch_stage_rows(void *dst, const void *src, size_t bytes, cudaStream_t st) {
@@ -582,7 +579,9 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
     const int e0 = blockIdx.x * EPB;
     const int tbeg = blockIdx.y * 64;
     const int tend = min(a.T, tbeg + 64);
-    const int nchunk = a.H / kRouterKS;
+    // 256-column chunks per warp iteration; the last one may be partial
+    // (hidden a multiple of 64): lanes past the width load nothing
+    const int nchunk = (a.H + kRouterKS - 1) / kRouterKS;
     __shared__ float s_bias[EPB];
     if (tid < EPB) s_bias[tid] = (a.bias && e0 + tid < a.E) ? a.bias[e0 + tid] : 0.0f;
     // Router weights are read once per layer call: evict-first in L2.
@@ -597,7 +596,7 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
 #pragma unroll
         for (int i = 0; i < EPB; ++i) {
             wpre[j][i] = make_uint4(0, 0, 0, 0);
-            if (one_pass && ch < nchunk && e0 + i < a.E)
+            if (one_pass && ch < nchunk && e0 + i < a.E && ch * kRouterKS + lane * 8 < a.H)
                 wpre[j][i] = ldg_u128_hint(
                     reinterpret_cast<const uint4 *>(a.wg + (size_t)(e0 + i) * a.H + ch * kRouterKS + lane * 8), wpol);
         }
@@ -630,7 +629,7 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
     for (int j = 0; j < 2; ++j) {
         const int ch = warp + 8 * j;
         xpre[j] = make_uint4(0, 0, 0, 0);
-        if (one_tok && ch < nchunk) xpre[j] = __ldg(reinterpret_cast<const uint4 *>(a.x + (size_t)tbeg * a.H + ch * kRouterKS + lane * 8));
+        if (one_tok && ch < nchunk && ch * kRouterKS + lane * 8 < a.H) xpre[j] = __ldg(reinterpret_cast<const uint4 *>(a.x + (size_t)tbeg * a.H + ch * kRouterKS + lane * 8));
     }
 
     // ---- gate/up activation panel + 16-column sums for this block's share.
@@ -692,6 +691,7 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
 #pragma unroll 2
         for (int ch = warp, j = 0; ch < nchunk; ch += 8, ++j) {
             const int col = ch * kRouterKS + lane * 8;
+            const bool kin = col < a.H;  // zeros past the width add nothing
             uint4 wv[EPB];
 #pragma unroll
             for (int i = 0; i < EPB; ++i) {
@@ -701,7 +701,7 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
                     wv[i] = wpre[1][i];
                 } else {
                     wv[i] = make_uint4(0, 0, 0, 0);
-                    if (e0 + i < a.E)
+                    if (e0 + i < a.E && kin)
                         wv[i] = ldg_u128_hint(reinterpret_cast<const uint4 *>(a.wg + (size_t)(e0 + i) * a.H + col), wpol);
                 }
             }
@@ -711,7 +711,7 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
                 xv[n] = make_uint4(0, 0, 0, 0);
                 if (n == 0 && one_tok && j == 0) xv[0] = xpre[0];
                 else if (n == 0 && one_tok && j == 1) xv[0] = xpre[1];
-                else if (n < nt) xv[n] = __ldg(reinterpret_cast<const uint4 *>(a.x + (size_t)(ts + n) * a.H + col));
+                else if (n < nt && kin) xv[n] = __ldg(reinterpret_cast<const uint4 *>(a.x + (size_t)(ts + n) * a.H + col));
             }
 #pragma unroll
             for (int n = 0; n < 8; ++n) {

@@ -315,8 +315,10 @@ class MoEKernel:
                     w: torch.Tensor | None = None) -> torch.Tensor:
         """The layer through ``lmoe_moe_layer_static``: no workspace is
         allocated; the library's fixed 8 MiB device scratch is used instead
-        (for callers that cannot allocate device memory).  Calls that overlap
-        on the GPU share that scratch and must not run concurrently."""
+        (for callers that cannot allocate device memory).  It always runs the
+        decode path.  Calls that overlap on the GPU share that scratch and
+        must not run concurrently.  :func:`static_status` reports the device
+        error flag of the latest such call."""
         flat = self._x(x)
         T = flat.shape[0]
         if out is None:
@@ -354,6 +356,12 @@ class MoEKernel:
         check(lmoe().lmoe_moe_routed(ctypes.byref(self.desc), flat.data_ptr(), T, idx.data_ptr(), w.data_ptr(),
                                      out.data_ptr(), self.ws.ptr(), self.ws.nbytes, _stream()), "lmoe_moe_routed")
         return out.reshape(x.shape)
+
+
+def static_status() -> None:
+    """Synchronise and raise if the latest ``lmoe_moe_layer_static`` call on
+    the current device flagged a bad expert id or slot (clears the flag)."""
+    check(lmoe().lmoe_static_status(_stream()), "static scratch status")
 
 
 def _hash(hash_idx: torch.Tensor | None, T: int, k: int) -> torch.Tensor | None:

@@ -292,3 +292,29 @@ def test_host_buffers_match_device_call(built, T):
         assert torch.equal(o, wv.cpu())
     with pytest.raises(Exception):  # pageable host memory: no CPU fallback
         kern(xs[0].cpu())
+
+
+@pytest.mark.parametrize("T", [1, 5])
+def test_host_buffers_chained_calls(built, T):
+    """One host call's pinned output is the next host call's input
+    (mod2(mod1(x_pinned))), with no host synchronisation between them: the
+    second call's staging kernel must read the rows only after the first
+    call's combine has written them.  Compared with the same chain on the
+    device, bit for bit, over several layers."""
+    cfg = synth.config("c1", n_experts=32)
+    kerns = []
+    for i in range(4):
+        layer = synth.make_layer(cfg, seed=60 + i, device="cuda")
+        layer.experts.pack_tiles()
+        kerns.append(ops.MoEKernel(layer.router, layer.experts, layer.expert_slot, cfg.swiglu_limit, "fused"))
+    x = synth.make_tokens(cfg, T, seed=70 + T, device="cuda")
+    want = x
+    for k in kerns:
+        want = k(want)
+    h = x.cpu().pin_memory()
+    for k in kerns:
+        h = k(h)
+    torch.cuda.synchronize()
+    for k in kerns:
+        k.ws.check()
+    assert torch.equal(h, want.cpu())
