@@ -295,6 +295,56 @@ int lmoe_tile_pack(const lmoe_qproj *src, int32_t n_slots, int32_t rows,
                    int32_t cols, int32_t slot_begin, int32_t slot_count,
                    void *tiles, void *stream);
 
+/* ---- Expert parallel (no counterpart in the reference, which runs every
+ * expert of a layer on one device, arena.py:508-672; the arithmetic is that
+ * layer's, split by expert owner).  world ranks; rank r owns experts
+ * [r * E/world, (r+1) * E/world) and routes its own tokens.  One layer step:
+ *   lmoe_route (replicated router) -> lmoe_ep_dispatch -> all-to-all of the
+ *   send rows (equal splits of tokens rows per rank pair) -> lmoe_ep_experts
+ *   -> all-to-all of the fp32 partial rows back -> lmoe_ep_combine.
+ * Every buffer has a fixed size, so the step needs no host-side counts and
+ * no host wait.  An exchanged row is lmoe_ep_row_bytes(hidden, top_k)
+ * bytes: the hidden activations, then int32 local expert ids [top_k] (-1:
+ * owned by another rank), fp32 weights [top_k], the int32 source token (-1:
+ * padding row) and zero padding to 16 bytes. */
+size_t lmoe_ep_row_bytes(int32_t hidden, int32_t top_k);
+
+/* Source side.  idx/w [tokens, top_k] (lmoe_route output), x [tokens,
+ * hidden]; send [world][tokens][row_bytes] receives, for every destination
+ * rank d, the rows of the tokens with an expert on d in token order (then
+ * padding rows); slot_of [tokens][world] the row of token t in d's block
+ * (-1: none).  workspace: any lmoe workspace (its status word receives
+ * LMOE_EINDEX for an expert id outside [0, n_experts), which then
+ * contributes zero) or NULL.  n_experts % world == 0, world <= 32,
+ * hidden % 8 == 0. */
+int lmoe_ep_dispatch(const int32_t *idx, const float *w, const void *x,
+                     int32_t tokens, int32_t hidden, int32_t top_k,
+                     int32_t n_experts, int32_t world, void *send,
+                     int32_t *slot_of, void *workspace, void *stream);
+
+/* Expert side.  local: the rank's experts as a layer (router.n_experts =
+ * experts per rank, router.top_k = the route width, expert_slot = local
+ * expert -> arena slot; the router weights are not read).  recv [rows]
+ * exchanged rows (rows = world * tokens per rank).  partial [rows, hidden]
+ * fp32: for each real row, the rounded y*w rows of its local routes summed
+ * in route order (padding rows are left unwritten).  path as in
+ * lmoe_moe_layer_path; AUTO applies its rule to rows * top_k / world
+ * routes. */
+size_t lmoe_ep_workspace_size(const lmoe_layer *local, int32_t rows,
+                              int32_t world, int32_t path);
+int lmoe_ep_experts(const lmoe_layer *local, const void *recv, int32_t rows,
+                    int32_t world, float *partial, void *workspace,
+                    size_t ws_bytes, void *stream, int32_t path);
+
+/* Source side, after the return exchange.  back [world][tokens][hidden] fp32
+ * (rank d's partials in the order of d's received rows); out[t] = the
+ * partials of the ranks that own t's experts added in rank order in fp32,
+ * rounded once to dtype; with residual [tokens, hidden] (may be NULL),
+ * out[t] = dtype(residual[t] + that).  out may alias residual. */
+int lmoe_ep_combine(const float *back, int32_t tokens, int32_t world,
+                    int32_t hidden, int32_t dtype, const int32_t *slot_of,
+                    const void *residual, void *out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

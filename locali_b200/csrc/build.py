@@ -24,7 +24,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
               "-Wno-deprecated-gpu-targets"]
 
-LMOE_SOURCES = ["lmoe_route.cu", "lmoe_gemv.cu", "lmoe_prefill.cu", "lmoe_api.cu"]
+LMOE_SOURCES = ["lmoe_route.cu", "lmoe_gemv.cu", "lmoe_prefill.cu", "lmoe_ep.cu", "lmoe_api.cu"]
 LMOE_DEPS = LMOE_SOURCES + ["lmoe_common.cuh", "lmoe_kernels.cuh"]
 LMOE_LIB = PKG / "liblmoe.so"
 CORE_LIB = PKG / "liblocali_core.so"
@@ -58,13 +58,15 @@ def build_lmoe(force: bool = False, verbose: bool = False) -> Path:
     nvcc = _nvcc()
     objdir = CSRC / "_build"
     objdir.mkdir(exist_ok=True)
+    headers = [CSRC / s for s in LMOE_DEPS if s.endswith(".cuh")] + [INCLUDE / "lmoe.h", Path(__file__)]
     objs = []
     for src in LMOE_SOURCES:
         obj = objdir / (Path(src).stem + ".o")
-        cmd = [nvcc, *ARCH, *NVCC_FLAGS, f"-I{INCLUDE}", "-c", str(CSRC / src), "-o", str(obj)]
-        if verbose:
-            cmd.insert(1, "-Xptxas=-v")
-        _run(cmd)
+        if force or verbose or _stale(obj, [CSRC / src, *headers]):
+            cmd = [nvcc, *ARCH, *NVCC_FLAGS, f"-I{INCLUDE}", "-c", str(CSRC / src), "-o", str(obj)]
+            if verbose:
+                cmd.insert(1, "-Xptxas=-v")
+            _run(cmd)
         objs.append(str(obj))
     tmp = LMOE_LIB.with_suffix(".so.tmp")
     _run([nvcc, *ARCH, "-shared", "-o", str(tmp), *objs, "-lcudart"])

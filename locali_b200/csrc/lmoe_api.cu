@@ -178,7 +178,7 @@ int cuda_rc(cudaError_t e) {
 
 // Runs dispatch for R routes into buckets [0, n_experts) (+ zero bucket).
 int run_dispatch(const Layout &L, void *ws, const int32_t *idx, int R, int n_experts,
-                 const int32_t *expert_slot, int n_slots, int chunk_tok, cudaStream_t st) {
+                 const int32_t *expert_slot, int n_slots, int chunk_tok, cudaStream_t st, bool drop_zero = false) {
     DispatchIn din;
     din.idx = idx;
     din.R = R;
@@ -186,6 +186,7 @@ int run_dispatch(const Layout &L, void *ws, const int32_t *idx, int R, int n_exp
     din.n_experts = n_experts;
     din.expert_slot = expert_slot;
     din.n_slots = n_slots;
+    din.drop_zero = drop_zero ? 1 : 0;
     DispatchOut dout;
     dout.sorted_routes = at<int32_t>(ws, L.sorted);
     dout.chunks = at<Chunk>(ws, L.chunks);
@@ -229,6 +230,8 @@ int layer_chunk(const lmoe_layer *l, int T) {
 }
 
 // gate/up + SwiGLU then down + combine over an already dispatched layer.
+// out == nullptr: the down kernel leaves the rounded y*w rows of every
+// computed route in the workspace and combines nothing.
 int run_experts(const lmoe_layer *l, const Layout &L, void *ws, int T, const float *route_w,
                 void *out, cudaStream_t st, cudaEvent_t ev_gateup = nullptr) {
     const lmoe_experts &ex = l->experts;
@@ -264,14 +267,15 @@ int run_experts(const lmoe_layer *l, const Layout &L, void *ws, int T, const flo
     dn.out = at<uint16_t>(ws, L.yw);
     dn.route_w = route_w;
     dn.top_k = k;
-    dn.counters = at<uint32_t>(ws, L.cnt);
+    dn.counters = out ? at<uint32_t>(ws, L.cnt) : nullptr;
     dn.combined = static_cast<uint16_t *>(out);
     dn.n_tok = T;
     // Few tokens: blocks own row pairs and combine locally (no device-wide
     // counters or fences at the tail).  More tokens: row tiles spread over
-    // every SM and the counter-based combine.
+    // every SM and the counter-based combine.  Without a combine the paired
+    // tiles serve any token count.
     GemvCfg d2;
-    const int mode = (T <= kDown2MaxTokens && H % 32 == 0 && down2_grid(H / 32) > 0 &&
+    const int mode = ((T <= kDown2MaxTokens || !out) && H % 32 == 0 && down2_grid(H / 32) > 0 &&
                       gemv_config(MODE_DOWN2, ex.down.bits, ex.down.group_size, I, ntok_max, &d2))
                          ? MODE_DOWN2
                          : MODE_DOWN;
@@ -283,7 +287,7 @@ int run_experts(const lmoe_layer *l, const Layout &L, void *ws, int T, const flo
 // routes): x rows -> tiled panel, gate/up + SwiGLU on tcgen05 (h straight
 // into the down panel), down on tcgen05 (y*w rows), combine per token.
 int run_experts_pf(const lmoe_layer *l, const Layout &L, void *ws, const void *x, int T, const float *route_w,
-                   void *out, cudaStream_t st, cudaEvent_t ev_gateup = nullptr) {
+                   void *out, cudaStream_t st, cudaEvent_t ev_gateup = nullptr, int x_stride = 0) {
     const lmoe_experts &ex = l->experts;
     const int H = ex.hidden, I = ex.inter, k = l->router.top_k;
     const int f16 = ex.dtype == LMOE_F16;
@@ -291,6 +295,7 @@ int run_experts_pf(const lmoe_layer *l, const Layout &L, void *ws, const void *x
     std::memset(&pa, 0, sizeof(pa));
     pa.x = static_cast<const uint16_t *>(x);
     pa.K = H;
+    pa.x_stride = x_stride;
     pa.route_div = k;
     pa.chunks = at<Chunk>(ws, L.chunks);
     pa.n_chunks = at<int32_t>(ws, L.nchunks);
@@ -333,7 +338,7 @@ int run_experts_pf(const lmoe_layer *l, const Layout &L, void *ws, const void *x
     d.H = H;
     d.route_w = route_w;
     rc = cuda_rc(launch_pf_gemm(PF_DOWN, f16, ex.down.bits, ex.down.group_size, d, st));
-    if (rc) return rc;
+    if (rc || !out) return rc;  // out == nullptr: the caller combines the y*w rows
     return cuda_rc(launch_pf_combine(f16, d.yw, T, H, k, static_cast<uint16_t *>(out), st));
 }
 
@@ -373,6 +378,57 @@ int choose_path(const lmoe_layer *l, int T, int path) {
     const long routes = (long)T * l->router.top_k;
     return ok && routes >= LMOE_PREFILL_MIN_ROUTES &&
            4 * routes >= (long)LMOE_PREFILL_ROUTES_PER_4_EXPERTS * l->router.n_experts;
+}
+
+// ---- expert-parallel receive side
+// The local layer: the rank's experts, its slot table and the route width;
+// its router is never evaluated (n_experts = local experts, top_k may exceed it).
+int check_ep_local(const lmoe_layer *l) {
+    if (!l) return LMOE_EINVAL;
+    int rc = check_experts(&l->experts);
+    if (rc) return rc;
+    const lmoe_router &r = l->router;
+    if (r.n_experts < 1 || r.top_k < 1 || r.top_k > 16) return LMOE_EINVAL;
+    if (r.n_experts + 1 > kDispatchSmallMaxBuckets) return LMOE_EUNSUPPORTED;
+    if (l->swiglu_mode != LMOE_SWIGLU_FUSED && l->swiglu_mode != LMOE_SWIGLU_STOCK) return LMOE_EUNSUPPORTED;
+    if (!l->expert_slot) return LMOE_EINVAL;
+    return LMOE_OK;
+}
+
+// Path of the received routes: AUTO applies the layer rule to the routes a
+// rank receives on average, rows * top_k / world (each rank sends its
+// tokens' top_k routes spread over the world).
+int ep_path(const lmoe_layer *l, int rows, int world, int path) {
+    const bool dec = layer_gemv_ok(l);
+    if (path == LMOE_PATH_DECODE) return dec ? 0 : -1;
+    const bool ok = layer_pf_ok(l);
+    if (path == LMOE_PATH_PREFILL) return ok ? 1 : -1;
+    if (path != LMOE_PATH_AUTO) return -1;
+    if (!dec) return ok ? 1 : -1;
+    const long routes = (long)rows * l->router.top_k / world;
+    return ok && routes >= LMOE_PREFILL_MIN_ROUTES &&
+           4 * routes >= (long)LMOE_PREFILL_ROUTES_PER_4_EXPERTS * l->router.n_experts;
+}
+
+// Workspace of the receive side: the routing regions over rows * top_k
+// route slots (no router logits), the decode panels or the prefill panels,
+// and the y*w rows.
+Layout ep_layout(const lmoe_layer *l, int rows, bool pf) {
+    const int H = l->experts.hidden, I = l->experts.inter;
+    const int R = rows * l->router.top_k;
+    const int buckets = l->router.n_experts + 1;
+    if (!pf) return make_layout(rows, R, H, I, H, buckets, 1, 1, rows);
+    Layout L = make_layout(rows, R, H, 0, H, buckets, 1, 1, 0);
+    L.prefill = true;
+    L.pf_chunks = pf_max_chunks(buckets, R);
+    L.pf_rows = pf_panel_rows(R, L.pf_chunks);
+    size_t off = (L.total + 1023) & ~size_t(1023);
+    L.pfx = off;
+    off += (((size_t)L.pf_rows * H * 2) + 1023) & ~size_t(1023);
+    L.pfh = off;
+    off += (((size_t)L.pf_rows * I * 2) + 1023) & ~size_t(1023);
+    L.total = off;
+    return L;
 }
 
 }  // namespace
@@ -889,6 +945,101 @@ int lmoe_tile_pack(const lmoe_qproj *src, int32_t n_slots, int32_t rows, int32_t
     const QView q = view(p, n_slots, rows, cols);
     return cuda_rc(launch_tile_pack(q, src->bits, src->group_size, slot_begin, slot_count,
                                     static_cast<uint8_t *>(tiles), static_cast<cudaStream_t>(stream)));
+}
+
+// ------------------------------------------------------------ expert parallel
+size_t lmoe_ep_row_bytes(int32_t hidden, int32_t top_k) {
+    if (hidden <= 0 || hidden % 8 != 0 || top_k < 1 || top_k > 16) return 0;
+    return (size_t)ep_row_bytes(hidden, top_k);
+}
+
+int lmoe_ep_dispatch(const int32_t *idx, const float *w, const void *x, int32_t tokens, int32_t hidden,
+                     int32_t top_k, int32_t n_experts, int32_t world, void *send, int32_t *slot_of, void *workspace,
+                     void *stream) {
+    if (tokens < 0 || hidden <= 0 || hidden % 8 != 0 || top_k < 1 || top_k > 16) return LMOE_EINVAL;
+    if (world < 1 || world > kEpMaxWorld || n_experts < 1 || n_experts % world != 0) return LMOE_EINVAL;
+    if (tokens == 0) return LMOE_OK;
+    if (!idx || !w || !x || !send || !slot_of || !aligned16(x) || !aligned16(send)) return LMOE_EINVAL;
+    EpDispatchArgs a;
+    a.idx = idx;
+    a.w = w;
+    a.x = static_cast<const uint16_t *>(x);
+    a.T = tokens;
+    a.k = top_k;
+    a.H = hidden;
+    a.E = n_experts;
+    a.world = world;
+    a.send = static_cast<uint8_t *>(send);
+    a.slot_of = slot_of;
+    a.err = static_cast<int32_t *>(workspace);
+    return cuda_rc(launch_ep_dispatch(a, static_cast<cudaStream_t>(stream)));
+}
+
+size_t lmoe_ep_workspace_size(const lmoe_layer *local, int32_t rows, int32_t world, int32_t path) {
+    if (check_ep_local(local) || rows < 0 || world < 1 || world > kEpMaxWorld) return 0;
+    const int n = rows > 0 ? rows : 1;
+    const int pf = ep_path(local, n, world, path);
+    if (pf < 0) return 0;
+    return ep_layout(local, n, pf != 0).total;
+}
+
+int lmoe_ep_experts(const lmoe_layer *local, const void *recv, int32_t rows, int32_t world, float *partial,
+                    void *workspace, size_t ws_bytes, void *stream, int32_t path) {
+    int rc = check_ep_local(local);
+    if (rc) return rc;
+    if (rows < 0 || world < 1 || world > kEpMaxWorld) return LMOE_EINVAL;
+    if (rows == 0) return LMOE_OK;
+    if (!recv || !partial || !workspace || !aligned16(recv) || !aligned16(partial)) return LMOE_EINVAL;
+    const lmoe_experts &ex = local->experts;
+    const int H = ex.hidden, k = local->router.top_k;
+    if (H % 8 != 0) return LMOE_EUNSUPPORTED;
+    const int pf = ep_path(local, rows, world, path);
+    if (pf < 0) return LMOE_EUNSUPPORTED;
+    const Layout L = ep_layout(local, rows, pf != 0);
+    if (ws_bytes < L.total) return LMOE_EWORKSPACE;
+    const int chunk_tok = pf ? kPfNmax : layer_chunk(local, rows);
+    if (chunk_tok < 1) return LMOE_EUNSUPPORTED;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int xs = ep_row_bytes(H, k) / 2;  // elements between received rows
+    int32_t *ridx = at<int32_t>(workspace, L.idx);
+    float *rw = at<float>(workspace, L.w);
+    rc = cuda_rc(launch_ep_unpack(static_cast<const uint8_t *>(recv), rows, H, k, ridx, rw, st));
+    if (rc) return rc;
+    if (!pf) {  // the decode GEMVs read the rows through the activation panel
+        PanelArgs pa;
+        std::memset(&pa, 0, sizeof(pa));
+        pa.x = static_cast<const uint16_t *>(recv);
+        pa.rows = rows;
+        pa.K = H;
+        pa.x_stride = xs;
+        pa.panel = at<uint16_t>(workspace, L.xpanel);
+        pa.sum16 = at<float>(workspace, L.xsum);
+        pa.bits = ex.gate.bits;
+        pa.gs = ex.gate.group_size;
+        pa.act_f16 = ex.dtype == LMOE_F16;
+        rc = cuda_rc(launch_panel(pa, st));
+        if (rc) return rc;
+    }
+    rc = run_dispatch(L, workspace, ridx, rows * k, local->router.n_experts, local->expert_slot, ex.n_slots,
+                      chunk_tok, st, /*drop_zero=*/true);
+    if (rc) return rc;
+    rc = pf ? run_experts_pf(local, L, workspace, recv, rows, rw, nullptr, st, nullptr, xs)
+            : run_experts(local, L, workspace, rows, rw, nullptr, st);
+    if (rc) return rc;
+    return cuda_rc(launch_ep_partial(ex.dtype == LMOE_F16, at<uint16_t>(workspace, L.yw), ridx, rows, H, k,
+                                     local->router.n_experts, partial, st));
+}
+
+int lmoe_ep_combine(const float *back, int32_t tokens, int32_t world, int32_t hidden, int32_t dtype,
+                    const int32_t *slot_of, const void *residual, void *out, void *stream) {
+    if (tokens < 0 || world < 1 || world > kEpMaxWorld || hidden <= 0 || hidden % 8 != 0) return LMOE_EINVAL;
+    if (dtype != LMOE_BF16 && dtype != LMOE_F16) return LMOE_EUNSUPPORTED;
+    if (tokens == 0) return LMOE_OK;
+    if (!back || !slot_of || !out || !aligned16(back) || !aligned16(out) || (residual && !aligned16(residual)))
+        return LMOE_EINVAL;
+    return cuda_rc(launch_ep_combine(dtype == LMOE_F16, back, tokens, world, hidden, slot_of,
+                                     static_cast<const uint16_t *>(residual), static_cast<uint16_t *>(out),
+                                     static_cast<cudaStream_t>(stream)));
 }
 
 }  // extern "C"

@@ -546,16 +546,18 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) gemv_kernel(const GemvArgs
                         a.out[(size_t)route * rows + row] = Act<TA>::from_f(y * wv);
                     }
                 }
-                if (lane < ntok) {
-                    int route = rr[0];
+                if (a.counters) {  // without counters the caller combines the y*w rows
+                    if (lane < ntok) {
+                        int route = rr[0];
 #pragma unroll
-                    for (int q = 0; q < 8; ++q)
-                        if (q == lane) route = rr[q];
-                    list[list_n + lane] = (route / a.top_k) * RT + rt;
+                        for (int q = 0; q < 8; ++q)
+                            if (q == lane) route = rr[q];
+                        list[list_n + lane] = (route / a.top_k) * RT + rt;
+                    }
+                    list_n += ntok;
+                    __syncwarp();
+                    if (list_n + 8 > c.list_cap) flush();
                 }
-                list_n += ntok;
-                __syncwarp();
-                if (list_n + 8 > c.list_cap) flush();
             } else {
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
@@ -575,6 +577,7 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) gemv_kernel(const GemvArgs
             if (list_n > 0) flush();
         }
         if constexpr (MODE == MODE_DOWN2) {
+            if (!a.combined) return;  // the caller combines the y*w rows
             // Weighted combine of the row pairs this block owns (u = chunk *
             // UT + pair with gridDim.x dividing UT, so the block ran every
             // chunk of pairs blockIdx.x + j * gridDim.x): each token's k y*w

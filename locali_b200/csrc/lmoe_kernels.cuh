@@ -84,6 +84,9 @@ struct DispatchIn {
     int32_t n_experts;           // valid ids are [0, n_experts); others -> zero bucket
     const int32_t *expert_slot;  // [n_experts] or nullptr (identity: id is the slot)
     int32_t n_slots;
+    // expert-parallel receive side: negative ids are routes owned by another
+    // rank (dropped without an error) and the zero bucket gets no chunks
+    int32_t drop_zero = 0;
 };
 
 struct RouterArgs {
@@ -134,6 +137,7 @@ struct TopkArgs {
 struct PanelArgs {
     const uint16_t *x;  // natural [rows, K]
     int32_t rows, K;
+    int32_t x_stride;   // elements between rows of x (0: K)
     uint16_t *panel;    // [rows, K]
     float *sum16;       // [rows, K/16, 2] (sum of x, sum of panel values)
     int32_t bits, gs;
@@ -267,6 +271,7 @@ inline int pf_max_chunks(int buckets, int R) {
 struct PfPanelArgs {
     const uint16_t *x;  // [rows of x, K]
     int32_t K;
+    int32_t x_stride;   // elements between rows of x (0: K)
     int32_t route_div;  // route r reads x row r / route_div
     const Chunk *chunks;
     const int32_t *n_chunks;
@@ -312,6 +317,29 @@ cudaError_t launch_pf_panel(const PfPanelArgs &a, int max_chunks, cudaStream_t s
 cudaError_t launch_pf_gemm(int mode, int act_f16, int bits, int gs, const PfArgs &a, cudaStream_t st);
 cudaError_t launch_pf_combine(int act_f16, const uint16_t *yw, int T, int H, int top_k, uint16_t *out,
                               cudaStream_t st);
+
+// ------------------------------------------------------------ expert parallel (lmoe_ep.cu)
+constexpr int kEpMaxWorld = 32;
+// trailer of one exchanged row: int32 ids[k], fp32 w[k], int32 token, zero
+// padding to a multiple of 16 bytes
+__host__ __device__ inline int ep_trailer_bytes(int k) { return (8 * k + 4 + 15) / 16 * 16; }
+__host__ __device__ inline int ep_row_bytes(int H, int k) { return 2 * H + ep_trailer_bytes(k); }
+
+struct EpDispatchArgs {
+    const int32_t *idx;  // [T, k] global expert ids
+    const float *w;      // [T, k] combine weights
+    const uint16_t *x;   // [T, H] activations
+    int32_t T, k, H, E, world;
+    uint8_t *send;     // [world][T][ep_row_bytes]
+    int32_t *slot_of;  // [T][world]: slot of token t in destination d's rows, -1 if none
+    int32_t *err;
+};
+cudaError_t launch_ep_dispatch(const EpDispatchArgs &a, cudaStream_t st);
+cudaError_t launch_ep_unpack(const uint8_t *recv, int rows, int H, int k, int32_t *idx, float *w, cudaStream_t st);
+cudaError_t launch_ep_partial(int act_f16, const uint16_t *yw, const int32_t *idx, int rows, int H, int k,
+                              int n_local, float *partial, cudaStream_t st);
+cudaError_t launch_ep_combine(int act_f16, const float *back, int T, int world, int H, const int32_t *slot_of,
+                              const uint16_t *residual, uint16_t *out, cudaStream_t st);
 
 constexpr int kDispatchSmallMaxRoutes = 512;
 constexpr int kDispatchSmallMaxBuckets = 1024;

@@ -406,7 +406,8 @@ __global__ void __launch_bounds__(256) pf_panel_kernel(const PfPanelArgs a) {
     for (int j = threadIdx.x >> 3; j < N; j += 32) {
         const int pr = pbase + j;
         const uint16_t *src = nullptr;
-        if (j < ch.ntok) src = a.x + (size_t)(a.sorted_routes[ch.route_start + j] / a.route_div) * a.K;
+        if (j < ch.ntok)
+            src = a.x + (size_t)(a.sorted_routes[ch.route_start + j] / a.route_div) * (a.x_stride ? a.x_stride : a.K);
         for (int at = a0; at < a1; ++at) {
             uint4 v = make_uint4(0u, 0u, 0u, 0u);
             if (src) v = pf_perm_chunk<BITS>(src + at * 64, h);

@@ -61,19 +61,20 @@ __device__ void dispatch_block(const DispatchIn &din, const DispatchOut &dout, i
         int b = id;
         if (id < 0 || id >= E) {
             b = E;
-            set_error(err, -3);
+            if (!(din.drop_zero && id < 0)) set_error(err, -3);
         }
         s_b[r] = b;
         atomicAdd(&s_cnt[b], 1);
     }
     __syncthreads();
     const int per = (NBk + 255) >> 8;
+    auto nchunks = [&](int b) { return (din.drop_zero && b == E) ? 0 : (s_cnt[b] + din.chunk_tok - 1) / din.chunk_tok; };
     int lr = 0, lc = 0;
     for (int q = 0; q < per; ++q) {
         const int b = tid * per + q;
         if (b < NBk) {
             lr += s_cnt[b];
-            lc += (s_cnt[b] + din.chunk_tok - 1) / din.chunk_tok;
+            lc += nchunks(b);
         }
     }
     int tr, tc;
@@ -85,7 +86,7 @@ __device__ void dispatch_block(const DispatchIn &din, const DispatchOut &dout, i
             s_roff[b] = er;
             s_coff[b] = ec;
             er += s_cnt[b];
-            ec += (s_cnt[b] + din.chunk_tok - 1) / din.chunk_tok;
+            ec += nchunks(b);
         }
     }
     __syncthreads();
@@ -95,7 +96,7 @@ __device__ void dispatch_block(const DispatchIn &din, const DispatchOut &dout, i
         for (int r2 = 0; r2 < r; ++r2) rank += (s_b[r2] == b);
         const int pos = s_roff[b] + rank;
         dout.sorted_routes[pos] = r;
-        if ((rank % din.chunk_tok) == 0) {
+        if ((rank % din.chunk_tok) == 0 && !(din.drop_zero && b == E)) {
             int slot = 0;
             if (b < E) {
                 slot = din.expert_slot ? din.expert_slot[b] : b;
@@ -129,13 +130,15 @@ __device__ void dispatch_warp(const DispatchIn &din, const DispatchOut &dout, in
         b = id;
         if (id < 0 || id >= E) {
             b = E;
-            set_error(err, -3);
+            if (!(din.drop_zero && id < 0)) set_error(err, -3);
         }
     }
     const unsigned same = __match_any_sync(LMOE_FULL, b);
     const int rank = __popc(same & ((1u << lane) - 1u));
     const int cnt = __popc(same);
-    const int nch = rank == 0 ? (cnt + ct - 1) / ct : 0;  // bucket leaders carry the chunk count
+    const bool dropped = din.drop_zero && b == E;
+    // bucket leaders carry the chunk count
+    const int nch = (rank == 0 && !dropped) ? (cnt + ct - 1) / ct : 0;
     int before_r = 0, before_c = 0, total_c = 0;
     for (int j = 0; j < R; ++j) {
         const int bj = __shfl_sync(LMOE_FULL, b, j);
@@ -147,7 +150,7 @@ __device__ void dispatch_warp(const DispatchIn &din, const DispatchOut &dout, in
     if (lane < R) {
         const int pos = before_r + rank;
         dout.sorted_routes[pos] = lane;
-        if (rank % ct == 0) {
+        if (rank % ct == 0 && !dropped) {
             int slot = 0;
             if (b < E) {
                 slot = s_slot ? s_slot[b] : (din.expert_slot ? din.expert_slot[b] : b);
@@ -193,8 +196,8 @@ __global__ void __launch_bounds__(256) dispatch_rank_kernel(DispatchIn din, Disp
     for (int r = tid; r < din.R; r += blockDim.x) {
         int id = din.idx[r];
         if (id < 0 || id >= E) {
+            if (b == 0 && !(din.drop_zero && id < 0)) set_error(err, -3);
             id = E;
-            if (b == 0) set_error(err, -3);
         }
         lt += (id < b);
         eq += (id == b);
@@ -229,16 +232,18 @@ __global__ void __launch_bounds__(256) dispatch_chunks_kernel(DispatchIn din, Di
     const int NBk = din.n_experts + 1;
     const int tid = threadIdx.x;
     const int per = (NBk + 255) >> 8;
+    // the zero bucket of an expert-parallel receive side gets no chunks
+    const int NBc = din.drop_zero ? din.n_experts : NBk;
     int lc = 0;
     for (int q = 0; q < per; ++q) {
         const int b = tid * per + q;
-        if (b < NBk) lc += (dout.counts[b] + din.chunk_tok - 1) / din.chunk_tok;
+        if (b < NBc) lc += (dout.counts[b] + din.chunk_tok - 1) / din.chunk_tok;
     }
     int tc;
     int ec = block_scan_256(lc, s_tmp, &tc);
     for (int q = 0; q < per; ++q) {
         const int b = tid * per + q;
-        if (b >= NBk) continue;
+        if (b >= NBc) continue;
         const int cnt = dout.counts[b];
         int slot = 0;
         if (b < din.n_experts && cnt > 0) {
@@ -935,7 +940,7 @@ __global__ void __launch_bounds__(256) router_logits_mma_kernel(RouterArgs a) {
 __device__ __forceinline__ int dispatch_bucket(const DispatchIn &din, int r, int32_t *err) {
     const int id = din.idx[r];
     if (id < 0 || id >= din.n_experts) {
-        set_error(err, -3);
+        if (!(din.drop_zero && id < 0)) set_error(err, -3);
         return din.n_experts;
     }
     return id;
@@ -1062,7 +1067,7 @@ __global__ void __launch_bounds__(256) panel_kernel(PanelArgs a) {
     }
     const int row = blockIdx.x;
     const int col = blockIdx.y * 256 + threadIdx.x;
-    const uint16_t *src = a.x + (size_t)row * a.K;
+    const uint16_t *src = a.x + (size_t)row * (a.x_stride ? a.x_stride : a.K);
     if (col < a.K) {
         int p;
         const int pos = panel_pos(col, a.bits, a.gs, &p);

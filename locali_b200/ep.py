@@ -1,36 +1,41 @@
 """Expert-parallel routed-MoE layer: experts sharded over ranks.
 
-Rank r owns experts ``[r*E/N, (r+1)*E/N)`` in its own HBM arena; the router
-weights are replicated and every rank routes its own tokens (data parallel).
-One layer step:
+Rank r owns experts ``[r*E/N, (r+1)*E/N)`` of every layer in its own HBM
+arena; the router weights are replicated and every rank routes its own
+tokens (the same number of tokens on every rank).  One layer step, all on
+the device with no host wait (include/lmoe.h, lmoe_ep_*):
 
 1. route the local tokens (``lmoe_route``);
-2. plan the dispatch: a token goes once to every rank that owns at least one
-   of its experts, with its local expert ids there and their combine weights
-   (``-1`` / 0 for routes owned elsewhere);
-3. exchange counts, token rows and route metadata (all-to-all);
-4. run the received routes through the local experts (one
-   ``lmoe_moe_routed`` call, one route per entry) and sum each received row's
-   routes in route order in fp32;
-5. send the fp32 partial rows home (all-to-all) and add them per token in
-   rank order, then round once.
+2. ``lmoe_ep_dispatch``: for every destination rank, the rows of the tokens
+   with an expert there, each carrying its local expert ids and weights, in
+   token order, then padding rows (a fixed ``T`` rows per rank pair);
+3. NCCL ``all_to_all_single`` of the rows (equal splits);
+4. ``lmoe_ep_experts``: the received routes through the local experts (the
+   decode GEMVs or the tcgen05 grouped GEMM), each row's rounded ``y*w``
+   terms summed in route order in fp32;
+5. NCCL ``all_to_all_single`` of the fp32 partial rows back (equal splits);
+6. ``lmoe_ep_combine``: per token, the partials of its owning ranks added in
+   rank order, rounded once (plus an optional residual).
 
-The reference runs every expert on one device (``arena.py:508-672``); this
-module is the expert-parallel deployment of the same layer (no counterpart
-in the reference).  The per-rank phases are plain methods so the same code
-runs under ``torch.distributed`` (:class:`ExpertParallelMoE`, NCCL on GPUs,
-gloo in the CPU tests) and under a single-process loopback that emulates N
-ranks (:func:`loopback_forward`).
+Every buffer has a fixed size, so a step can be captured in a CUDA graph
+with its NCCL calls.  The reference runs every expert on one device
+(``arena.py:508-672``); this module is the expert-parallel deployment of
+the same layer (no counterpart in the reference).  The per-rank operations
+are methods of :class:`EPRank`, so the same :class:`ExpertParallelMoE`
+sequencing runs with NCCL on GPUs, with gloo in the CPU tests (where a test
+rank object supplies the four operations), and as a single-process
+loopback that emulates N ranks (:func:`loopback_forward`).
 """
 
 from __future__ import annotations
 
-from dataclasses import dataclass
-from typing import Callable, Sequence
+import ctypes
+from typing import Sequence
 
 import torch
 
-from . import ops
+from . import _lib, ops
+from ._lib import check, lmoe
 
 
 def owned_range(n_experts: int, rank: int, world: int) -> tuple[int, int]:
@@ -55,196 +60,157 @@ def shard_experts(experts: ops.ExpertArrays, rank: int, world: int, n_experts: i
     return ops.ExpertArrays(cut(experts.gate), cut(experts.up), cut(experts.down))
 
 
-@dataclass
-class DispatchPlan:
-    tok: torch.Tensor          # [S] token of each sent row, grouped by destination rank
-    send_counts: list[int]     # rows per destination rank
-    rows: torch.Tensor         # [S, H] the token rows
-    meta: torch.Tensor         # [S, 2k] int32: local expert ids (-1 = elsewhere), fp32 weight bits
-
-
-def plan_dispatch(x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, n_experts: int, world: int) -> DispatchPlan:
-    """Step 2: one row per (token, destination rank that owns one of its
-    experts), in (destination, token) order."""
-    T, k = idx.shape
-    per = n_experts // world
-    idx = idx.to(torch.int64)
-    owner = idx // per                                            # [T, k]
-    ranks = torch.arange(world, device=idx.device)
-    hits = (owner.unsqueeze(-1) == ranks).any(1)                  # [T, world]
-    dst, tok = hits.t().nonzero(as_tuple=True)                    # destination-major, then token
-    own = owner[tok] == dst.unsqueeze(1)                          # [S, k]
-    local = torch.where(own, idx[tok] - dst.unsqueeze(1) * per, torch.full_like(idx[tok], -1))
-    wsel = torch.where(own, w[tok].to(torch.float32), torch.zeros_like(w[tok], dtype=torch.float32))
-    meta = torch.cat([local.to(torch.int32), wsel.view(torch.int32)], dim=1)
-    counts = hits.sum(0).tolist()
-    return DispatchPlan(tok, counts, x[tok], meta)
-
-
-def dispatch_counts(idx: torch.Tensor, n_experts: int, world: int) -> tuple[torch.Tensor, torch.Tensor]:
-    """Per destination rank: the token rows it receives from this rank and
-    the routes those rows carry, as one int64 [world, 2] tensor on the
-    device, together with the token x destination hit mask."""
-    per = n_experts // world
-    owner = idx.to(torch.int64) // per                                            # [T, k]
-    own = owner.unsqueeze(-1) == torch.arange(world, device=idx.device)           # [T, k, world]
-    hits = own.any(1)                                                             # [T, world]
-    return torch.stack([hits.sum(0), own.sum((0, 1))], 1), hits
-
-
-def plan_dispatch_sized(x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, n_experts: int, world: int,
-                        hits: torch.Tensor, send_counts: list[int]) -> DispatchPlan:
-    """plan_dispatch with the per-destination row counts already on the host
-    (no host wait)."""
-    T, k = idx.shape
-    per = n_experts // world
-    idx = idx.to(torch.int64)
-    owner = idx // per
-    dst, tok = torch.nonzero_static(hits.t(), size=sum(send_counts)).unbind(1)
-    own = owner[tok] == dst.unsqueeze(1)
-    local = torch.where(own, idx[tok] - dst.unsqueeze(1) * per, torch.full_like(idx[tok], -1))
-    wsel = torch.where(own, w[tok].to(torch.float32), torch.zeros_like(w[tok], dtype=torch.float32))
-    meta = torch.cat([local.to(torch.int32), wsel.view(torch.int32)], dim=1)
-    return DispatchPlan(tok, list(send_counts), x[tok], meta)
-
-
-def expert_partials(recv_rows: torch.Tensor, recv_meta: torch.Tensor, k: int,
-                    local_fn: Callable[[torch.Tensor, torch.Tensor, torch.Tensor], torch.Tensor],
-                    n_routes: int | None = None) -> torch.Tensor:
-    """Step 4: each received row's routes through the local experts, summed in
-    route order in fp32.  ``local_fn(x [R,H], idx [R,1], w [R,1])`` returns the
-    rounded per-route products ``T(T(y)*T(w))`` [R, H].  Every local (row,
-    route) pair goes through one ``local_fn`` call; the products are placed
-    at their route position and summed over the routes in order 0..k-1
-    (absent routes add exact zeros).  ``n_routes``, the number of local
-    routes when the caller knows it, saves a host wait."""
-    n, H = recv_rows.shape
-    out = torch.zeros((n, H), dtype=torch.float32, device=recv_rows.device)
+def row_bytes(hidden: int, top_k: int) -> int:
+    """Bytes of one exchanged row (``lmoe_ep_row_bytes``)."""
+    n = int(lmoe().lmoe_ep_row_bytes(int(hidden), int(top_k)))
     if n == 0:
-        return out
-    loc = recv_meta[:, :k]
-    wr = recv_meta[:, k:].contiguous().view(torch.float32)
-    if n_routes is None:
-        rows, js = (loc >= 0).nonzero(as_tuple=True)
-    else:
-        rows, js = torch.nonzero_static(loc >= 0, size=n_routes).unbind(1)
-    if rows.numel() == 0:
-        return out
-    y = local_fn(recv_rows[rows], loc[rows, js].unsqueeze(1), wr[rows, js].unsqueeze(1))
-    per_route = torch.zeros((n, k, H), dtype=torch.float32, device=recv_rows.device)
-    per_route[rows, js] = y.float()
-    for j in range(k):  # route order j = 0..k-1, fp32
-        out += per_route[:, j]
-    return out
-
-
-def combine_home(T: int, H: int, tok: torch.Tensor, back: torch.Tensor, send_counts: Sequence[int],
-                 dtype: torch.dtype) -> torch.Tensor:
-    """Step 5: add the partial rows per token in rank order (fp32), round once."""
-    out = torch.zeros((T, H), dtype=torch.float32, device=back.device)
-    start = 0
-    for n in send_counts:  # rank order
-        if n:
-            out[tok[start:start + n]] += back[start:start + n]
-        start += n
-    return out.to(dtype)
+        raise _lib.LmoeError(_lib.LMOE_EINVAL, f"exchange row of hidden {hidden}, top_k {top_k}")
+    return n
 
 
 class EPRank:
-    """The per-rank state: replicated router, local expert shard."""
+    """The per-rank state on the GPU: replicated router, local expert shard
+    (slot ``1 + j`` = local expert ``j``), workspaces."""
 
     def __init__(self, router: ops.RouterArrays, local_experts: ops.ExpertArrays, rank: int, world: int,
-                 n_experts: int, swiglu_limit: float = 10.0, swiglu_mode: str = "fused"):
+                 n_experts: int, swiglu_limit: float = 10.0, swiglu_mode: str = "fused", path: str = "auto"):
+        ops._need_cuda(router.weight, local_experts.gate.weight)
         self.router, self.rank, self.world, self.n_experts = router, rank, world, n_experts
         self.lo, self.hi = owned_range(n_experts, rank, world)
-        n_local = self.hi - self.lo
+        self.n_local = self.hi - self.lo
+        self.top_k = router.top_k
+        self.experts = local_experts
+        self.hidden = local_experts.hidden
+        self.act_dtype = local_experts.dtype
+        self.path = path
         dev = router.weight.device
-        # a top-1 layer over the local experts for the routed products; its
-        # router is never evaluated
-        local_router = ops.RouterArrays(torch.zeros((n_local, router.weight.shape[1]), dtype=torch.bfloat16,
-                                                    device=dev), None, 1)
-        self.slot_table = torch.arange(1, n_local + 1, dtype=torch.int32, device=dev)
-        self.local = ops.MoEKernel(local_router, local_experts, self.slot_table, swiglu_limit, swiglu_mode)
+        self.device = dev
+        self.slot_table = torch.arange(1, self.n_local + 1, dtype=torch.int32, device=dev)
+        # the local layer: the shard's experts with the route width top_k; its
+        # router is never evaluated (weight pointer unused)
+        local_router = _lib.Router(router.weight.data_ptr(), None, self.n_local, int(self.top_k), 0, 1, 1.0)
+        self.local = _lib.Layer(local_router, local_experts.ctype(), self.slot_table.data_ptr(), float(swiglu_limit),
+                                _lib.SWIGLU_MODE[swiglu_mode])
         self.route_ws = ops.Workspace(dev)
+        self.ws = ops.Workspace(dev)
+        self.row_bytes = row_bytes(self.hidden, self.top_k)
 
+    # ---- the four per-rank operations of a step
     def route(self, x: torch.Tensor):
         return ops.route(x, self.router, self.route_ws)
 
-    def local_fn(self, xr: torch.Tensor, ir: torch.Tensor, wr: torch.Tensor) -> torch.Tensor:
-        return self.local.routed(xr, ir, wr)
+    def dispatch(self, idx: torch.Tensor, w: torch.Tensor, x: torch.Tensor, send: torch.Tensor,
+                 slot_of: torch.Tensor) -> None:
+        T = x.shape[0]
+        check(lmoe().lmoe_ep_dispatch(idx.data_ptr(), w.data_ptr(), x.data_ptr(), T, self.hidden, int(self.top_k),
+                                      self.n_experts, self.world, send.data_ptr(), slot_of.data_ptr(),
+                                      self.route_ws.ptr(), ops._stream()), "lmoe_ep_dispatch")
+
+    def workspace_bytes(self, rows: int) -> int:
+        n = int(lmoe().lmoe_ep_workspace_size(ctypes.byref(self.local), int(rows), self.world,
+                                              _lib.PATH[self.path]))
+        if n == 0:
+            raise _lib.LmoeError(_lib.LMOE_EUNSUPPORTED, "expert-parallel local layer")
+        return n
+
+    def experts_partial(self, recv: torch.Tensor, partial: torch.Tensor) -> None:
+        rows = recv.shape[0] if recv.dim() == 2 else recv.shape[0] * recv.shape[1]
+        self.ws.ensure(self.workspace_bytes(rows))
+        check(lmoe().lmoe_ep_experts(ctypes.byref(self.local), recv.data_ptr(), rows, self.world,
+                                     partial.data_ptr(), self.ws.ptr(), self.ws.nbytes, ops._stream(),
+                                     _lib.PATH[self.path]), "lmoe_ep_experts")
+
+    def combine(self, back: torch.Tensor, slot_of: torch.Tensor, out: torch.Tensor,
+                residual: torch.Tensor | None = None) -> None:
+        T = slot_of.shape[0]
+        check(lmoe().lmoe_ep_combine(back.data_ptr(), T, self.world, self.hidden, ops._ACT[self.act_dtype],
+                                     slot_of.data_ptr(), ops._ptr(residual), out.data_ptr(), ops._stream()),
+              "lmoe_ep_combine")
+
+    def buffers(self, T: int) -> dict:
+        """Fixed-size exchange buffers of a step with T tokens per rank."""
+        dev, N, H = self.device, self.world, self.hidden
+        return {
+            "send": torch.empty((N, T, self.row_bytes), dtype=torch.uint8, device=dev),
+            "recv": torch.empty((N, T, self.row_bytes), dtype=torch.uint8, device=dev),
+            "part": torch.empty((N, T, H), dtype=torch.float32, device=dev),
+            "back": torch.empty((N, T, H), dtype=torch.float32, device=dev),
+            "slot_of": torch.empty((T, N), dtype=torch.int32, device=dev),
+        }
+
+    def check(self) -> None:
+        """Synchronise and raise if a kernel flagged a bad expert id or slot."""
+        self.route_ws.check()
+        self.ws.check()
 
 
 class ExpertParallelMoE:
-    """One expert-parallel layer step under ``torch.distributed``."""
+    """One expert-parallel layer step under ``torch.distributed`` (NCCL on
+    GPUs).  ``rank_state`` supplies route / dispatch / experts_partial /
+    combine / buffers (:class:`EPRank` on a GPU).  Every rank calls it with
+    the same number of tokens."""
 
-    def __init__(self, rank_state: EPRank, group=None):
+    def __init__(self, rank_state, group=None):
         self.r = rank_state
         self.group = group
+        self._bufs: dict[int, dict] = {}
 
-    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+    def _exchange(self, dst: torch.Tensor, src: torch.Tensor) -> None:
+        if self.r.world == 1:
+            dst.copy_(src)
+            return
         import torch.distributed as dist
 
+        dist.all_to_all_single(dst, src, group=self.group)
+
+    def __call__(self, x: torch.Tensor, residual: torch.Tensor | None = None,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
         flat = x.reshape(-1, x.shape[-1])
-        T, H = flat.shape
+        if flat.dtype != self.r.act_dtype:
+            flat = flat.to(self.r.act_dtype)
+        flat = flat.contiguous()
+        T = flat.shape[0]
+        b = self._bufs.get(T)
+        if b is None:
+            b = self._bufs[T] = self.r.buffers(T)
         idx, w = self.r.route(flat)
-        k = idx.shape[1]
-        world = self.r.world
-        # rows and routes per destination, exchanged as one [world, 2] tensor;
-        # one host wait then gives every split size of the step
-        cnt, hits = dispatch_counts(idx, self.r.n_experts, world)
-        recv_cnt = torch.empty_like(cnt)
-        dist.all_to_all_single(recv_cnt, cnt, group=self.group)
-        host = torch.cat([cnt.reshape(-1), recv_cnt.reshape(-1)]).tolist()
-        send_counts, rc = host[0:2 * world:2], host[2 * world::2]
-        n_routes = sum(host[2 * world + 1::2])
-        plan = plan_dispatch_sized(flat, idx, w, self.r.n_experts, world, hits, send_counts)
-        recv_rows = flat.new_empty((sum(rc), H))
-        dist.all_to_all_single(recv_rows, plan.rows, rc, plan.send_counts, group=self.group)
-        recv_meta = plan.meta.new_empty((sum(rc), 2 * k))
-        dist.all_to_all_single(recv_meta, plan.meta, rc, plan.send_counts, group=self.group)
-        part = expert_partials(recv_rows, recv_meta, k, self.r.local_fn, n_routes)
-        back = part.new_empty((sum(plan.send_counts), H))
-        dist.all_to_all_single(back, part, plan.send_counts, rc, group=self.group)
-        return combine_home(T, H, plan.tok, back, plan.send_counts, flat.dtype).reshape(x.shape)
+        self.r.dispatch(idx, w, flat, b["send"], b["slot_of"])
+        self._exchange(b["recv"], b["send"])
+        self.r.experts_partial(b["recv"].view(-1, b["recv"].shape[-1]), b["part"])
+        self._exchange(b["back"], b["part"])
+        if out is None:
+            out = torch.empty_like(flat)
+        res = None if residual is None else residual.reshape(flat.shape).to(flat.dtype).contiguous()
+        self.r.combine(b["back"], b["slot_of"], out, res)
+        return out.reshape(x.shape)
 
 
-def loopback_forward(ranks: Sequence, xs: Sequence[torch.Tensor], route_fns=None, local_fns=None,
-                     n_experts: int | None = None) -> list[torch.Tensor]:
+def loopback_forward(ranks: Sequence, xs: Sequence[torch.Tensor],
+                     residuals: Sequence[torch.Tensor] | None = None) -> list[torch.Tensor]:
     """The same step for N ranks emulated in one process (the exchanges are
-    list shuffles).  ``ranks`` are :class:`EPRank` objects, or ``None`` when
-    ``route_fns`` / ``local_fns`` supply the per-rank routing and expert
-    products."""
-    world = len(xs)
-    E = n_experts if n_experts is not None else ranks[0].n_experts
-    plans, ks = [], []
-    for r in range(world):
-        route = route_fns[r] if route_fns else ranks[r].route
-        idx, w = route(xs[r])
-        ks.append(idx.shape[1])
-        plans.append(plan_dispatch(xs[r], idx, w, E, world))
-    k = ks[0]
-    # rows each destination receives, in source-rank order
-    starts = []
-    for p in plans:
-        s, acc = [], 0
-        for n in p.send_counts:
-            s.append(acc)
-            acc += n
-        starts.append(s)
-    backs = [[None] * world for _ in range(world)]
-    for d in range(world):
-        rows = [plans[s].rows[starts[s][d]:starts[s][d] + plans[s].send_counts[d]] for s in range(world)]
-        metas = [plans[s].meta[starts[s][d]:starts[s][d] + plans[s].send_counts[d]] for s in range(world)]
-        fn = local_fns[d] if local_fns else ranks[d].local_fn
-        part = expert_partials(torch.cat(rows), torch.cat(metas), k, fn)
-        o = 0
+    block copies between the ranks' buffers).  ``ranks`` are objects with the
+    :class:`EPRank` operations; every x holds the same number of tokens."""
+    world = len(ranks)
+    T = xs[0].shape[0]
+    if any(x.shape[0] != T for x in xs):
+        raise ValueError("every rank holds the same number of tokens")
+    bufs = [r.buffers(T) for r in ranks]
+    flats = [x.reshape(T, -1).contiguous() for x in xs]
+    for r, b, x in zip(ranks, bufs, flats):
+        idx, w = r.route(x)
+        r.dispatch(idx, w, x, b["send"], b["slot_of"])
+    for d in range(world):  # rank d receives block d of every sender, in sender order
         for s in range(world):
-            n = plans[s].send_counts[d]
-            backs[s][d] = part[o:o + n]
-            o += n
+            bufs[d]["recv"][s].copy_(bufs[s]["send"][d])
+    for r, b in zip(ranks, bufs):
+        r.experts_partial(b["recv"].view(-1, b["recv"].shape[-1]), b["part"])
+    for s in range(world):  # partials of sender s's rows go back to s, in rank order
+        for d in range(world):
+            bufs[s]["back"][d].copy_(bufs[d]["part"][s])
     outs = []
-    for s in range(world):
-        back = torch.cat(backs[s])
-        T, H = xs[s].shape
-        outs.append(combine_home(T, H, plans[s].tok, back, plans[s].send_counts, xs[s].dtype))
+    for i, (r, b, x) in enumerate(zip(ranks, bufs, flats)):
+        out = torch.empty_like(x)
+        res = None if residuals is None else residuals[i].reshape(x.shape).contiguous()
+        r.combine(b["back"], b["slot_of"], out, res)
+        outs.append(out)
     return outs
