@@ -267,7 +267,9 @@ def ep_workload_config(cfg, T, world, n_layers):
         "workload": f"c4 expert-parallel stack: {n_layers} layers of hidden {cfg.hidden}, {cfg.n_experts} experts "
                     f"top-{cfg.top_k}, inter {cfg.inter}, {cfg.bits_gate}/{cfg.bits_up}/{cfg.bits_down}-bit affine "
                     f"g{cfg.group_size}, Zipf routing, routed scaling {cfg.routed_scaling}, T={T} tokens per rank "
-                    f"per layer step, residual add between layers, {cfg.n_experts // world} experts per GPU",
+                    f"per layer step, residual add between layers (the combine adds the residual and writes the "
+                    f"weightless RMSNorm of the stream as the next layer's MoE input), {cfg.n_experts // world} "
+                    f"experts per GPU",
         "global_batch": T * world, "parallelism": f"ep{world}", "layers_cycled": n_layers,
         "l2": f"{n_layers} distinct layers ({n_layers * cfg.n_experts // world * cfg.expert_bytes() / 1e9:.1f} GB "
               "of expert bytes per GPU) cycled",
@@ -584,14 +586,21 @@ def measure_ep(cfg, n_layers, K, W, dev, world, rank, path="auto", phase_steps=N
     n_batches = 4
     g = torch.Generator(device=dev).manual_seed(177 + rank)
     xs = torch.randn((n_batches, T, cfg.hidden), generator=g, device=dev).to(torch.bfloat16)
+    xf = xs.float()
+    xns = (xf * torch.rsqrt(xf.square().mean(-1, keepdim=True) + 1e-6)).to(torch.bfloat16)
+    del xf
+    # the residual stream and its weightless RMSNorm (each layer's MoE input,
+    # written by the previous layer's combine)
     x = torch.empty((T, cfg.hidden), dtype=torch.bfloat16, device=dev)
+    xn = torch.empty_like(x)
 
     def steps(s0, n):
         for s in range(s0, s0 + n):
             li = s % n_layers
             if li == 0:
                 x.copy_(xs[(s // n_layers) % n_batches])
-            mods[li](x, residual=x, out=x)
+                xn.copy_(xns[(s // n_layers) % n_batches])
+            mods[li](xn, residual=x, out=x, normed=xn)
 
     steps(0, max(W, n_layers))  # warm-up: every layer once (sizes workspaces, NCCL communicator)
     torch.cuda.synchronize()
@@ -628,9 +637,10 @@ def measure_ep(cfg, n_layers, K, W, dev, world, rank, path="auto", phase_steps=N
         r, b = m.r, m._bufs[T]
         if li == 0:
             x.copy_(xs[(s_ // n_layers) % n_batches])
+            xn.copy_(xns[(s_ // n_layers) % n_batches])
         ev[s_][0].record()
-        idx, w = r.route(x)
-        r.dispatch(idx, w, x, b["send"], b["slot_of"])
+        idx, w = r.route(xn)
+        r.dispatch(idx, w, xn, b["send"], b["slot_of"])
         ev[s_][1].record()
         m._exchange(b["recv"], b["send"])
         ev[s_][2].record()
@@ -638,7 +648,7 @@ def measure_ep(cfg, n_layers, K, W, dev, world, rank, path="auto", phase_steps=N
         ev[s_][3].record()
         m._exchange(b["back"], b["part"])
         ev[s_][4].record()
-        r.combine(b["back"], b["slot_of"], x, x)
+        r.combine(b["back"], b["slot_of"], x, x, xn)
         ev[s_][5].record()
         idxs.append(idx)
     torch.cuda.synchronize()
@@ -671,8 +681,10 @@ def measure_ep(cfg, n_layers, K, W, dev, world, rank, path="auto", phase_steps=N
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for s_ in range(e2e_steps):
-            x.copy_(xh[s_ % n_batches], non_blocking=True)
-            mods[s_ % n_layers](x, residual=x, out=x)
+            # the step's MoE input rows from the host; the updated residual
+            # stream back to the host
+            xn.copy_(xh[s_ % n_batches], non_blocking=True)
+            mods[s_ % n_layers](xn, residual=x, out=x, normed=xn)
             oh[s_ % n_batches].copy_(x, non_blocking=True)
         e1.record()
         torch.cuda.synchronize()

@@ -207,6 +207,24 @@ int lmoe_moe_layer_hashed(const lmoe_layer *layer, const void *x, int32_t tokens
                           float *w, void *workspace, size_t ws_bytes,
                           void *stream, int32_t path);
 
+/* The patched DeepSeek-V4 MoE block (dsv4_engine.py:255-261: routed +
+ * shared_experts(x)) with the decoder layer's residual add, fused into the
+ * routed layer's combine:
+ *   out = T(residual + T(T(sum_j y_j * w_j) + T(shared(x))))
+ * (T = rounding to the activation dtype; each term as lmoe_moe_layer_path
+ * computes it).  The shared expert is an ordinary SwitchGLU expert stored
+ * in arena slot shared_slot of the same arrays (so with the routed experts'
+ * quantisation), taken by every token with weight 1; shared_slot < 0 leaves
+ * it out.  residual [tokens, hidden] may be NULL and may alias out (an
+ * in-place residual stream); x may alias both.  Workspace:
+ * lmoe_workspace_size_block. */
+int lmoe_moe_block(const lmoe_layer *layer, int32_t shared_slot, const void *x,
+                   int32_t tokens, const void *residual, void *out,
+                   int32_t *idx, float *w, void *workspace, size_t ws_bytes,
+                   void *stream, int32_t path);
+size_t lmoe_workspace_size_block(const lmoe_layer *layer, int32_t max_tokens,
+                                 int32_t path);
+
 /* Workspace bytes for lmoe_moe_layer_path calls of up to max_tokens tokens
  * on `path` (0 when the path is unavailable).  lmoe_workspace_size equals
  * this with LMOE_PATH_AUTO. */
@@ -340,10 +358,14 @@ int lmoe_ep_experts(const lmoe_layer *local, const void *recv, int32_t rows,
  * (rank d's partials in the order of d's received rows); out[t] = the
  * partials of the ranks that own t's experts added in rank order in fp32,
  * rounded once to dtype; with residual [tokens, hidden] (may be NULL),
- * out[t] = dtype(residual[t] + that).  out may alias residual. */
+ * out[t] = dtype(residual[t] + that).  out may alias residual.  With normed
+ * (may be NULL), normed[t] = dtype(out[t] * rsqrt(mean(out[t]^2) + eps)) in
+ * fp32: a weightless RMSNorm of the updated residual stream, the next
+ * layer's MoE input (the decoder's ffn_norm without its weight). */
 int lmoe_ep_combine(const float *back, int32_t tokens, int32_t world,
                     int32_t hidden, int32_t dtype, const int32_t *slot_of,
-                    const void *residual, void *out, void *stream);
+                    const void *residual, void *out, void *normed, float eps,
+                    void *stream);
 
 #ifdef __cplusplus
 }

@@ -84,19 +84,23 @@ Layout make_layout(int T, int R, int K, int I, int H_out, int buckets, int E_rou
     return L;
 }
 
-Layout layer_layout(const lmoe_layer *l, int T) {
+// shared: one more route per token for the block's shared expert (its
+// routes follow the T * top_k routed ones)
+Layout layer_layout(const lmoe_layer *l, int T, bool shared = false) {
     const int H = l->experts.hidden, I = l->experts.inter;
-    const int R = T * l->router.top_k;
-    return make_layout(T, R, H, I, H, l->router.n_experts + 1, l->router.n_experts, 1, T);
+    const int R = T * l->router.top_k + (shared ? T : 0);
+    return make_layout(T, R, H, I, H, l->router.n_experts + 1, l->router.n_experts,
+                       router_ksplit(T, l->router.n_experts, H, l->experts.dtype == LMOE_F16), T);
 }
 
 // Layout of the prefill path: the shared routing regions and the y*w rows
 // of make_layout (no GEMV panels), then the two tiled activation panels.
-Layout prefill_layout(const lmoe_layer *l, int T) {
+Layout prefill_layout(const lmoe_layer *l, int T, bool shared = false) {
     const int H = l->experts.hidden, I = l->experts.inter;
-    const int R = T * l->router.top_k;
-    const int buckets = l->router.n_experts + 1;
-    Layout L = make_layout(T, R, H, 0, H, buckets, l->router.n_experts, 1, 0);
+    const int R = T * l->router.top_k + (shared ? T : 0);
+    const int buckets = l->router.n_experts + 1 + (shared ? 1 : 0);
+    Layout L = make_layout(T, R, H, 0, H, buckets, l->router.n_experts,
+                           router_ksplit(T, l->router.n_experts, H, l->experts.dtype == LMOE_F16), 0);
     L.prefill = true;
     L.pf_chunks = pf_max_chunks(buckets, R);
     L.pf_rows = pf_panel_rows(R, L.pf_chunks);
@@ -229,11 +233,18 @@ int layer_chunk(const lmoe_layer *l, int T) {
     return a < b ? a : b;
 }
 
+// What the combine adds after the routed sum: the shared expert's rows
+// (routes shared_base + t, when shared_base > 0) and a residual.
+struct Extra {
+    int shared_base = 0;
+    const uint16_t *residual = nullptr;
+};
+
 // gate/up + SwiGLU then down + combine over an already dispatched layer.
 // out == nullptr: the down kernel leaves the rounded y*w rows of every
 // computed route in the workspace and combines nothing.
 int run_experts(const lmoe_layer *l, const Layout &L, void *ws, int T, const float *route_w,
-                void *out, cudaStream_t st, cudaEvent_t ev_gateup = nullptr) {
+                void *out, cudaStream_t st, cudaEvent_t ev_gateup = nullptr, Extra extra = Extra()) {
     const lmoe_experts &ex = l->experts;
     const int H = ex.hidden, I = ex.inter, k = l->router.top_k;
     const int ntok_max = layer_chunk(l, T);
@@ -251,6 +262,7 @@ int run_experts(const lmoe_layer *l, const Layout &L, void *ws, int T, const flo
     gu.out_gs = ex.down.group_size;
     gu.limit = l->swiglu_limit;
     gu.swiglu_mode = l->swiglu_mode;
+    gu.shared_base = extra.shared_base;  // the shared expert's routes read token rows
 #ifdef LMOE_PROFILE_TRACE
     gu.trace = g_trace;
     gu.trace_units = g_trace_units;
@@ -270,6 +282,8 @@ int run_experts(const lmoe_layer *l, const Layout &L, void *ws, int T, const flo
     dn.counters = out ? at<uint32_t>(ws, L.cnt) : nullptr;
     dn.combined = static_cast<uint16_t *>(out);
     dn.n_tok = T;
+    dn.shared_base = extra.shared_base;
+    dn.residual = extra.residual;
     // Few tokens: blocks own row pairs and combine locally (no device-wide
     // counters or fences at the tail).  More tokens: row tiles spread over
     // every SM and the counter-based combine.  Without a combine the paired
@@ -287,7 +301,8 @@ int run_experts(const lmoe_layer *l, const Layout &L, void *ws, int T, const flo
 // routes): x rows -> tiled panel, gate/up + SwiGLU on tcgen05 (h straight
 // into the down panel), down on tcgen05 (y*w rows), combine per token.
 int run_experts_pf(const lmoe_layer *l, const Layout &L, void *ws, const void *x, int T, const float *route_w,
-                   void *out, cudaStream_t st, cudaEvent_t ev_gateup = nullptr, int x_stride = 0) {
+                   void *out, cudaStream_t st, cudaEvent_t ev_gateup = nullptr, int x_stride = 0,
+                   Extra extra = Extra()) {
     const lmoe_experts &ex = l->experts;
     const int H = ex.hidden, I = ex.inter, k = l->router.top_k;
     const int f16 = ex.dtype == LMOE_F16;
@@ -296,6 +311,7 @@ int run_experts_pf(const lmoe_layer *l, const Layout &L, void *ws, const void *x
     pa.x = static_cast<const uint16_t *>(x);
     pa.K = H;
     pa.x_stride = x_stride;
+    pa.shared_base = extra.shared_base;
     pa.route_div = k;
     pa.chunks = at<Chunk>(ws, L.chunks);
     pa.n_chunks = at<int32_t>(ws, L.nchunks);
@@ -339,7 +355,8 @@ int run_experts_pf(const lmoe_layer *l, const Layout &L, void *ws, const void *x
     d.route_w = route_w;
     rc = cuda_rc(launch_pf_gemm(PF_DOWN, f16, ex.down.bits, ex.down.group_size, d, st));
     if (rc || !out) return rc;  // out == nullptr: the caller combines the y*w rows
-    return cuda_rc(launch_pf_combine(f16, d.yw, T, H, k, static_cast<uint16_t *>(out), st));
+    return cuda_rc(launch_pf_combine(f16, d.yw, T, H, k, static_cast<uint16_t *>(out), st, extra.shared_base,
+                                     extra.residual));
 }
 
 // The prefill kernels read the row-major arena arrays in 16-byte pieces.
@@ -498,7 +515,7 @@ static int route_impl(const lmoe_router &r, int H, int dtype, const lmoe_layer *
                       const int32_t *hash_idx = nullptr) {
     const int k = r.top_k;
     const int R = T * k;
-    const int ksplit = 1;
+    const int ksplit = router_ksplit(T, r.n_experts, H, dtype == LMOE_F16);
     const int chunk_tok = l ? (L.prefill ? kPfNmax : layer_chunk(l, T)) : kChunkTok;
     if (chunk_tok < 1) return LMOE_EUNSUPPORTED;
     RouterArgs a;
@@ -514,8 +531,11 @@ static int route_impl(const lmoe_router &r, int H, int dtype, const lmoe_layer *
     a.norm_topk = r.norm_topk;
     a.scaling = r.routed_scaling;
     a.partial = at<float>(ws, L.partial);
-    // element-wise scorings are finished by the logit blocks themselves
-    a.scores = r.scoring == LMOE_SCORE_SOFTMAX
+    a.ksplit = ksplit;
+    // element-wise scorings are finished by the logit blocks themselves,
+    // unless the logits are split over the hidden dimension (then the top-k
+    // sums the splits and scores)
+    a.scores = (r.scoring == LMOE_SCORE_SOFTMAX || ksplit > 1)
                    ? nullptr
                    : reinterpret_cast<float2 *>(a.partial + (((size_t)ksplit * T * r.n_experts + 1) & ~size_t(1)));
     if (l) {
@@ -582,7 +602,7 @@ static int route_impl(const lmoe_router &r, int H, int dtype, const lmoe_layer *
         TopkArgs tk;
         tk.partial = a.partial;
         tk.scores = a.scores;
-        tk.ksplit = 1;
+        tk.ksplit = ksplit;
         tk.T = T;
         tk.E = a.E;
         tk.top_k = k;
@@ -614,8 +634,9 @@ int check_router(const lmoe_router *r, int hidden) {
 size_t lmoe_workspace_size_route(const lmoe_router *router, int32_t hidden, int32_t max_tokens) {
     if (check_router(router, hidden) || max_tokens < 0) return 0;
     const int T = max_tokens > 0 ? max_tokens : 1;
+    // the bf16 split count bounds the f16 one (1)
     return make_layout(T, T * router->top_k, 0, 0, 0, router->n_experts + 1, router->n_experts,
-                       1, 0).total;
+                       router_ksplit(T, router->n_experts, hidden, false), 0).total;
 }
 
 static int route_entry(const lmoe_router *router, int32_t hidden, int32_t dtype, const void *x, int32_t tokens,
@@ -626,8 +647,8 @@ static int route_entry(const lmoe_router *router, int32_t hidden, int32_t dtype,
     if (dtype != LMOE_BF16 && dtype != LMOE_F16) return LMOE_EUNSUPPORTED;
     if (tokens < 0 || (tokens > 0 && (!x || !idx || !w || !workspace))) return LMOE_EINVAL;
     if (tokens == 0) return LMOE_OK;
-    const Layout L = make_layout(tokens, tokens * router->top_k, 0, 0, 0, router->n_experts + 1,
-                                 router->n_experts, 1, 0);
+    const Layout L = make_layout(tokens, tokens * router->top_k, 0, 0, 0, router->n_experts + 1, router->n_experts,
+                                 router_ksplit(tokens, router->n_experts, hidden, dtype == LMOE_F16), 0);
     if (ws_bytes < L.total) return LMOE_EWORKSPACE;
     return route_impl(*router, hidden, dtype, nullptr, L, x, tokens, idx, w, workspace,
                       static_cast<cudaStream_t>(stream), hash_idx);
@@ -645,26 +666,43 @@ int lmoe_route(const lmoe_router *router, int32_t hidden, int32_t dtype, const v
     return route_entry(router, hidden, dtype, x, tokens, nullptr, idx, w, workspace, ws_bytes, stream);
 }
 
+// shared_slot >= 0: the block's shared expert lives in that arena slot (same
+// quantisation as the routed experts) and its row is added to the routed
+// sum; residual (may be NULL, may alias out) is added last.
 static int layer_entry(const lmoe_layer *layer, const void *x, int32_t tokens, const int32_t *hash_idx, void *out,
                        int32_t *idx, float *w, void *workspace, size_t ws_bytes, void *stream, int32_t path,
-                       void *ev_routed, void *ev_gateup) {
+                       void *ev_routed, void *ev_gateup, int32_t shared_slot = -1, const void *residual = nullptr) {
     int rc = check_layer(layer);
     if (rc) return rc;
     if (tokens < 0 || (tokens > 0 && (!x || !out || !workspace))) return LMOE_EINVAL;
+    if (shared_slot >= layer->experts.n_slots) return LMOE_EINVAL;
     if (tokens == 0) return LMOE_OK;
     if (!router_hidden_ok(layer->experts.hidden)) return LMOE_EUNSUPPORTED;
     const int pf = choose_path(layer, tokens, path);
     if (pf < 0) return LMOE_EUNSUPPORTED;
-    const Layout L = pf ? prefill_layout(layer, tokens) : layer_layout(layer, tokens);
+    const bool shared = shared_slot >= 0;
+    const Layout L = pf ? prefill_layout(layer, tokens, shared) : layer_layout(layer, tokens, shared);
     if (ws_bytes < L.total) return LMOE_EWORKSPACE;
+    if (residual && !aligned16(residual)) return LMOE_EINVAL;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     rc = route_impl(layer->router, layer->experts.hidden, layer->experts.dtype, layer, L, x, tokens, idx, w,
                     workspace, st, hash_idx);
     if (rc) return rc;
+    Extra ex;
+    ex.residual = static_cast<const uint16_t *>(residual);
+    if (shared) {
+        ex.shared_base = tokens * layer->router.top_k;
+        const int ct = pf ? kPfNmax : layer_chunk(layer, tokens);
+        rc = cuda_rc(launch_shared_chunks(at<Chunk>(workspace, L.chunks), at<int32_t>(workspace, L.nchunks),
+                                          at<int32_t>(workspace, L.sorted), at<float>(workspace, L.w),
+                                          ex.shared_base, tokens, ct, shared_slot, st));
+        if (rc) return rc;
+    }
     if (ev_routed && cudaEventRecord(static_cast<cudaEvent_t>(ev_routed), st) != cudaSuccess) return LMOE_ECUDA;
     const float *rw = at<float>(workspace, L.w);
-    if (pf) return run_experts_pf(layer, L, workspace, x, tokens, rw, out, st, static_cast<cudaEvent_t>(ev_gateup));
-    return run_experts(layer, L, workspace, tokens, rw, out, st, static_cast<cudaEvent_t>(ev_gateup));
+    if (pf)
+        return run_experts_pf(layer, L, workspace, x, tokens, rw, out, st, static_cast<cudaEvent_t>(ev_gateup), 0, ex);
+    return run_experts(layer, L, workspace, tokens, rw, out, st, static_cast<cudaEvent_t>(ev_gateup), ex);
 }
 
 int lmoe_moe_layer_path(const lmoe_layer *layer, const void *x, int32_t tokens, void *out, int32_t *idx, float *w,
@@ -701,6 +739,27 @@ int lmoe_moe_layer_hashed(const lmoe_layer *layer, const void *x, int32_t tokens
     if (tokens > 0 && !hash_idx) return LMOE_EINVAL;
     return layer_entry(layer, x, tokens, hash_idx, out, idx, w, workspace, ws_bytes, stream, path, nullptr,
                        nullptr);
+}
+
+int lmoe_moe_block(const lmoe_layer *layer, int32_t shared_slot, const void *x, int32_t tokens,
+                   const void *residual, void *out, int32_t *idx, float *w, void *workspace, size_t ws_bytes,
+                   void *stream, int32_t path) {
+    return layer_entry(layer, x, tokens, nullptr, out, idx, w, workspace, ws_bytes, stream, path, nullptr, nullptr,
+                       shared_slot < 0 ? -1 : shared_slot, residual);
+}
+
+size_t lmoe_workspace_size_block(const lmoe_layer *layer, int32_t max_tokens, int32_t path) {
+    if (check_layer(layer) || max_tokens < 0) return 0;
+    const int T = max_tokens > 0 ? max_tokens : 1;
+    const int pf = choose_path(layer, T, path);
+    if (pf < 0) return 0;
+    if (path == LMOE_PATH_PREFILL) return prefill_layout(layer, T, true).total;
+    size_t n = layer_layout(layer, T, true).total;
+    if (pf) {
+        const size_t p = prefill_layout(layer, T, true).total;
+        if (p > n) n = p;
+    }
+    return n;
 }
 
 size_t lmoe_workspace_size_path(const lmoe_layer *layer, int32_t max_tokens, int32_t path) {
@@ -1031,15 +1090,17 @@ int lmoe_ep_experts(const lmoe_layer *local, const void *recv, int32_t rows, int
 }
 
 int lmoe_ep_combine(const float *back, int32_t tokens, int32_t world, int32_t hidden, int32_t dtype,
-                    const int32_t *slot_of, const void *residual, void *out, void *stream) {
+                    const int32_t *slot_of, const void *residual, void *out, void *normed, float eps,
+                    void *stream) {
     if (tokens < 0 || world < 1 || world > kEpMaxWorld || hidden <= 0 || hidden % 8 != 0) return LMOE_EINVAL;
     if (dtype != LMOE_BF16 && dtype != LMOE_F16) return LMOE_EUNSUPPORTED;
     if (tokens == 0) return LMOE_OK;
-    if (!back || !slot_of || !out || !aligned16(back) || !aligned16(out) || (residual && !aligned16(residual)))
+    if (!back || !slot_of || !out || !aligned16(back) || !aligned16(out) || (residual && !aligned16(residual)) ||
+        (normed && !aligned16(normed)) || !(eps >= 0.0f))
         return LMOE_EINVAL;
     return cuda_rc(launch_ep_combine(dtype == LMOE_F16, back, tokens, world, hidden, slot_of,
                                      static_cast<const uint16_t *>(residual), static_cast<uint16_t *>(out),
-                                     static_cast<cudaStream_t>(stream)));
+                                     static_cast<uint16_t *>(normed), eps, static_cast<cudaStream_t>(stream)));
 }
 
 }  // extern "C"

@@ -160,54 +160,83 @@ __global__ void __launch_bounds__(256) ep_partial_kernel(const uint16_t *yw, con
     dst[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
 }
 
-// out[t] = T(sum over ranks d, in rank order, of back[d][slot_of[t][d]]);
-// with a residual, out[t] = T(residual[t] + that).
+// One block per token t:
+//   out[t] = T(sum over ranks d, in rank order, of back[d][slot_of[t][d]]);
+//   with a residual, out[t] = T(residual[t] + that);
+//   with normed, normed[t] = T(out[t] * rsqrt(mean(out[t]^2) + eps)), fp32
+//   statistics of the rounded out values (a weightless RMSNorm: the next
+//   layer's MoE input when out is the residual stream).
 template <typename TA>
 __global__ void __launch_bounds__(256) ep_combine_kernel(const float *back, int T, int world, int H,
                                                          const int32_t *slot_of, const uint16_t *residual,
-                                                         uint16_t *out) {
+                                                         uint16_t *out, uint16_t *normed, float eps) {
+    __shared__ int s_slot[kEpMaxWorld];
+    __shared__ float s_red[8];
     pdl_wait();
     pdl_trigger();
+    const int t = blockIdx.x, tid = threadIdx.x;
+    if (tid < world) s_slot[tid] = slot_of[(size_t)t * world + tid];
+    __syncthreads();
     const int per = H >> 3;
-    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= (long)T * per) return;
-    const long t = i / per;
-    const int cc = (int)(i - t * per);
-    float acc[8];
+    float ss = 0.0f;
+    for (int cc = tid; cc < per; cc += blockDim.x) {
+        float acc[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) acc[e] = 0.0f;
-    for (int d = 0; d < world; ++d) {
-        const int s = slot_of[t * world + d];
-        if (s < 0) continue;
-        const float4 *p = reinterpret_cast<const float4 *>(back + ((size_t)d * T + s) * H + (size_t)cc * 8);
-        const float4 v0 = p[0], v1 = p[1];
-        acc[0] += v0.x;
-        acc[1] += v0.y;
-        acc[2] += v0.z;
-        acc[3] += v0.w;
-        acc[4] += v1.x;
-        acc[5] += v1.y;
-        acc[6] += v1.z;
-        acc[7] += v1.w;
-    }
-    float o[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) o[e] = Act<TA>::round(acc[e]);
-    if (residual) {
-        const uint4 v = *reinterpret_cast<const uint4 *>(residual + (size_t)t * H + (size_t)cc * 8);
-        const uint32_t u[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            o[2 * e] += Act<TA>::to_f(static_cast<uint16_t>(u[e] & 0xFFFFu));
-            o[2 * e + 1] += Act<TA>::to_f(static_cast<uint16_t>(u[e] >> 16));
+        for (int e = 0; e < 8; ++e) acc[e] = 0.0f;
+        for (int d = 0; d < world; ++d) {
+            const int s = s_slot[d];
+            if (s < 0) continue;
+            const float4 *p = reinterpret_cast<const float4 *>(back + ((size_t)d * T + s) * H + (size_t)cc * 8);
+            const float4 v0 = p[0], v1 = p[1];
+            acc[0] += v0.x;
+            acc[1] += v0.y;
+            acc[2] += v0.z;
+            acc[3] += v0.w;
+            acc[4] += v1.x;
+            acc[5] += v1.y;
+            acc[6] += v1.z;
+            acc[7] += v1.w;
         }
+        float o[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = Act<TA>::round(acc[e]);
+        if (residual) {
+            const uint4 v = *reinterpret_cast<const uint4 *>(residual + (size_t)t * H + (size_t)cc * 8);
+            const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                o[2 * e] = Act<TA>::round(o[2 * e] + Act<TA>::to_f(static_cast<uint16_t>(u[e] & 0xFFFFu)));
+                o[2 * e + 1] = Act<TA>::round(o[2 * e + 1] + Act<TA>::to_f(static_cast<uint16_t>(u[e] >> 16)));
+            }
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss = fmaf(o[e], o[e], ss);
+        uint4 r;
+        r.x = Act<TA>::pack2(o[0], o[1]);
+        r.y = Act<TA>::pack2(o[2], o[3]);
+        r.z = Act<TA>::pack2(o[4], o[5]);
+        r.w = Act<TA>::pack2(o[6], o[7]);
+        *reinterpret_cast<uint4 *>(out + (size_t)t * H + (size_t)cc * 8) = r;
     }
-    uint4 r;
-    r.x = Act<TA>::pack2(o[0], o[1]);
-    r.y = Act<TA>::pack2(o[2], o[3]);
-    r.z = Act<TA>::pack2(o[4], o[5]);
-    r.w = Act<TA>::pack2(o[6], o[7]);
-    *reinterpret_cast<uint4 *>(out + (size_t)t * H + (size_t)cc * 8) = r;
+    if (!normed) return;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((tid & 31) == 0) s_red[tid >> 5] = ss;
+    __syncthreads();
+    float tot = 0.0f;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) tot += s_red[w];  // fixed order
+    const float inv = rsqrtf(tot / static_cast<float>(H) + eps);
+    // each thread re-reads only the chunks it wrote above
+    for (int cc = tid; cc < per; cc += blockDim.x) {
+        const uint4 v = *reinterpret_cast<const uint4 *>(out + (size_t)t * H + (size_t)cc * 8);
+        const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+        uint32_t q[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+            q[e] = Act<TA>::pack2(Act<TA>::to_f(static_cast<uint16_t>(u[e] & 0xFFFFu)) * inv,
+                                  Act<TA>::to_f(static_cast<uint16_t>(u[e] >> 16)) * inv);
+        *reinterpret_cast<uint4 *>(normed + (size_t)t * H + (size_t)cc * 8) = make_uint4(q[0], q[1], q[2], q[3]);
+    }
 }
 
 cudaError_t launch_ep_dispatch(const EpDispatchArgs &a, cudaStream_t st) {
@@ -234,14 +263,15 @@ cudaError_t launch_ep_partial(int act_f16, const uint16_t *yw, const int32_t *id
 }
 
 cudaError_t launch_ep_combine(int act_f16, const float *back, int T, int world, int H, const int32_t *slot_of,
-                              const uint16_t *residual, uint16_t *out, cudaStream_t st) {
-    const long n = (long)T * (H / 8);
-    if (n <= 0) return cudaSuccess;
-    dim3 grid(static_cast<unsigned>((n + 255) / 256));
+                              const uint16_t *residual, uint16_t *out, uint16_t *normed, float eps,
+                              cudaStream_t st) {
+    if (T <= 0) return cudaSuccess;
+    dim3 grid(static_cast<unsigned>(T));
     if (act_f16)
-        return launch_pdl(ep_combine_kernel<__half>, grid, dim3(256), 0, st, back, T, world, H, slot_of, residual, out);
+        return launch_pdl(ep_combine_kernel<__half>, grid, dim3(256), 0, st, back, T, world, H, slot_of, residual, out,
+                          normed, eps);
     return launch_pdl(ep_combine_kernel<__nv_bfloat16>, grid, dim3(256), 0, st, back, T, world, H, slot_of, residual,
-                      out);
+                      out, normed, eps);
 }
 
 }  // namespace lmoe

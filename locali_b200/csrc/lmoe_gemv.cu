@@ -292,7 +292,11 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) gemv_kernel(const GemvArgs
             // The activation rows already in this stage (from its previous
             // unit) are reused when the new unit needs the same rows in the
             // same order: in decode every unit of a chunk reads one row.
-            const int prow = route >= 0 ? route / a.route_div : -1;
+            // gate/up reads token rows (the shared expert's routes map to their
+            // token); down reads the h row of each route
+            const int prow = route < 0 ? -1
+                             : (MODE == MODE_GATEUP ? route_row(route, a.route_div, a.shared_base)
+                                                    : route / a.route_div);
             bool reuse = false;
             if (pw == 0) {
                 const bool same = lane >= ntok || lane >= 8 || hdr[kHdrPanel + lane] == prow;
@@ -387,7 +391,8 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) gemv_kernel(const GemvArgs
                 if (i < list_n) {
                     const int key = list[i];
                     const unsigned prev = atomicAdd(a.counters + key, 1u);
-                    if (prev == static_cast<unsigned>(a.top_k - 1)) done_key = key;
+                    // the token's routed rows, plus its shared-expert row when present
+                    if (prev == static_cast<unsigned>(a.top_k - (a.shared_base > 0 ? 0 : 1))) done_key = key;
                 }
                 unsigned m = __ballot_sync(LMOE_FULL, done_key >= 0);
                 while (m) {
@@ -404,7 +409,13 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) gemv_kernel(const GemvArgs
                                 a.out + ((size_t)tok * a.top_k + j) * rows + row));
                             sacc += Act<TA>::to_f(v);
                         }
-                        a.combined[(size_t)tok * rows + row] = Act<TA>::from_f(sacc);
+                        const bool sh = a.shared_base > 0;
+                        const uint16_t sv = sh ? __ldcg(reinterpret_cast<const unsigned short *>(
+                                                     a.out + ((size_t)a.shared_base + tok) * rows + row))
+                                               : 0;
+                        const uint16_t rv = a.residual ? a.residual[(size_t)tok * rows + row] : 0;
+                        a.combined[(size_t)tok * rows + row] =
+                            Act<TA>::from_f(combine_finish<TA>(sacc, sh, sv, a.residual != nullptr, rv));
                     }
                     if (lane == 0) a.counters[key] = 0u;
                 }
@@ -552,7 +563,7 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) gemv_kernel(const GemvArgs
 #pragma unroll
                         for (int q = 0; q < 8; ++q)
                             if (q == lane) route = rr[q];
-                        list[list_n + lane] = (route / a.top_k) * RT + rt;
+                        list[list_n + lane] = route_row(route, a.top_k, a.shared_base) * RT + rt;
                     }
                     list_n += ntok;
                     __syncwarp();
@@ -598,7 +609,13 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) gemv_kernel(const GemvArgs
                     for (int r = 0; r < a.top_k; ++r)
                         sacc += Act<TA>::to_f(__ldcg(reinterpret_cast<const unsigned short *>(
                             a.out + ((size_t)tok * a.top_k + r) * rows + row)));
-                    a.combined[(size_t)tok * rows + row] = Act<TA>::from_f(sacc);
+                    const bool sh = a.shared_base > 0;
+                    const uint16_t sv = sh ? __ldcg(reinterpret_cast<const unsigned short *>(
+                                                 a.out + ((size_t)a.shared_base + tok) * rows + row))
+                                           : 0;
+                    const uint16_t rv = a.residual ? a.residual[(size_t)tok * rows + row] : 0;
+                    a.combined[(size_t)tok * rows + row] =
+                        Act<TA>::from_f(combine_finish<TA>(sacc, sh, sv, a.residual != nullptr, rv));
                 }
             }
         }

@@ -119,7 +119,26 @@ struct RouterArgs {
     int32_t zero_words;
     // token-id hash routing: [T, top_k] expert ids replacing the top-k search, or nullptr
     const int32_t *hash_idx;
+    // tensor-core logits split over the hidden dimension (router_ksplit):
+    // block z writes partial[z][T][E]; the top-k sums the splits in order
+    int32_t ksplit;
 };
+
+// Splits of the hidden dimension for the tensor-core router logits: with few
+// tokens the 64-token x 128-expert tiles leave most SMs idle, so each tile's
+// K range is divided over up to KT/4 blocks (at least four 64-column stages
+// each) until about one block per SM.  The partial logits are summed in
+// split order by the top-k (fixed order: deterministic).
+__host__ __device__ inline int router_ksplit(int T, int E, int H, bool act_f16) {
+    if (T <= 64 || act_f16 || T > 1024 || H % 64 != 0) return 1;
+    const int blocks = ((T + 63) / 64) * ((E + 127) / 128);
+    const int KT = H / 64;
+    const int want = (148 + blocks - 1) / blocks;
+    int ks = 1;
+    for (int c = 1; c <= KT / 4 && c <= want; ++c)
+        if (KT % c == 0) ks = c;
+    return ks;
+}
 
 struct TopkArgs {
     const float *partial;
@@ -167,6 +186,11 @@ struct GemvArgs {
     uint32_t *counters;
     uint16_t *combined;
     int32_t *err;
+    // shared expert: routes >= shared_base (> 0 when present) are the shared
+    // expert's, one per token (route shared_base + t reads activation row t);
+    // the combine adds its row after rounding the routed sum, then residual
+    int32_t shared_base;
+    const uint16_t *residual;  // [tokens, rows] or nullptr
 #ifdef LMOE_PROFILE_TRACE
     // per-unit timeline (nanoseconds, %globaltimer) of a profiling build:
     // [block][unit slot][8]
@@ -272,6 +296,7 @@ struct PfPanelArgs {
     const uint16_t *x;  // [rows of x, K]
     int32_t K;
     int32_t x_stride;   // elements between rows of x (0: K)
+    int32_t shared_base;  // routes >= shared_base (> 0) read row route - shared_base
     int32_t route_div;  // route r reads x row r / route_div
     const Chunk *chunks;
     const int32_t *n_chunks;
@@ -316,7 +341,29 @@ bool pf_supported(int K, int rows, int bits, int gs, int mode);
 cudaError_t launch_pf_panel(const PfPanelArgs &a, int max_chunks, cudaStream_t st);
 cudaError_t launch_pf_gemm(int mode, int act_f16, int bits, int gs, const PfArgs &a, cudaStream_t st);
 cudaError_t launch_pf_combine(int act_f16, const uint16_t *yw, int T, int H, int top_k, uint16_t *out,
-                              cudaStream_t st);
+                              cudaStream_t st, int shared_base = 0, const uint16_t *residual = nullptr);
+// appends the shared expert's chunks (routes R .. R + T - 1, weight 1, arena
+// slot `slot`) after the dispatched chunks (lmoe_route.cu)
+cudaError_t launch_shared_chunks(Chunk *chunks, int32_t *n_chunks, int32_t *sorted_routes, float *route_w, int R,
+                                 int T, int chunk_tok, int slot, cudaStream_t st);
+
+// Activation row of a route: routed routes r read row r / route_div; the
+// shared expert's routes (r >= shared_base > 0) read row r - shared_base.
+__host__ __device__ inline int route_row(int r, int route_div, int shared_base) {
+    return (shared_base > 0 && r >= shared_base) ? r - shared_base : r / route_div;
+}
+// Final value of one output element: routed fp32 sum rounded once; with the
+// shared expert's row the sum is rounded again after adding it; with a
+// residual, once more after adding that (dsv4_engine.py:259, routed +
+// shared_experts(x), then the decoder layer's residual add).
+template <typename TA>
+__device__ __forceinline__ float combine_finish(float routed, bool has_shared, uint16_t shared_v, bool has_res,
+                                                uint16_t res_v) {
+    float o = Act<TA>::round(routed);
+    if (has_shared) o = Act<TA>::round(o + Act<TA>::to_f(shared_v));
+    if (has_res) o = Act<TA>::round(Act<TA>::to_f(res_v) + o);
+    return o;
+}
 
 // ------------------------------------------------------------ expert parallel (lmoe_ep.cu)
 constexpr int kEpMaxWorld = 32;
@@ -339,7 +386,8 @@ cudaError_t launch_ep_unpack(const uint8_t *recv, int rows, int H, int k, int32_
 cudaError_t launch_ep_partial(int act_f16, const uint16_t *yw, const int32_t *idx, int rows, int H, int k,
                               int n_local, float *partial, cudaStream_t st);
 cudaError_t launch_ep_combine(int act_f16, const float *back, int T, int world, int H, const int32_t *slot_of,
-                              const uint16_t *residual, uint16_t *out, cudaStream_t st);
+                              const uint16_t *residual, uint16_t *out, uint16_t *normed, float eps,
+                              cudaStream_t st);
 
 constexpr int kDispatchSmallMaxRoutes = 512;
 constexpr int kDispatchSmallMaxBuckets = 1024;

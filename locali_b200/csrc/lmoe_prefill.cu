@@ -407,7 +407,8 @@ __global__ void __launch_bounds__(256) pf_panel_kernel(const PfPanelArgs a) {
         const int pr = pbase + j;
         const uint16_t *src = nullptr;
         if (j < ch.ntok)
-            src = a.x + (size_t)(a.sorted_routes[ch.route_start + j] / a.route_div) * (a.x_stride ? a.x_stride : a.K);
+            src = a.x + (size_t)route_row(a.sorted_routes[ch.route_start + j], a.route_div, a.shared_base) *
+                            (a.x_stride ? a.x_stride : a.K);
         for (int at = a0; at < a1; ++at) {
             uint4 v = make_uint4(0u, 0u, 0u, 0u);
             if (src) v = pf_perm_chunk<BITS>(src + at * 64, h);
@@ -417,9 +418,12 @@ __global__ void __launch_bounds__(256) pf_panel_kernel(const PfPanelArgs a) {
 }
 
 // out[t] = sum over j < k, in route order, of the fp32 values of yw[t*k + j],
-// rounded once (the combine of arena.py:619-624 as the decode kernels do it).
+// rounded once (the combine of arena.py:619-624 as the decode kernels do it);
+// then the shared expert's row yw[shared_base + t] and the residual, each
+// followed by a rounding (combine_finish).
 template <typename TA>
-__global__ void __launch_bounds__(256) pf_combine_kernel(const uint16_t *yw, int T, int H, int k, uint16_t *out) {
+__global__ void __launch_bounds__(256) pf_combine_kernel(const uint16_t *yw, int T, int H, int k, uint16_t *out,
+                                                         int shared_base, const uint16_t *residual) {
     pdl_wait();
     pdl_trigger();
     const int per = H >> 3;
@@ -437,6 +441,19 @@ __global__ void __launch_bounds__(256) pf_combine_kernel(const uint16_t *yw, int
         for (int e = 0; e < 4; ++e) {
             acc[2 * e] += Act<TA>::to_f(static_cast<uint16_t>(w[e] & 0xFFFFu));
             acc[2 * e + 1] += Act<TA>::to_f(static_cast<uint16_t>(w[e] >> 16));
+        }
+    }
+    if (shared_base > 0 || residual) {
+        uint4 s4 = make_uint4(0u, 0u, 0u, 0u), r4 = make_uint4(0u, 0u, 0u, 0u);
+        if (shared_base > 0)
+            s4 = *reinterpret_cast<const uint4 *>(yw + ((size_t)(shared_base + t) * H + (size_t)cc * 8));
+        if (residual) r4 = *reinterpret_cast<const uint4 *>(residual + (size_t)t * H + (size_t)cc * 8);
+        const uint32_t sw[4] = {s4.x, s4.y, s4.z, s4.w}, rw[4] = {r4.x, r4.y, r4.z, r4.w};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const uint16_t sv = static_cast<uint16_t>(e & 1 ? sw[e >> 1] >> 16 : sw[e >> 1] & 0xFFFFu);
+            const uint16_t rv = static_cast<uint16_t>(e & 1 ? rw[e >> 1] >> 16 : rw[e >> 1] & 0xFFFFu);
+            acc[e] = combine_finish<TA>(acc[e], shared_base > 0, sv, residual != nullptr, rv);
         }
     }
     uint4 o;
@@ -991,12 +1008,15 @@ cudaError_t launch_pf_gemm(int mode, int act_f16, int bits, int gs, const PfArgs
 }
 
 cudaError_t launch_pf_combine(int act_f16, const uint16_t *yw, int T, int H, int top_k, uint16_t *out,
-                              cudaStream_t st) {
+                              cudaStream_t st, int shared_base, const uint16_t *residual) {
     const long n = (long)T * (H / 8);
     if (n <= 0) return cudaSuccess;
     dim3 grid(static_cast<unsigned>((n + 255) / 256));
-    if (act_f16) return launch_pdl(pf_combine_kernel<__half>, grid, dim3(256), 0, st, yw, T, H, top_k, out);
-    return launch_pdl(pf_combine_kernel<__nv_bfloat16>, grid, dim3(256), 0, st, yw, T, H, top_k, out);
+    if (act_f16)
+        return launch_pdl(pf_combine_kernel<__half>, grid, dim3(256), 0, st, yw, T, H, top_k, out, shared_base,
+                          residual);
+    return launch_pdl(pf_combine_kernel<__nv_bfloat16>, grid, dim3(256), 0, st, yw, T, H, top_k, out, shared_base,
+                      residual);
 }
 
 }  // namespace lmoe

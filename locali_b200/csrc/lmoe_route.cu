@@ -170,6 +170,41 @@ __device__ void dispatch_warp(const DispatchIn &din, const DispatchOut &dout, in
     if (lane == 0) *dout.n_chunks = total_c;
 }
 
+// The shared expert of a block (dsv4_engine.py:259, routed + shared_experts(x)):
+// one more route per token, routes R .. R + T - 1 in token order with weight
+// 1, in chunks of at most chunk_tok after the dispatched routed chunks.  One
+// block, after the dispatch (it appends to the chunk count).
+__global__ void __launch_bounds__(256) shared_chunks_kernel(Chunk *chunks, int32_t *n_chunks, int32_t *sorted_routes,
+                                                            float *route_w, int R, int T, int ct, int slot) {
+    __shared__ int s_n0;
+    pdl_wait();
+    pdl_trigger();
+    if (threadIdx.x == 0) s_n0 = *n_chunks;
+    __syncthreads();
+    const int n0 = s_n0;
+    for (int t = threadIdx.x; t < T; t += blockDim.x) {
+        sorted_routes[R + t] = R + t;
+        route_w[R + t] = 1.0f;
+    }
+    const int nsc = (T + ct - 1) / ct;
+    for (int c = threadIdx.x; c < nsc; c += blockDim.x) {
+        Chunk ch;
+        ch.slot = slot;
+        ch.route_start = R + c * ct;
+        ch.ntok = min(ct, T - c * ct);
+        ch.expert = -1;
+        chunks[n0 + c] = ch;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) *n_chunks = n0 + nsc;
+}
+
+cudaError_t launch_shared_chunks(Chunk *chunks, int32_t *n_chunks, int32_t *sorted_routes, float *route_w, int R,
+                                 int T, int chunk_tok, int slot, cudaStream_t st) {
+    return launch_pdl(shared_chunks_kernel, dim3(1), dim3(256), 0, st, chunks, n_chunks, sorted_routes, route_w, R, T,
+                      chunk_tok, slot);
+}
+
 __global__ void __launch_bounds__(256) dispatch_small_kernel(DispatchIn din, DispatchOut dout,
                                                              int32_t *err) {
     __shared__ int s_mem[kDispatchSmallMaxRoutes + 3 * (kDispatchSmallMaxBuckets + 1) + 16];
@@ -841,7 +876,10 @@ __global__ void __launch_bounds__(256) router_logits_mma_kernel(RouterArgs a) {
     const int t0 = blockIdx.x * kRlBM, e0 = blockIdx.y * kRlBN;
     const int wm = warp >> 2, wn = warp & 3;
     const uint32_t sb = smem_u32(rl_smem);
-    const int KT = a.H / kRlBK;
+    // split z of the hidden dimension: stages [kt0, kt0 + KT)
+    const int ks = a.ksplit > 1 ? a.ksplit : 1;
+    const int KT = a.H / kRlBK / ks;
+    const int kt0 = static_cast<int>(blockIdx.z) * KT;
     pdl_wait();
     pdl_trigger();
     if (a.zero) {
@@ -850,7 +888,7 @@ __global__ void __launch_bounds__(256) router_logits_mma_kernel(RouterArgs a) {
             a.zero[i] = 0u;
     }
     auto load_stage = [&](int kt) {
-        const int kc = kt * kRlBK;
+        const int kc = (kt0 + kt) * kRlBK;
         const uint32_t base = sb + (uint32_t)((kt % kRlStages) * kRlStage);
         for (int i = tid; i < (kRlBM + kRlBN) * 8; i += 256) {
             const int row = i >> 3, ch = i & 7;
@@ -922,8 +960,8 @@ __global__ void __launch_bounds__(256) router_logits_mma_kernel(RouterArgs a) {
                 const int ex = e0 + wn * 32 + ni * 8 + 2 * tq + (e & 1);
                 if (t >= a.T || ex >= a.E) continue;
                 const float v = acc[mi][ni][e];
-                a.partial[(size_t)t * a.E + ex] = v;
-                if (a.scores) {
+                a.partial[((size_t)blockIdx.z * a.T + t) * a.E + ex] = v;
+                if (a.scores && ks == 1) {
                     const float sc = score_fn(v, a.scoring);
                     a.scores[(size_t)t * a.E + ex] = make_float2(sc, sc + (a.bias ? a.bias[ex] : 0.0f));
                 }
@@ -1137,7 +1175,9 @@ cudaError_t launch_router_logits_mma(const RouterArgs &a, cudaStream_t st) {
         if (e != cudaSuccess) return e;
         configured = true;
     }
-    dim3 grid((a.T + kRlBM - 1) / kRlBM, (a.E + kRlBN - 1) / kRlBN, 1);
+    const int ks = a.ksplit > 1 ? a.ksplit : 1;
+    if (a.H % (kRlBK * ks) != 0) return cudaErrorInvalidValue;
+    dim3 grid((a.T + kRlBM - 1) / kRlBM, (a.E + kRlBN - 1) / kRlBN, ks);
     return launch_pdl(router_logits_mma_kernel, grid, dim3(256), kRlSmem, st, a);
 }
 

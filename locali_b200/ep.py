@@ -121,11 +121,12 @@ class EPRank:
                                      _lib.PATH[self.path]), "lmoe_ep_experts")
 
     def combine(self, back: torch.Tensor, slot_of: torch.Tensor, out: torch.Tensor,
-                residual: torch.Tensor | None = None) -> None:
+                residual: torch.Tensor | None = None, normed: torch.Tensor | None = None,
+                eps: float = 1e-6) -> None:
         T = slot_of.shape[0]
         check(lmoe().lmoe_ep_combine(back.data_ptr(), T, self.world, self.hidden, ops._ACT[self.act_dtype],
-                                     slot_of.data_ptr(), ops._ptr(residual), out.data_ptr(), ops._stream()),
-              "lmoe_ep_combine")
+                                     slot_of.data_ptr(), ops._ptr(residual), out.data_ptr(), ops._ptr(normed),
+                                     float(eps), ops._stream()), "lmoe_ep_combine")
 
     def buffers(self, T: int) -> dict:
         """Fixed-size exchange buffers of a step with T tokens per rank."""
@@ -164,7 +165,9 @@ class ExpertParallelMoE:
         dist.all_to_all_single(dst, src, group=self.group)
 
     def __call__(self, x: torch.Tensor, residual: torch.Tensor | None = None,
-                 out: torch.Tensor | None = None) -> torch.Tensor:
+                 out: torch.Tensor | None = None, normed: torch.Tensor | None = None) -> torch.Tensor:
+        """``out = residual + moe(x)`` (without residual: ``moe(x)``); with
+        ``normed``, also its weightless RMSNorm (the next layer's input)."""
         flat = x.reshape(-1, x.shape[-1])
         if flat.dtype != self.r.act_dtype:
             flat = flat.to(self.r.act_dtype)
@@ -181,7 +184,10 @@ class ExpertParallelMoE:
         if out is None:
             out = torch.empty_like(flat)
         res = None if residual is None else residual.reshape(flat.shape).to(flat.dtype).contiguous()
-        self.r.combine(b["back"], b["slot_of"], out, res)
+        if normed is None:
+            self.r.combine(b["back"], b["slot_of"], out, res)
+        else:
+            self.r.combine(b["back"], b["slot_of"], out, res, normed)
         return out.reshape(x.shape)
 
 

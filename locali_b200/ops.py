@@ -311,6 +311,36 @@ class MoEKernel:
                                          None, None), "lmoe_moe_layer")
         return out.reshape(x.shape)
 
+    def block(self, x: torch.Tensor, shared_slot: int = -1, residual: torch.Tensor | None = None,
+              out: torch.Tensor | None = None, idx: torch.Tensor | None = None,
+              w: torch.Tensor | None = None) -> torch.Tensor:
+        """The DeepSeek-V4 MoE block with the decoder's residual add, fused
+        into the combine (``lmoe_moe_block``): ``residual + (routed +
+        shared_expert(x))``, each sum rounded once.  The shared expert is the
+        expert in arena slot ``shared_slot`` (-1: none); ``residual`` (None:
+        none) may be ``out`` and ``x`` itself (in-place residual stream)."""
+        flat = self._x(x)
+        T = flat.shape[0]
+        if out is None:
+            out = torch.empty_like(flat)
+        res = None
+        if residual is not None:
+            res = residual.reshape(flat.shape)
+            if res.dtype != flat.dtype or not res.is_contiguous():
+                res = res.to(flat.dtype).contiguous()
+        cache = self.__dict__.setdefault("_blk_bytes", {})
+        n = cache.get((T, self.path))
+        if n is None:
+            n = int(lmoe().lmoe_workspace_size_block(ctypes.byref(self.desc), int(T), _lib.PATH[self.path]))
+            if n == 0:
+                raise _lib.LmoeError(_lib.LMOE_EUNSUPPORTED, "layer descriptor")
+            cache[(T, self.path)] = n
+        self.ws.ensure(n)
+        check(lmoe().lmoe_moe_block(ctypes.byref(self.desc), int(shared_slot), flat.data_ptr(), T, _ptr(res),
+                                    out.data_ptr(), _ptr(idx), _ptr(w), self.ws.ptr(), self.ws.nbytes, _stream(),
+                                    _lib.PATH[self.path]), "lmoe_moe_block")
+        return out.reshape(x.shape)
+
     def call_static(self, x: torch.Tensor, out: torch.Tensor | None = None, idx: torch.Tensor | None = None,
                     w: torch.Tensor | None = None) -> torch.Tensor:
         """The layer through ``lmoe_moe_layer_static``: no workspace is

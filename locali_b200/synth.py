@@ -109,8 +109,10 @@ class SynthLayer:
 
 
 def make_layer(cfg: MoEConfig, seed: int = 0, device: str | torch.device = "cpu",
-               dtype: torch.dtype = torch.bfloat16) -> SynthLayer:
-    """All tensors are generated on ``device`` with a generator seeded by ``seed``."""
+               dtype: torch.dtype = torch.bfloat16, extra_slots: int = 0) -> SynthLayer:
+    """All tensors are generated on ``device`` with a generator seeded by
+    ``seed``.  ``extra_slots`` more arena slots after the experts' (slot
+    ``E + 1``: e.g. the block's shared expert) hold random weights too."""
     device = torch.device(device)
     g = torch.Generator(device=device)
     g.manual_seed(seed)
@@ -120,7 +122,7 @@ def make_layer(cfg: MoEConfig, seed: int = 0, device: str | torch.device = "cpu"
     if cfg.zipf:
         rb = rb + zipf_bias(E, g)
     router = RouterArrays(rw, rb.float().contiguous(), cfg.top_k, cfg.scoring, cfg.routed_scaling, True)
-    n_slots = E + 1
+    n_slots = E + 1 + extra_slots
     gate = _qproj(I, H, cfg.bits_gate, cfg.group_size, n_slots, g, dtype)
     up = _qproj(I, H, cfg.bits_up, cfg.group_size, n_slots, g, dtype)
     down = _qproj(H, I, cfg.bits_down, cfg.group_size, n_slots, g, dtype)

@@ -128,3 +128,10 @@ def combine(back: np.ndarray, slot_of: np.ndarray, dtype: str = "bf16", residual
     if residual is not None:
         out = O.round_act(out + np.asarray(residual, np.float32), dtype)
     return out
+
+
+def rms_normed(out: np.ndarray, dtype: str = "bf16", eps: float = 1e-6) -> np.ndarray:
+    """Weightless RMSNorm of the combined rows (fp32 statistics), rounded."""
+    o = np.asarray(out, np.float64)
+    inv = 1.0 / np.sqrt(np.mean(o * o, axis=-1, keepdims=True) + eps)
+    return O.round_act((o * inv).astype(np.float32), dtype)

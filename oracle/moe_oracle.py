@@ -41,7 +41,7 @@ What is restated, and from where (paths within gabrielekarra/locali):
 
 from __future__ import annotations
 
-from dataclasses import dataclass, field
+from dataclasses import dataclass, field, replace
 
 import numpy as np
 
@@ -385,6 +385,27 @@ def moe_layer(x: np.ndarray, layer: LayerNP, idx: np.ndarray | None = None,
         out["ties"] = near_ties(biased, layer.top_k)
     up, gate, h, y = expert_ffn(x, idx, layer, acc, weights)
     out.update(idx=idx, w=w, up=up, gate=gate, h=h, y=y, out=combine(y, w, layer.dtype))
+    return out
+
+
+def moe_block(x: np.ndarray, layer: LayerNP, shared_slot: int | None = None, residual: np.ndarray | None = None,
+              acc=np.float64, weights: str = "exact") -> dict:
+    """The patched V4 MoE block (``dsv4_engine.py:255-261``: ``routed +
+    block.shared_experts(x)``) followed by the decoder layer's residual add.
+    The shared expert is a SwitchGLU expert of the same arena (slot
+    ``shared_slot``) taken by every token; each sum is rounded to the
+    activation dtype: ``T(residual + T(T(routed) + T(shared)))``."""
+    out = moe_layer(x, layer, acc=acc, weights=weights)
+    o = out["out"]
+    T = np.asarray(x).shape[0]
+    if shared_slot is not None:
+        shared_layer = replace(layer, expert_slot=np.array([shared_slot]))
+        _, _, _, ys = expert_ffn(x, np.zeros((T, 1), np.int64), shared_layer, acc, weights)
+        out["shared"] = ys[:, 0]
+        o = round_act(o + ys[:, 0], layer.dtype)
+    if residual is not None:
+        o = round_act(np.asarray(residual, np.float32) + o, layer.dtype)
+    out["block"] = o
     return out
 
 

@@ -61,9 +61,11 @@ class OracleRank:
         p = EO.partials(recv.numpy(), self.H, self.k, self.local)
         partial.copy_(torch.from_numpy(np.nan_to_num(p)).reshape(partial.shape))
 
-    def combine(self, back, slot_of, out, residual=None):
+    def combine(self, back, slot_of, out, residual=None, normed=None):
         o = EO.combine(back.numpy(), slot_of.numpy(), "bf16", None if residual is None else t2np(residual))
         out.copy_(torch.from_numpy(o).to(out.dtype))
+        if normed is not None:
+            normed.copy_(torch.from_numpy(EO.rms_normed(o)).to(normed.dtype))
 
 
 def _layer():

@@ -135,6 +135,30 @@ def test_ep_loopback_prefill_path_and_residual(built):
         assert float(np.mean(t2np(o) != t2np(want))) < 0.02
 
 
+@pytest.mark.parametrize("path,T", [("decode", 24), ("prefill", 128)])
+def test_ep_one_rank_residual_and_norm(built, path, T):
+    """At one rank the expert-parallel step sums each token's routes in the
+    single-GPU combine's order, so with the residual it equals the fused
+    block entry bit for bit; the normed output is the weightless RMSNorm of
+    that result (the next layer's input)."""
+    cfg = synth.config("c2", n_experts=32)
+    layer = synth.make_layer(cfg, seed=17, device="cuda")
+    (r,) = _ranks(layer, cfg, 1, path=path)
+    moe = ep.ExpertParallelMoE(r)
+    x = synth.make_tokens(cfg, T, seed=18, device="cuda")
+    res = synth.make_tokens(cfg, T, seed=19, device="cuda")
+    out, xn = torch.empty_like(x), torch.empty_like(x)
+    moe(x, residual=res, out=out, normed=xn)
+    kern = ops.MoEKernel(layer.router, layer.experts, layer.expert_slot, cfg.swiglu_limit, "fused", path=path)
+    want = kern.block(x, -1, res)
+    torch.cuda.synchronize()
+    r.check()
+    assert torch.equal(out, want)
+    ref = EO.rms_normed(t2np(out))
+    assert O.rel_l2(t2np(xn), ref) < 2e-3
+    assert float(np.mean(t2np(xn) != ref)) < 0.02
+
+
 def _nccl_worker(rank, world, port, out_dir):
     import datetime
 
