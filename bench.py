@@ -268,7 +268,7 @@ def ep_workload_config(cfg, T, world, n_layers):
                     f"top-{cfg.top_k}, inter {cfg.inter}, {cfg.bits_gate}/{cfg.bits_up}/{cfg.bits_down}-bit affine "
                     f"g{cfg.group_size}, Zipf routing, routed scaling {cfg.routed_scaling}, T={T} tokens per rank "
                     f"per layer step, residual add between layers (the combine adds the residual and writes the "
-                    f"weightless RMSNorm of the stream as the next layer's MoE input), {cfg.n_experts // world} "
+                    f"weightless LayerNorm of the stream as the next layer's MoE input), {cfg.n_experts // world} "
                     f"experts per GPU",
         "global_batch": T * world, "parallelism": f"ep{world}", "layers_cycled": n_layers,
         "l2": f"{n_layers} distinct layers ({n_layers * cfg.n_experts // world * cfg.expert_bytes() / 1e9:.1f} GB "
@@ -587,9 +587,11 @@ def measure_ep(cfg, n_layers, K, W, dev, world, rank, path="auto", phase_steps=N
     g = torch.Generator(device=dev).manual_seed(177 + rank)
     xs = torch.randn((n_batches, T, cfg.hidden), generator=g, device=dev).to(torch.bfloat16)
     xf = xs.float()
-    xns = (xf * torch.rsqrt(xf.square().mean(-1, keepdim=True) + 1e-6)).to(torch.bfloat16)
+    xc = xf - xf.mean(-1, keepdim=True)
+    xns = (xc * torch.rsqrt(xc.square().mean(-1, keepdim=True) + 1e-6)).to(torch.bfloat16)
+    del xc
     del xf
-    # the residual stream and its weightless RMSNorm (each layer's MoE input,
+    # the residual stream and its weightless LayerNorm (each layer's MoE input,
     # written by the previous layer's combine)
     x = torch.empty((T, cfg.hidden), dtype=torch.bfloat16, device=dev)
     xn = torch.empty_like(x)

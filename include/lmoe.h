@@ -276,6 +276,28 @@ int lmoe_moe_routed(const lmoe_layer *layer, const void *x, int32_t tokens,
                     const int32_t *idx, const float *w, void *out,
                     void *workspace, size_t ws_bytes, void *stream);
 
+/* The expert products of lmoe_moe_routed without its combine, for the
+ * layer calls the reference splits (ArenaMoE._apply, arena.py:549-672):
+ * for every route r = t * top_k + j with idx[r] >= 0, products[r] =
+ * T(T(y_r) * T(w[r])), or T(y_r) when w is NULL; routes with idx[r] < 0
+ * (another tier's, or not ready yet) are skipped and their rows left as they
+ * were.  products [tokens * top_k, hidden], 16-byte aligned.  Decode GEMVs;
+ * same workspace as lmoe_moe_routed. */
+int lmoe_moe_products(const lmoe_layer *layer, const void *x, int32_t tokens,
+                      const int32_t *idx, const float *w, void *products,
+                      void *workspace, size_t ws_bytes, void *stream);
+
+/* out[t] = T(sum over i < top_k of products[t * top_k + o_i] * w[...] in
+ * fp32), o_i = order[t * top_k + i] (route order when order is NULL; w NULL
+ * = 1).  Without weights: the single-tier combine of rows that lmoe_moe_products
+ * already weighted (arena.py:619-624; lmoe_moe_layer's arithmetic bit for
+ * bit).  With fp32 weights (the routing weights rounded to the activation
+ * dtype) over unweighted rows and a tier-major order: the mixed-tier fp32
+ * scatter-add of y * g (arena.py:632-672). */
+int lmoe_combine_routes(const void *products, const float *w, const int32_t *order,
+                        int32_t tokens, int32_t top_k, int32_t hidden,
+                        int32_t dtype, void *out, void *stream);
+
 /* Fused gate/up products + clamped SwiGLU over arena slots: replaces
  * fused_affine2_swiglu (dsv4_kernels.py:246-300) for 2/4/8-bit and any batch.
  * x [T, hidden]; slots [T, top_k] uint32 arena slots (gather_qmm
@@ -359,9 +381,11 @@ int lmoe_ep_experts(const lmoe_layer *local, const void *recv, int32_t rows,
  * partials of the ranks that own t's experts added in rank order in fp32,
  * rounded once to dtype; with residual [tokens, hidden] (may be NULL),
  * out[t] = dtype(residual[t] + that).  out may alias residual.  With normed
- * (may be NULL), normed[t] = dtype(out[t] * rsqrt(mean(out[t]^2) + eps)) in
- * fp32: a weightless RMSNorm of the updated residual stream, the next
- * layer's MoE input (the decoder's ffn_norm without its weight). */
+ * (may be NULL), normed[t] = dtype((out[t] - mean) * rsqrt(var + eps)) with
+ * fp32 statistics over the row: a weightless LayerNorm of the updated
+ * residual stream, the next layer's MoE input (the decoder's ffn_norm
+ * without its weight; centred so that a common-mode component in the expert
+ * outputs does not steer every token to the same experts). */
 int lmoe_ep_combine(const float *back, int32_t tokens, int32_t world,
                     int32_t hidden, int32_t dtype, const int32_t *slot_of,
                     const void *residual, void *out, void *normed, float eps,

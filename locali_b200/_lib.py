@@ -127,6 +127,10 @@ _SIGS = {
     "lmoe_tile_bytes": ([ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32], ctypes.c_size_t),
     "lmoe_tile_pack": ([ctypes.POINTER(QProj), ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                         ctypes.c_int32, _VP, _VP], ctypes.c_int),
+    "lmoe_moe_products": ([ctypes.POINTER(Layer), _VP, ctypes.c_int32, _VP, _VP, _VP, _VP, ctypes.c_size_t, _VP],
+                          ctypes.c_int),
+    "lmoe_combine_routes": ([_VP, _VP, _VP, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _VP,
+                             _VP], ctypes.c_int),
     "lmoe_moe_block": ([ctypes.POINTER(Layer), ctypes.c_int32, _VP, ctypes.c_int32, _VP, _VP, _VP, _VP, _VP,
                         ctypes.c_size_t, _VP, ctypes.c_int32], ctypes.c_int),
     "lmoe_workspace_size_block": ([ctypes.POINTER(Layer), ctypes.c_int32, ctypes.c_int32], ctypes.c_size_t),

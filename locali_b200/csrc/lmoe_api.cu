@@ -129,9 +129,13 @@ QView view(const lmoe_qproj &p, int n_slots, int rows, int cols) {
     v.sb_slot_stride = (int64_t)rows * v.groups_per_row;
     v.rows = rows;
     v.cols = cols;
-    v.tiles = static_cast<const uint8_t *>(p.tiles);
-    TileGeo tg;
-    v.tile_slot_stride = tile_geo(cols, p.bits, p.group_size, &tg) ? (int64_t)(rows / 16) * tg.TB : 0;
+    // the pre-tiled copy is in the stream format (StreamGeo); without its
+    // geometry there is no copy to read
+    StreamGeo sg;
+    const bool sok = gemv_ok(p.bits, p.group_size) && stream_geo(rows, cols, p.bits, p.group_size, &sg) &&
+                     sg.tg.SB == 16;
+    v.tiles = sok ? static_cast<const uint8_t *>(p.tiles) : nullptr;
+    v.tile_slot_stride = sok ? sg.slot : 0;
     (void)n_slots;
     return v;
 }
@@ -226,11 +230,34 @@ int chunk_for(int mode, int bits, int gs, int K, int cap) {
     return c;
 }
 
+// The stream GEMVs run a projection when its pre-tiled copy is present (in
+// the stream format; view() keeps the pointer only for that geometry); the
+// row-major bulk-copy GEMV runs it otherwise.
+bool gateup_streamed(const lmoe_experts &ex, StreamCfg *c) {
+    const QView g = view(ex.gate, ex.n_slots, ex.inter, ex.hidden), u = view(ex.up, ex.n_slots, ex.inter, ex.hidden);
+    return g.tiles && u.tiles && ex.gate.bits == ex.up.bits && ex.gate.group_size == ex.up.group_size &&
+           stream_config(SMODE_GATEUP, ex.inter, ex.hidden, ex.gate.bits, ex.gate.group_size, false, c);
+}
+bool down_streamed(const lmoe_experts &ex, bool local, StreamCfg *c) {
+    return view(ex.down, ex.n_slots, ex.hidden, ex.inter).tiles &&
+           stream_config(SMODE_PAIR, ex.hidden, ex.inter, ex.down.bits, ex.down.group_size, local, c);
+}
+
+// Routes per chunk: up to 8 (one MMA n-tile), also bounded by the stage plan
+// of the row-major GEMV for the projections it runs.
 int layer_chunk(const lmoe_layer *l, int T) {
     const lmoe_experts &ex = l->experts;
-    const int a = chunk_for(MODE_GATEUP, ex.gate.bits, ex.gate.group_size, ex.hidden, T);
-    const int b = chunk_for(MODE_DOWN, ex.down.bits, ex.down.group_size, ex.inter, T);
-    return a < b ? a : b;
+    StreamCfg sc;
+    int c = T < kChunkTok ? T : kChunkTok;
+    if (!gateup_streamed(ex, &sc)) {
+        const int a = chunk_for(MODE_GATEUP, ex.gate.bits, ex.gate.group_size, ex.hidden, T);
+        if (a < c) c = a;
+    }
+    if (!down_streamed(ex, false, &sc)) {
+        const int b = chunk_for(MODE_DOWN, ex.down.bits, ex.down.group_size, ex.inter, T);
+        if (b < c) c = b;
+    }
+    return c;
 }
 
 // What the combine adds after the routed sum: the shared expert's rows
@@ -238,6 +265,7 @@ int layer_chunk(const lmoe_layer *l, int T) {
 struct Extra {
     int shared_base = 0;
     const uint16_t *residual = nullptr;
+    uint16_t *yw = nullptr;  // caller buffer for the per-route rows (default: the workspace's)
 };
 
 // gate/up + SwiGLU then down + combine over an already dispatched layer.
@@ -267,8 +295,17 @@ int run_experts(const lmoe_layer *l, const Layout &L, void *ws, int T, const flo
     gu.trace = g_trace;
     gu.trace_units = g_trace_units;
 #endif
-    int rc = cuda_rc(launch_gemv(MODE_GATEUP, ex.dtype == LMOE_F16, ex.gate.bits, ex.gate.group_size,
-                                 gu, L.max_chunks, st));
+    const int f16 = ex.dtype == LMOE_F16;
+    int rc;
+    StreamCfg sc;
+    if (gateup_streamed(ex, &sc)) {
+        rc = cuda_rc(launch_stream(SMODE_GATEUP, f16, ex.gate.bits, ex.gate.group_size, gu, sc, L.max_chunks, st));
+    } else {
+        // row-major arrays through the bulk-copy GEMV
+        if (!ex.gate.weight || !ex.up.weight) return LMOE_EINVAL;
+        gu.q0.tiles = gu.q1.tiles = nullptr;
+        rc = cuda_rc(launch_gemv(MODE_GATEUP, f16, ex.gate.bits, ex.gate.group_size, gu, L.max_chunks, st));
+    }
     if (rc) return rc;
     if (ev_gateup && cudaEventRecord(ev_gateup, st) != cudaSuccess) return LMOE_ECUDA;
     GemvArgs dn = gemv_base(L, ws, ex.n_slots, ntok_max);
@@ -276,7 +313,7 @@ int run_experts(const lmoe_layer *l, const Layout &L, void *ws, int T, const flo
     dn.panel = at<uint16_t>(ws, L.hpanel);
     dn.sum16 = at<float>(ws, L.hsum);
     dn.route_div = 1;
-    dn.out = at<uint16_t>(ws, L.yw);
+    dn.out = extra.yw ? extra.yw : at<uint16_t>(ws, L.yw);
     dn.route_w = route_w;
     dn.top_k = k;
     dn.counters = out ? at<uint32_t>(ws, L.cnt) : nullptr;
@@ -284,6 +321,26 @@ int run_experts(const lmoe_layer *l, const Layout &L, void *ws, int T, const flo
     dn.n_tok = T;
     dn.shared_base = extra.shared_base;
     dn.residual = extra.residual;
+    if (down_streamed(ex, false, &sc)) {
+        // Few tokens: blocks own row pairs and combine locally.  More
+        // tokens (or no combine): units spread over every SM, then the
+        // route-order combine kernel (the same arithmetic).
+        StreamCfg lc;
+        const int grid = down2_grid(sc.pairs);
+        if (out && T <= kDown2MaxTokens && grid > 0 && down_streamed(ex, true, &lc)) {
+            lc.grid = grid;
+            dn.counters = nullptr;
+            return cuda_rc(launch_stream(SMODE_PAIR, f16, ex.down.bits, ex.down.group_size, dn, lc, L.max_chunks, st));
+        }
+        dn.counters = nullptr;
+        dn.combined = nullptr;
+        rc = cuda_rc(launch_stream(SMODE_PAIR, f16, ex.down.bits, ex.down.group_size, dn, sc, L.max_chunks, st));
+        if (rc || !out) return rc;
+        return cuda_rc(launch_pf_combine(f16, dn.out, T, H, k, static_cast<uint16_t *>(out), st, extra.shared_base,
+                                         extra.residual));
+    }
+    if (!ex.down.weight) return LMOE_EINVAL;
+    dn.q0.tiles = nullptr;  // row-major arrays through the bulk-copy GEMV
     // Few tokens: blocks own row pairs and combine locally (no device-wide
     // counters or fences at the tail).  More tokens: row tiles spread over
     // every SM and the counter-based combine.  Without a combine the paired
@@ -858,12 +915,16 @@ int lmoe_static_status(void *stream) {
     return lmoe_workspace_status(ws, stream);
 }
 
-int lmoe_moe_routed(const lmoe_layer *layer, const void *x, int32_t tokens, const int32_t *idx,
-                    const float *w, void *out, void *workspace, size_t ws_bytes, void *stream) {
+// Routing supplied by the caller through the decode GEMVs.  out != nullptr:
+// the combined layer output; otherwise the per-route rows go to products
+// (routes with a negative id skipped, w == nullptr: unit weights).
+static int routed_impl(const lmoe_layer *layer, const void *x, int32_t tokens, const int32_t *idx, const float *w,
+                       void *out, void *products, void *workspace, size_t ws_bytes, void *stream) {
     int rc = check_layer(layer);
     if (rc) return rc;
     if (!layer_gemv_ok(layer)) return LMOE_EUNSUPPORTED;  // the decode GEMVs (2/4/8-bit)
-    if (tokens < 0 || (tokens > 0 && (!x || !idx || !w || !out || !workspace))) return LMOE_EINVAL;
+    if (tokens < 0 || (tokens > 0 && (!x || !idx || (!w && out) || (!out && !products) || !workspace)))
+        return LMOE_EINVAL;
     if (tokens == 0) return LMOE_OK;
     const Layout L = layer_layout(layer, tokens);
     if (ws_bytes < L.total) return LMOE_EWORKSPACE;
@@ -886,9 +947,35 @@ int lmoe_moe_routed(const lmoe_layer *layer, const void *x, int32_t tokens, cons
     const int R = tokens * layer->router.top_k;
     const int ct = layer_chunk(layer, tokens);
     if (ct < 1) return LMOE_EUNSUPPORTED;
-    rc = run_dispatch(L, workspace, idx, R, layer->router.n_experts, layer->expert_slot, ex.n_slots, ct, st);
+    rc = run_dispatch(L, workspace, idx, R, layer->router.n_experts, layer->expert_slot, ex.n_slots, ct, st,
+                      /*drop_zero=*/out == nullptr);
     if (rc) return rc;
-    return run_experts(layer, L, workspace, tokens, w, out, st);
+    Extra e;
+    e.yw = static_cast<uint16_t *>(products);
+    return run_experts(layer, L, workspace, tokens, w, out, st, nullptr, e);
+}
+
+int lmoe_moe_routed(const lmoe_layer *layer, const void *x, int32_t tokens, const int32_t *idx,
+                    const float *w, void *out, void *workspace, size_t ws_bytes, void *stream) {
+    if (tokens > 0 && !out) return LMOE_EINVAL;
+    return routed_impl(layer, x, tokens, idx, w, out, nullptr, workspace, ws_bytes, stream);
+}
+
+int lmoe_moe_products(const lmoe_layer *layer, const void *x, int32_t tokens, const int32_t *idx, const float *w,
+                      void *products, void *workspace, size_t ws_bytes, void *stream) {
+    if (tokens > 0 && (!products || !aligned16(products))) return LMOE_EINVAL;
+    return routed_impl(layer, x, tokens, idx, w, nullptr, products, workspace, ws_bytes, stream);
+}
+
+int lmoe_combine_routes(const void *products, const float *w, const int32_t *order, int32_t tokens, int32_t top_k,
+                        int32_t hidden, int32_t dtype, void *out, void *stream) {
+    if (tokens < 0 || top_k < 1 || top_k > 16 || hidden <= 0 || hidden % 8 != 0) return LMOE_EINVAL;
+    if (dtype != LMOE_BF16 && dtype != LMOE_F16) return LMOE_EUNSUPPORTED;
+    if (tokens == 0) return LMOE_OK;
+    if (!products || !out || !aligned16(products) || !aligned16(out)) return LMOE_EINVAL;
+    return cuda_rc(launch_combine_routes(dtype == LMOE_F16, static_cast<const uint16_t *>(products), w, order, tokens,
+                                         top_k, hidden, static_cast<uint16_t *>(out),
+                                         static_cast<cudaStream_t>(stream)));
 }
 
 int lmoe_gateup_swiglu(const lmoe_experts *experts, const void *x, int32_t tokens, int32_t top_k,
@@ -926,7 +1013,10 @@ int lmoe_gateup_swiglu(const lmoe_experts *experts, const void *x, int32_t token
     pa.act_f16 = experts->dtype == LMOE_F16;
     rc = cuda_rc(launch_panel(pa, st));
     if (rc) return rc;
-    const int ntok_max = chunk_for(MODE_GATEUP, experts->gate.bits, experts->gate.group_size, H, tokens);
+    StreamCfg sc;
+    const bool streamed = gateup_streamed(*experts, &sc);
+    const int ntok_max = streamed ? (R < kChunkTok ? R : kChunkTok)
+                                  : chunk_for(MODE_GATEUP, experts->gate.bits, experts->gate.group_size, H, tokens);
     if (ntok_max < 1) return LMOE_EUNSUPPORTED;
     rc = run_dispatch(L, workspace, reinterpret_cast<const int32_t *>(slots), R, experts->n_slots,
                       nullptr, experts->n_slots, ntok_max, st);
@@ -941,6 +1031,11 @@ int lmoe_gateup_swiglu(const lmoe_experts *experts, const void *x, int32_t token
     gu.out_panel = 0;
     gu.limit = limit;
     gu.swiglu_mode = swiglu_mode;
+    if (streamed)
+        return cuda_rc(launch_stream(SMODE_GATEUP, pa.act_f16, experts->gate.bits, experts->gate.group_size, gu, sc,
+                                     L.max_chunks, st));
+    if (!experts->gate.weight || !experts->up.weight) return LMOE_EINVAL;
+    gu.q0.tiles = gu.q1.tiles = nullptr;
     return cuda_rc(launch_gemv(MODE_GATEUP, pa.act_f16, experts->gate.bits, experts->gate.group_size,
                                gu, L.max_chunks, st));
 }
@@ -970,26 +1065,34 @@ int lmoe_gather_qmm(const lmoe_qproj *proj, int32_t n_slots, int32_t rows, int32
     pa.act_f16 = dtype == LMOE_F16;
     rc = cuda_rc(launch_panel(pa, st));
     if (rc) return rc;
-    const int ntok_max = chunk_for(MODE_QMM, proj->bits, proj->group_size, cols, routes);
+    const QView qv = view(*proj, n_slots, rows, cols);
+    StreamCfg sc;
+    const bool streamed = qv.tiles && stream_config(SMODE_PAIR, rows, cols, proj->bits, proj->group_size, false, &sc);
+    const int ntok_max = streamed ? (routes < kChunkTok ? routes : kChunkTok)
+                                  : chunk_for(MODE_QMM, proj->bits, proj->group_size, cols, routes);
     if (ntok_max < 1) return LMOE_EUNSUPPORTED;
     rc = run_dispatch(L, workspace, reinterpret_cast<const int32_t *>(slots), routes, n_slots, nullptr,
                       n_slots, ntok_max, st);
     if (rc) return rc;
     GemvArgs q = gemv_base(L, workspace, n_slots, ntok_max);
-    q.q0 = view(*proj, n_slots, rows, cols);
+    q.q0 = qv;
     q.panel = pa.panel;
     q.sum16 = pa.sum16;
     q.route_div = 1;
     q.out = static_cast<uint16_t *>(y);
+    if (streamed)  // y per route (no weights: the plain gather_qmm output)
+        return cuda_rc(launch_stream(SMODE_PAIR, pa.act_f16, proj->bits, proj->group_size, q, sc, L.max_chunks, st));
+    if (!proj->weight) return LMOE_EINVAL;
+    q.q0.tiles = nullptr;
     return cuda_rc(launch_gemv(MODE_QMM, pa.act_f16, proj->bits, proj->group_size, q, L.max_chunks, st));
 }
 
 size_t lmoe_tile_bytes(int32_t rows, int32_t cols, int32_t bits, int32_t group_size) {
-    if (rows <= 0 || rows % 16 != 0 || group_size <= 0 || cols <= 0 || cols % group_size != 0) return 0;
+    if (rows <= 0 || group_size <= 0 || cols <= 0 || cols % group_size != 0) return 0;
     if (!gemv_ok(bits, group_size)) return 0;
-    TileGeo tg;
-    if (!tile_geo(cols, bits, group_size, &tg)) return 0;
-    return (size_t)(rows / 16) * (size_t)tg.TB;
+    StreamGeo sg;
+    if (!stream_geo(rows, cols, bits, group_size, &sg) || sg.tg.SB != 16) return 0;
+    return (size_t)sg.slot;
 }
 
 int lmoe_tile_pack(const lmoe_qproj *src, int32_t n_slots, int32_t rows, int32_t cols, int32_t slot_begin,
@@ -1002,8 +1105,8 @@ int lmoe_tile_pack(const lmoe_qproj *src, int32_t n_slots, int32_t rows, int32_t
     lmoe_qproj p = *src;
     p.tiles = tiles;
     const QView q = view(p, n_slots, rows, cols);
-    return cuda_rc(launch_tile_pack(q, src->bits, src->group_size, slot_begin, slot_count,
-                                    static_cast<uint8_t *>(tiles), static_cast<cudaStream_t>(stream)));
+    return cuda_rc(launch_stream_pack(q, src->bits, src->group_size, slot_begin, slot_count,
+                                      static_cast<uint8_t *>(tiles), static_cast<cudaStream_t>(stream)));
 }
 
 // ------------------------------------------------------------ expert parallel

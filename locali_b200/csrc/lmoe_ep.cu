@@ -163,22 +163,25 @@ __global__ void __launch_bounds__(256) ep_partial_kernel(const uint16_t *yw, con
 // One block per token t:
 //   out[t] = T(sum over ranks d, in rank order, of back[d][slot_of[t][d]]);
 //   with a residual, out[t] = T(residual[t] + that);
-//   with normed, normed[t] = T(out[t] * rsqrt(mean(out[t]^2) + eps)), fp32
-//   statistics of the rounded out values (a weightless RMSNorm: the next
-//   layer's MoE input when out is the residual stream).
+//   with normed, normed[t] = T((out[t] - mean) * rsqrt(var + eps)), fp32
+//   statistics of the rounded out values (a weightless LayerNorm: the next
+//   layer's MoE input when out is the residual stream; centring removes
+//   the common-mode component that expert outputs carry when the
+//   dequantised weights are not zero-mean, which would otherwise steer
+//   every token to the same experts).
 template <typename TA>
 __global__ void __launch_bounds__(256) ep_combine_kernel(const float *back, int T, int world, int H,
                                                          const int32_t *slot_of, const uint16_t *residual,
                                                          uint16_t *out, uint16_t *normed, float eps) {
     __shared__ int s_slot[kEpMaxWorld];
-    __shared__ float s_red[8];
+    __shared__ float s_red[2][8];
     pdl_wait();
     pdl_trigger();
     const int t = blockIdx.x, tid = threadIdx.x;
     if (tid < world) s_slot[tid] = slot_of[(size_t)t * world + tid];
     __syncthreads();
     const int per = H >> 3;
-    float ss = 0.0f;
+    float s1 = 0.0f, ss = 0.0f;
     for (int cc = tid; cc < per; cc += blockDim.x) {
         float acc[8];
 #pragma unroll
@@ -210,7 +213,10 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const float *back, int 
             }
         }
 #pragma unroll
-        for (int e = 0; e < 8; ++e) ss = fmaf(o[e], o[e], ss);
+        for (int e = 0; e < 8; ++e) {
+            s1 += o[e];
+            ss = fmaf(o[e], o[e], ss);
+        }
         uint4 r;
         r.x = Act<TA>::pack2(o[0], o[1]);
         r.y = Act<TA>::pack2(o[2], o[3]);
@@ -220,12 +226,23 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const float *back, int 
     }
     if (!normed) return;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if ((tid & 31) == 0) s_red[tid >> 5] = ss;
+    for (int o = 16; o > 0; o >>= 1) {
+        s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+        ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    }
+    if ((tid & 31) == 0) {
+        s_red[0][tid >> 5] = s1;
+        s_red[1][tid >> 5] = ss;
+    }
     __syncthreads();
-    float tot = 0.0f;
-    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) tot += s_red[w];  // fixed order
-    const float inv = rsqrtf(tot / static_cast<float>(H) + eps);
+    float t1 = 0.0f, t2 = 0.0f;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) {  // fixed order
+        t1 += s_red[0][w];
+        t2 += s_red[1][w];
+    }
+    const float mean = t1 / static_cast<float>(H);
+    const float var = fmaxf(t2 / static_cast<float>(H) - mean * mean, 0.0f);
+    const float inv = rsqrtf(var + eps);
     // each thread re-reads only the chunks it wrote above
     for (int cc = tid; cc < per; cc += blockDim.x) {
         const uint4 v = *reinterpret_cast<const uint4 *>(out + (size_t)t * H + (size_t)cc * 8);
@@ -233,10 +250,57 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const float *back, int 
         uint32_t q[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e)
-            q[e] = Act<TA>::pack2(Act<TA>::to_f(static_cast<uint16_t>(u[e] & 0xFFFFu)) * inv,
-                                  Act<TA>::to_f(static_cast<uint16_t>(u[e] >> 16)) * inv);
+            q[e] = Act<TA>::pack2((Act<TA>::to_f(static_cast<uint16_t>(u[e] & 0xFFFFu)) - mean) * inv,
+                                  (Act<TA>::to_f(static_cast<uint16_t>(u[e] >> 16)) - mean) * inv);
         *reinterpret_cast<uint4 *>(normed + (size_t)t * H + (size_t)cc * 8) = make_uint4(q[0], q[1], q[2], q[3]);
     }
+}
+
+// out[t] = T(sum over i < k of y[t*k + o_i] (* w[t*k + o_i]) in fp32), o_i =
+// order[t*k + i] (route order without an order).  Without weights the rows
+// are already the rounded y*w products (the single-tier combine of
+// arena.py:619-624); with fp32 weights the sum is the mixed-tier path's fp32
+// scatter-add of y * g in tier order (arena.py:632-672).
+template <typename TA>
+__global__ void __launch_bounds__(256) combine_routes_kernel(const uint16_t *y, const float *w, const int32_t *order,
+                                                             int T, int k, int H, uint16_t *out) {
+    pdl_wait();
+    pdl_trigger();
+    const int per = H >> 3;
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long)T * per) return;
+    const long t = i / per;
+    const int cc = (int)(i - t * per);
+    float acc[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = 0.0f;
+    for (int j = 0; j < k; ++j) {
+        const int r = (int)(t * k) + (order ? order[t * k + j] : j);
+        const float wr = w ? w[r] : 1.0f;
+        const uint4 v = *reinterpret_cast<const uint4 *>(y + (size_t)r * H + (size_t)cc * 8);
+        const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            acc[2 * e] = fmaf(Act<TA>::to_f(static_cast<uint16_t>(u[e] & 0xFFFFu)), wr, acc[2 * e]);
+            acc[2 * e + 1] = fmaf(Act<TA>::to_f(static_cast<uint16_t>(u[e] >> 16)), wr, acc[2 * e + 1]);
+        }
+    }
+    uint4 o;
+    o.x = Act<TA>::pack2(acc[0], acc[1]);
+    o.y = Act<TA>::pack2(acc[2], acc[3]);
+    o.z = Act<TA>::pack2(acc[4], acc[5]);
+    o.w = Act<TA>::pack2(acc[6], acc[7]);
+    *reinterpret_cast<uint4 *>(out + (size_t)t * H + (size_t)cc * 8) = o;
+}
+
+cudaError_t launch_combine_routes(int act_f16, const uint16_t *y, const float *w, const int32_t *order, int T, int k,
+                                  int H, uint16_t *out, cudaStream_t st) {
+    const long n = (long)T * (H / 8);
+    if (n <= 0) return cudaSuccess;
+    dim3 grid(static_cast<unsigned>((n + 255) / 256));
+    if (act_f16)
+        return launch_pdl(combine_routes_kernel<__half>, grid, dim3(256), 0, st, y, w, order, T, k, H, out);
+    return launch_pdl(combine_routes_kernel<__nv_bfloat16>, grid, dim3(256), 0, st, y, w, order, T, k, H, out);
 }
 
 cudaError_t launch_ep_dispatch(const EpDispatchArgs &a, cudaStream_t st) {

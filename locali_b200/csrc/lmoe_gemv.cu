@@ -534,7 +534,7 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) gemv_kernel(const GemvArgs
                                     wr = rw[q];
                                 }
                             const float y = Act<TA>::round(fin[m][e]);
-                            const float wv = Act<TA>::round(wr);
+                            const float wv = a.route_w ? Act<TA>::round(wr) : 1.0f;  // no weights: y itself
                             a.out[(size_t)route * rows + row] = Act<TA>::from_f(y * wv);
                         }
                     }
@@ -553,7 +553,7 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) gemv_kernel(const GemvArgs
                                 wr = rw[q];
                             }
                         const float y = Act<TA>::round(fin[0][e]);
-                        const float wv = Act<TA>::round(wr);
+                        const float wv = a.route_w ? Act<TA>::round(wr) : 1.0f;  // no weights: y itself
                         a.out[(size_t)route * rows + row] = Act<TA>::from_f(y * wv);
                     }
                 }

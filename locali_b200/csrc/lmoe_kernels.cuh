@@ -68,6 +68,35 @@ __host__ __device__ inline int tile_sb_chunk(const TileGeo &t, int i) {
     return (i << 4) ^ ((((i >> t.sb_l2)) & t.fm_s) << 4);
 }
 
+// ------------------------------------------------------------ stream format
+// The pre-tiled HBM copy the decode GEMVs stream (lmoe_tile_pack).  The K
+// dimension is cut into chunks of 8 quantisation groups (CK = 8 * gs, one
+// round of the GEMV's 8 group columns); 16-row tiles are paired (2p, 2p+1).
+// Block (pair p, chunk c) = two TileGeo(CK) tiles, rows 32p..32p+15 then
+// 32p+16..32p+31, each [codes 16 x RB][scales 16 x SB][biases 16 x SB]
+// swizzled and padded as TileGeo lays them out.  Per slot: pairs x chunks
+// blocks in (pair, chunk) order, so a GEMV unit's rounds are consecutive.
+struct StreamGeo {
+    TileGeo tg;     // one 16-row tile of a CK-column chunk
+    int32_t CK;     // columns per chunk
+    int32_t nck;    // chunks per row
+    int32_t pairs;  // 32-row pairs
+    int64_t block;  // bytes of one (pair, chunk) block = 2 * tg.TB
+    int64_t slot;   // bytes per slot
+};
+__host__ __device__ inline bool stream_geo(int rows, int K, int bits, int gs, StreamGeo *g) {
+    StreamGeo s;
+    s.CK = 8 * gs;
+    if (rows <= 0 || rows % 32 != 0 || K <= 0 || K % s.CK != 0) return false;
+    if (!tile_geo(s.CK, bits, gs, &s.tg)) return false;
+    s.nck = K / s.CK;
+    s.pairs = rows / 32;
+    s.block = 2 * (int64_t)s.tg.TB;
+    s.slot = s.block * s.nck * s.pairs;
+    *g = s;
+    return true;
+}
+
 struct DispatchOut {
     int32_t *sorted_routes;  // [R]
     Chunk *chunks;           // [max_chunks]
@@ -227,6 +256,28 @@ constexpr int kHdrPanel = 20;
 constexpr int kHdrPanelN = 28;
 bool gemv_config(int mode, int bits, int gs, int K, int ntok_max, GemvCfg *out);
 
+// ------------------------------------------------------------ stream GEMV (lmoe_stream.cu)
+// SMODE_GATEUP: units of gate + up tile pairs, clamped SwiGLU into the down
+// panel.  SMODE_PAIR: units of one projection's tile pair, y * w per route,
+// optional block-local combine.
+enum StreamMode { SMODE_GATEUP = 0, SMODE_PAIR = 1 };
+constexpr int kStrMaxWarps = 8;  // consumer warps per block (each feeds itself)
+constexpr int kStrStages = 4;    // ring stages per warp
+struct StreamCfg {
+    int32_t nm, nc, ns, stage_bytes;
+    int32_t TB, RB, SB, sb_l2, fm_c, fm_s;
+    int32_t CK, nck, pairs;
+    int64_t blk;
+    int32_t off_bars, off_ptab, off_stage, smem;
+    int32_t local;  // 1: the block owns pairs blockIdx.x + i * gridDim.x (block-local combine)
+    int32_t grid;   // grid of a local launch
+};
+bool stream_config(int smode, int rows, int K, int bits, int gs, bool local, StreamCfg *out);
+cudaError_t launch_stream(int smode, int act_f16, int bits, int gs, const GemvArgs &a, const StreamCfg &c,
+                          int max_chunks, cudaStream_t st);
+cudaError_t launch_stream_pack(const QView &q, int bits, int gs, int slot_begin, int slot_count, uint8_t *out,
+                               cudaStream_t st);
+
 // Launch with programmatic stream serialisation (see pdl_wait).
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
@@ -382,6 +433,9 @@ struct EpDispatchArgs {
     int32_t *err;
 };
 cudaError_t launch_ep_dispatch(const EpDispatchArgs &a, cudaStream_t st);
+// out[t] = T(sum_i y[t*k + order_i] * w[...]) in fp32 (lmoe_combine_routes)
+cudaError_t launch_combine_routes(int act_f16, const uint16_t *y, const float *w, const int32_t *order, int T, int k,
+                                  int H, uint16_t *out, cudaStream_t st);
 cudaError_t launch_ep_unpack(const uint8_t *recv, int rows, int H, int k, int32_t *idx, float *w, cudaStream_t st);
 cudaError_t launch_ep_partial(int act_f16, const uint16_t *yw, const int32_t *idx, int rows, int H, int k,
                               int n_local, float *partial, cudaStream_t st);

@@ -1,0 +1,609 @@
+// Decode-regime expert GEMVs over the stream format (StreamGeo), sm_100a.
+//
+// Every consumer warp owns whole units and feeds itself: a unit is one chunk
+// (<= 8 routes of one expert) x one pair of 16-row tiles over the full K
+// range -- of gate and up together (GATEUP, four matrices: gate rows
+// 32p..32p+31 and the same up rows) or of one projection (PAIR: down, or a
+// plain gather_qmm).  The warp streams the unit's K chunks (8 quantisation
+// groups each, one bulk copy of 2 tiles per projection) through its own ring
+// of shared-memory stages, issuing the copy of stage i + NS as soon as it has
+// consumed stage i; nothing is shared between warps until the optional
+// block-local combine at the end.  So warps drift freely (no block-wide
+// lockstep on the stages) and there is no cross-warp reduction per unit.
+//
+// Arithmetic per group (dsv4_kernels.py:152-154): acc += scale * sum(x * q)
+// + bias * sum(x), fp32; codes become exact small integers with one LOP3 per
+// pair (lmoe_common.cuh) and the dot products run on mma.sync m16n8k16 with
+// fp32 accumulation.  One token: the MMA's 8 columns are the round's 8
+// groups (each lane's B fragment is the token's activations where its group
+// equals its column).  Several tokens: the columns are the tokens.
+//
+// Epilogues: GATEUP rounds gate and up, clamps and applies SwiGLU
+// (dsv4_arena.py:223-235) and writes h into the down projection's panel with
+// its 16-column sums; PAIR writes T(T(y) * T(w)) per route (w = 1 without
+// weights: the plain gather_qmm output), then, when a combined output is
+// given, the block sums each token's routes in route order in fp32 over the
+// row pairs it owns (its grid divides the pair count), adds the shared
+// expert's row and the residual (combine_finish).
+//
+// All waits are bounded (mbar_wait): a wait that gives up sets LMOE_ECUDA in
+// the status word and the warp drains its copies in flight before leaving.
+#include "lmoe_kernels.cuh"
+
+namespace lmoe {
+
+#define LMOE_FULL 0xffffffffu
+
+namespace {
+
+template <typename T>
+__device__ __forceinline__ T sld(const uint8_t *p) {
+    return *reinterpret_cast<const T *>(p);
+}
+
+// ------------------------------------------------------------ stream packing
+// Row-major slot arrays -> stream blocks: block (tile ti, chunk c) of a slot;
+// 16-byte chunks land at their swizzled places, padding zeroed.
+__global__ void __launch_bounds__(256) stream_pack_kernel(const QView q, const StreamGeo sg, int32_t slot_begin,
+                                                          uint8_t *out) {
+    const int tile = blockIdx.x / sg.nck, c = blockIdx.x - tile * sg.nck;
+    const int slot = slot_begin + static_cast<int>(blockIdx.y);
+    const TileGeo &tg = sg.tg;
+    uint8_t *dst = out + (size_t)slot * sg.slot + ((size_t)(tile >> 1) * sg.nck + c) * sg.block +
+                   (size_t)(tile & 1) * tg.TB;
+    const uint8_t *codes = reinterpret_cast<const uint8_t *>(q.w + (size_t)slot * q.w_slot_stride) +
+                           (size_t)tile * 16 * q.words_per_row * 4 + (size_t)c * tg.RB;
+    const int cpr = tg.RB / 16;  // 16-byte chunks per row
+    for (int i = threadIdx.x; i < 16 * cpr; i += blockDim.x) {
+        const int r = i / cpr, j = i - r * cpr;
+        *reinterpret_cast<uint4 *>(dst + tile_code_chunk(tg, i)) =
+            *reinterpret_cast<const uint4 *>(codes + (size_t)r * q.words_per_row * 4 + j * 16);
+    }
+    // scales / biases: 8 groups x 2 bytes = 16 bytes per row
+    const size_t sb0 = (size_t)slot * q.sb_slot_stride + (size_t)tile * 16 * q.groups_per_row + (size_t)c * 8;
+    for (int r = threadIdx.x; r < 16; r += blockDim.x) {
+        const int o = tile_sb_chunk(tg, r);
+        *reinterpret_cast<uint4 *>(dst + tg.tS + o) =
+            *reinterpret_cast<const uint4 *>(q.s + sb0 + (size_t)r * q.groups_per_row);
+        *reinterpret_cast<uint4 *>(dst + tg.tB + o) =
+            *reinterpret_cast<const uint4 *>(q.b + sb0 + (size_t)r * q.groups_per_row);
+    }
+    for (int o = tg.tB + 16 * tg.SB + 16 * threadIdx.x; o < tg.TB; o += 16 * blockDim.x)
+        *reinterpret_cast<uint4 *>(dst + o) = make_uint4(0u, 0u, 0u, 0u);
+}
+
+}  // namespace
+
+cudaError_t launch_stream_pack(const QView &q, int bits, int gs, int slot_begin, int slot_count, uint8_t *out,
+                               cudaStream_t st) {
+    StreamGeo sg;
+    if (!stream_geo(q.rows, q.cols, bits, gs, &sg)) return cudaErrorInvalidValue;
+    if (sg.tg.SB != 16) return cudaErrorInvalidValue;  // 8 groups of 2-byte scales per row
+    if (slot_count <= 0) return cudaSuccess;
+    dim3 grid(static_cast<unsigned>((q.rows / 16) * sg.nck), static_cast<unsigned>(slot_count), 1);
+    stream_pack_kernel<<<grid, 256, 0, st>>>(q, sg, slot_begin, out);
+    return cudaGetLastError();
+}
+
+namespace {
+
+// ------------------------------------------------------------ the GEMV
+template <typename TA, int BITS, int GS, int SMODE>
+__global__ void __launch_bounds__(kStrMaxWarps * 32, 1) stream_kernel(const GemvArgs a, const StreamCfg c) {
+    using Gm = Geo<BITS, GS>;
+    using PX = PairX<TA, BITS>;
+    constexpr int NM = SMODE == SMODE_GATEUP ? 4 : 2;  // matrices per stage
+    constexpr int NROW = 2 * NM;                      // (matrix, row half) pairs per lane
+    constexpr int WPS = Gm::kWps;                     // words per lane slice of one group
+    constexpr int SPW = Gm::kStepsPerWord;            // k16 steps per code word
+    constexpr int S = Gm::kSteps;                     // k16 steps per group
+    constexpr int WPG = Gm::kWordsPerGroup;
+    constexpr int NW = 2 * WPG;                       // words per lane per row in one round (2 groups)
+    constexpr bool OFFSET = (BITS != 8) && FoldOffset<TA>::value;
+    constexpr float kM = Act<TA>::kMagicVal;
+    static_assert(NW % 4 == 0, "a lane's words per round must be whole 16-byte chunks");
+
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + c.off_bars) + warp * c.ns;
+    uint8_t *ring = smem + c.off_stage + (size_t)warp * c.ns * c.stage_bytes;
+    const int K = a.q0.cols;
+    const int rows = a.q0.rows;
+    const int RT = rows >> 4;
+    const int nck = c.nck;
+
+    if (lane == 0)
+        for (int s = 0; s < c.ns; ++s) mbar_init(&bars[s], 1);
+    uint16_t *ptab = reinterpret_cast<uint16_t *>(smem + c.off_ptab);
+    if (SMODE == SMODE_GATEUP && a.out_panel)
+        for (int i = threadIdx.x; i < a.out_gs; i += blockDim.x) {
+            int p;
+            const int pos = panel_pos(i, a.out_bits, a.out_gs, &p);
+            ptab[i] = static_cast<uint16_t>(pos | (p << 8));
+        }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    __syncthreads();
+
+    pdl_wait();  // chunk table and activation rows come from the preceding kernels
+    pdl_trigger();
+    const int nch = *a.n_chunks;
+    // this warp's units: global (u = gw + j * total warps) or, with the
+    // block-local combine, the block's own pairs (p = blockIdx.x + i * G)
+    const int G = static_cast<int>(gridDim.x);
+    const int own = c.local ? (c.pairs - static_cast<int>(blockIdx.x) + G - 1) / G : c.pairs;
+    const int units = nch * own;
+    const int first = c.local ? warp : static_cast<int>(blockIdx.x) * c.nc + warp;
+    const int step = c.local ? c.nc : G * c.nc;
+    const int my_units = first < units ? (units - first + step - 1) / step : 0;
+    const int stages = my_units * nck;
+    auto unit_of = [&](int j, int &ch, int &p) {
+        const int u = first + j * step;
+        ch = u / own;
+        const int i = u - ch * own;
+        p = c.local ? static_cast<int>(blockIdx.x) + i * G : i;
+    };
+    const uint64_t pol = evict_first_policy();
+    // lane 0 issues stage s (unit s / nck, round s % nck) into slot s % ns
+    auto issue = [&](int s) {
+        int ch, p;
+        unit_of(s / nck, ch, p);
+        const int r = s - (s / nck) * nck;
+        int slot = a.chunks[ch].slot;
+        if (slot < 0 || slot >= a.n_slots) {
+            set_error(a.err, -3);
+            slot = 0;
+        }
+        uint8_t *dst = ring + (size_t)(s % c.ns) * c.stage_bytes;
+        uint64_t *bar = &bars[s % c.ns];
+        const size_t off = (size_t)slot * a.q0.tile_slot_stride + ((size_t)p * nck + r) * c.blk;
+        mbar_expect_tx(bar, static_cast<uint32_t>(NM / 2 * c.blk));
+        bulk_g2s_hint(dst, a.q0.tiles + off, static_cast<uint32_t>(c.blk), bar, pol);
+        if (SMODE == SMODE_GATEUP)
+            bulk_g2s_hint(dst + c.blk, a.q1.tiles + (size_t)slot * a.q1.tile_slot_stride +
+                                           ((size_t)p * nck + r) * c.blk,
+                          static_cast<uint32_t>(c.blk), bar, pol);
+    };
+    if (lane == 0)
+        for (int s = 0; s < c.ns && s < stages; ++s) issue(s);
+
+    // per-lane row bases of the swizzled tiles: matrix m, row half h
+    int crow[NROW], cfx[NROW], srow[NROW], sfx[NROW];
+#pragma unroll
+    for (int r = 0; r < NROW; ++r) {
+        const int rr = g + 8 * (r & 1);
+        crow[r] = (r >> 1) * c.TB + rr * c.RB;
+        cfx[r] = ((rr & 7) & c.fm_c) << 4;
+        srow[r] = (r >> 1) * c.TB + rr * c.SB;
+        sfx[r] = (c.sb_l2 >= 0 ? (rr & c.fm_s) : 0) << 4;
+    }
+    const int tS = 16 * c.RB;  // scale block of a tile (TileGeo)
+    const int tB = tS + 16 * c.SB;
+
+    bool failed = false;
+    int s = 0;  // stage counter of this warp
+    for (int j = 0; j < my_units && !failed; ++j) {
+        int ch, p;
+        unit_of(j, ch, p);
+        const Chunk chk = a.chunks[ch];
+        int ntok = chk.ntok;
+        if (ntok < 0 || ntok > a.ntok_max) {
+            set_error(a.err, -3);
+            ntok = ntok < 0 ? 0 : a.ntok_max;
+        }
+        // lane n < ntok: route n of the chunk, its weight and activation row
+        int my_route = -1, my_row = -1;
+        float my_w = 1.0f;
+        if (lane < ntok) {
+            my_route = a.sorted_routes[chk.route_start + lane];
+            if (a.route_w) my_w = a.route_w[my_route];
+            my_row = SMODE == SMODE_GATEUP ? route_row(my_route, a.route_div, a.shared_base) : my_route;
+        }
+        const bool gpath = ntok == 1;
+        // token column of this lane in the token-column path (n = g)
+        const int col_row = __shfl_sync(LMOE_FULL, my_row, g < ntok ? g : 0);
+        const int row0 = __shfl_sync(LMOE_FULL, my_row, 0);
+        float racc[NM][4];
+#pragma unroll
+        for (int m = 0; m < NM; ++m)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) racc[m][e] = 0.0f;
+
+        for (int r = 0; r < nck; ++r, ++s) {
+            const int slot_i = s % c.ns;
+            if (!mbar_wait(&bars[slot_i], (s / c.ns) & 1)) {
+                if (lane == 0) set_error(a.err, -4);
+                failed = true;
+                break;
+            }
+            const uint8_t *sb = ring + (size_t)slot_i * c.stage_bytes;
+            const int kbase = r * c.CK;  // first column of this round
+            if (gpath) {
+                // ---- one token: columns = the round's 8 groups; lane t
+                // covers words [t * NW, (t + 1) * NW) = groups 2t, 2t + 1
+                const uint16_t *xp = a.panel + (size_t)row0 * K + kbase;
+                const float2 *xs = reinterpret_cast<const float2 *>(a.sum16) + (size_t)row0 * (K / 16) + kbase / 16;
+                // group sums of the token (4 lanes per group)
+                float2 gx = make_float2(0.0f, 0.0f);
+                {
+                    const int n = lane >> 2, sub = lane & 3;
+                    for (int q = sub; q < S; q += 4) {
+                        const float2 v = __ldg(xs + n * S + q);
+                        gx.x += v.x;
+                        gx.y += v.y;
+                    }
+                }
+                uint16_t sbr[NM][2][4];
+#pragma unroll
+                for (int m = 0; m < NM; ++m)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int rr = 2 * m + h;
+                        const int os0 = srow[rr] + ((2 * (2 * t)) ^ sfx[rr]);
+                        const int os1 = srow[rr] + ((2 * (2 * t + 1)) ^ sfx[rr]);
+                        sbr[m][h][0] = sld<uint16_t>(sb + tS + os0);
+                        sbr[m][h][1] = sld<uint16_t>(sb + tB + os0);
+                        sbr[m][h][2] = sld<uint16_t>(sb + tS + os1);
+                        sbr[m][h][3] = sld<uint16_t>(sb + tB + os1);
+                    }
+                float d[NM][4];
+#pragma unroll
+                for (int m = 0; m < NM; ++m)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) d[m][e] = 0.0f;
+#pragma unroll
+                for (int qc = 0; qc < NW / 4; ++qc) {
+                    const int w0 = t * NW + 4 * qc;  // first code word of this chunk in the row
+                    const bool act = (g == w0 / WPG);
+                    uint32_t raw[NROW][4];
+#pragma unroll
+                    for (int rr = 0; rr < NROW; ++rr) {
+                        const uint4 v = sld<uint4>(sb + crow[rr] + ((w0 * 4) ^ cfx[rr]));
+                        raw[rr][0] = v.x;
+                        raw[rr][1] = v.y;
+                        raw[rr][2] = v.z;
+                        raw[rr][3] = v.w;
+                    }
+                    const uint16_t *bp = xp + w0 * SPW * 4;
+                    uint4 bq = make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        typename PX::W pw[NROW];
+#pragma unroll
+                        for (int rr = 0; rr < NROW; ++rr) pw[rr] = PX::prep(raw[rr][i]);
+#pragma unroll
+                        for (int s2 = 0; s2 < SPW; ++s2) {
+                            const int js = i * SPW + s2;
+                            if ((js & 1) == 0 && act) bq = __ldg(reinterpret_cast<const uint4 *>(bp + js * 4));
+                            const uint32_t b0 = (js & 1) ? bq.z : bq.x;
+                            const uint32_t b1 = (js & 1) ? bq.w : bq.y;
+#pragma unroll
+                            for (int m = 0; m < NM; ++m)
+                                Act<TA>::mma(d[m], PX::get(pw[2 * m], 2 * s2), PX::get(pw[2 * m + 1], 2 * s2),
+                                             PX::get(pw[2 * m], 2 * s2 + 1), PX::get(pw[2 * m + 1], 2 * s2 + 1), b0,
+                                             b1);
+                        }
+                    }
+                }
+                gx.x += __shfl_xor_sync(LMOE_FULL, gx.x, 1);
+                gx.y += __shfl_xor_sync(LMOE_FULL, gx.y, 1);
+                gx.x += __shfl_xor_sync(LMOE_FULL, gx.x, 2);
+                gx.y += __shfl_xor_sync(LMOE_FULL, gx.y, 2);
+                const float X0 = __shfl_sync(LMOE_FULL, gx.x, 8 * t), P0 = __shfl_sync(LMOE_FULL, gx.y, 8 * t);
+                const float X1 = __shfl_sync(LMOE_FULL, gx.x, 8 * t + 4), P1 = __shfl_sync(LMOE_FULL, gx.y, 8 * t + 4);
+#pragma unroll
+                for (int m = 0; m < NM; ++m)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const float s0 = Act<TA>::to_f(sbr[m][h][0]), b0 = Act<TA>::to_f(sbr[m][h][1]);
+                        const float s1 = Act<TA>::to_f(sbr[m][h][2]), b1 = Act<TA>::to_f(sbr[m][h][3]);
+                        float e0 = d[m][2 * h], e1 = d[m][2 * h + 1];
+                        if constexpr (OFFSET) {
+                            e0 = fmaf(-kM, P0, e0);
+                            e1 = fmaf(-kM, P1, e1);
+                        }
+                        float tot = fmaf(s0, e0, b0 * X0);
+                        tot = fmaf(s1, e1, tot);
+                        tot = fmaf(b1, X1, tot);
+                        tot += __shfl_xor_sync(LMOE_FULL, tot, 1);
+                        tot += __shfl_xor_sync(LMOE_FULL, tot, 2);
+                        racc[m][2 * h] += tot;  // column 0: the unit's single token
+                    }
+            } else {
+                // ---- several tokens: columns = tokens (lane column g);
+                // per group, lane t's slice of WPS words per row
+                const bool has_b = g < ntok;
+                const uint16_t *xp = a.panel + (size_t)col_row * K + kbase;
+                const float2 *xs = reinterpret_cast<const float2 *>(a.sum16) + (size_t)col_row * (K / 16) + kbase / 16;
+#pragma unroll 1
+                for (int G8 = 0; G8 < 8; ++G8) {
+                    typename PX::W pw[NROW][WPS];
+                    uint16_t sv[NROW], bv[NROW];
+                    const int goff = G8 * WPG * 4 + t * WPS * 4;
+#pragma unroll
+                    for (int rr = 0; rr < NROW; ++rr) {
+                        uint32_t wd[WPS];
+                        if constexpr (WPS == 1) {
+                            wd[0] = sld<uint32_t>(sb + crow[rr] + (goff ^ cfx[rr]));
+                        } else if constexpr (WPS == 2) {
+                            const uint2 v = sld<uint2>(sb + crow[rr] + (goff ^ cfx[rr]));
+                            wd[0] = v.x;
+                            wd[1] = v.y;
+                        } else {
+#pragma unroll
+                            for (int q = 0; q < WPS / 4; ++q) {
+                                const uint4 v = sld<uint4>(sb + crow[rr] + ((goff + 16 * q) ^ cfx[rr]));
+                                wd[4 * q] = v.x;
+                                wd[4 * q + 1] = v.y;
+                                wd[4 * q + 2] = v.z;
+                                wd[4 * q + 3] = v.w;
+                            }
+                        }
+#pragma unroll
+                        for (int q = 0; q < WPS; ++q) pw[rr][q] = PX::prep(wd[q]);
+                        const int os = srow[rr] + ((2 * G8) ^ sfx[rr]);
+                        sv[rr] = sld<uint16_t>(sb + tS + os);
+                        bv[rr] = sld<uint16_t>(sb + tB + os);
+                    }
+                    // (sum x, sum of stored panel values) of the lane's two token columns
+                    float2 xt[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int n = 2 * t + h;
+                        const int rn = __shfl_sync(LMOE_FULL, my_row, n < ntok ? n : 0);
+                        if (n < ntok) {
+                            const float2 *p2 =
+                                reinterpret_cast<const float2 *>(a.sum16) + (size_t)rn * (K / 16) + kbase / 16 + G8 * S;
+#pragma unroll
+                            for (int q = 0; q < S; ++q) {
+                                const float2 v = __ldg(p2 + q);
+                                xt[h].x += v.x;
+                                xt[h].y += v.y;
+                            }
+                        }
+                    }
+                    (void)xs;
+                    float d[NM][4];
+#pragma unroll
+                    for (int m = 0; m < NM; ++m)
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) d[m][e] = 0.0f;
+                    uint4 bq = make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+                    for (int k = 0; k < S; ++k) {
+                        const int wi = k / SPW, s2 = k % SPW;
+                        if ((k & 1) == 0 && has_b)
+                            bq = __ldg(reinterpret_cast<const uint4 *>(xp + ((G8 * 4 + t) * S + k) * 4));
+                        const uint32_t b0 = (k & 1) ? bq.z : bq.x;
+                        const uint32_t b1 = (k & 1) ? bq.w : bq.y;
+#pragma unroll
+                        for (int m = 0; m < NM; ++m)
+                            Act<TA>::mma(d[m], PX::get(pw[2 * m][wi], 2 * s2), PX::get(pw[2 * m + 1][wi], 2 * s2),
+                                         PX::get(pw[2 * m][wi], 2 * s2 + 1), PX::get(pw[2 * m + 1][wi], 2 * s2 + 1),
+                                         b0, b1);
+                    }
+#pragma unroll
+                    for (int m = 0; m < NM; ++m) {
+                        float e[4] = {d[m][0], d[m][1], d[m][2], d[m][3]};
+                        if constexpr (OFFSET) {
+                            e[0] = fmaf(-kM, xt[0].y, e[0]);
+                            e[1] = fmaf(-kM, xt[1].y, e[1]);
+                            e[2] = fmaf(-kM, xt[0].y, e[2]);
+                            e[3] = fmaf(-kM, xt[1].y, e[3]);
+                        }
+                        const float s0 = Act<TA>::to_f(sv[2 * m]), s1 = Act<TA>::to_f(sv[2 * m + 1]);
+                        const float b0 = Act<TA>::to_f(bv[2 * m]), b1 = Act<TA>::to_f(bv[2 * m + 1]);
+                        racc[m][0] = fmaf(e[0], s0, fmaf(xt[0].x, b0, racc[m][0]));
+                        racc[m][1] = fmaf(e[1], s0, fmaf(xt[1].x, b0, racc[m][1]));
+                        racc[m][2] = fmaf(e[2], s1, fmaf(xt[0].x, b1, racc[m][2]));
+                        racc[m][3] = fmaf(e[3], s1, fmaf(xt[1].x, b1, racc[m][3]));
+                    }
+                }
+            }
+            // release the slot: order this warp's reads of it before the
+            // asynchronous refill, then queue stage s + ns into it
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0 && s + c.ns < stages) issue(s + c.ns);
+        }
+        if (failed) break;
+
+        // ---- epilogue of the unit (racc: rows g / g + 8 x token columns 2t, 2t + 1)
+        if constexpr (SMODE == SMODE_GATEUP) {
+            // matrices: 0 / 1 = gate tiles 2p / 2p + 1, 2 / 3 = the same up tiles
+#pragma unroll
+            for (int ti = 0; ti < 2; ++ti) {
+                const int rt = 2 * p + ti;
+                float hv[4], hp[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float h = swiglu_h<TA>(racc[ti][e], racc[2 + ti][e], a.limit, a.swiglu_mode);
+                    const int n = 2 * t + (e & 1);
+                    const int row = rt * 16 + g + 8 * (e >> 1);
+                    const int route = __shfl_sync(LMOE_FULL, my_route, n < ntok ? n : 0);
+                    hv[e] = 0.0f;
+                    hp[e] = 0.0f;
+                    if (n < ntok) {
+                        hv[e] = h;
+                        if (a.out_panel) {
+                            const int tv = ptab[row & (a.out_gs - 1)];
+                            const int out_lg = __ffs(a.out_gs) - 1;
+                            const int pos = ((row >> out_lg) << out_lg) + (tv & 0xff);
+                            const int pe = tv >> 8;
+                            const uint16_t pv =
+                                Act<TA>::from_f(h * (pe == 0 ? 1.0f : (pe == 1 ? 0.25f : 0.0625f)));
+                            hp[e] = Act<TA>::to_f(pv);
+                            a.out[(size_t)route * rows + pos] = pv;
+                        } else {
+                            a.out[(size_t)route * rows + row] = Act<TA>::from_f(h);
+                        }
+                    }
+                }
+                if (a.out_sum16) {
+                    float s0 = hv[0] + hv[2], s1 = hv[1] + hv[3];
+                    float p0 = hp[0] + hp[2], p1 = hp[1] + hp[3];
+#pragma unroll
+                    for (int o = 4; o < 32; o <<= 1) {
+                        s0 += __shfl_xor_sync(LMOE_FULL, s0, o);
+                        s1 += __shfl_xor_sync(LMOE_FULL, s1, o);
+                        p0 += __shfl_xor_sync(LMOE_FULL, p0, o);
+                        p1 += __shfl_xor_sync(LMOE_FULL, p1, o);
+                    }
+                    const int r0 = __shfl_sync(LMOE_FULL, my_route, 2 * t < ntok ? 2 * t : 0);
+                    const int r1 = __shfl_sync(LMOE_FULL, my_route, 2 * t + 1 < ntok ? 2 * t + 1 : 0);
+                    if (g == 0) {
+                        if (2 * t < ntok)
+                            *reinterpret_cast<float2 *>(a.out_sum16 + ((size_t)r0 * RT + rt) * 2) = make_float2(s0, p0);
+                        if (2 * t + 1 < ntok)
+                            *reinterpret_cast<float2 *>(a.out_sum16 + ((size_t)r1 * RT + rt) * 2) = make_float2(s1, p1);
+                    }
+                }
+            }
+        } else {
+            // y * w per route row of both tiles (w = 1 without weights)
+#pragma unroll
+            for (int m = 0; m < 2; ++m)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int n = 2 * t + (e & 1);
+                    const int row = (2 * p + m) * 16 + g + 8 * (e >> 1);
+                    const int route = __shfl_sync(LMOE_FULL, my_route, n < ntok ? n : 0);
+                    const float wr = __shfl_sync(LMOE_FULL, my_w, n < ntok ? n : 0);
+                    if (n < ntok) {
+                        const float y = Act<TA>::round(racc[m][e]);
+                        const float wv = a.route_w ? Act<TA>::round(wr) : 1.0f;
+                        a.out[(size_t)route * rows + row] = Act<TA>::from_f(y * wv);
+                    }
+                }
+        }
+    }
+    if (failed) {
+        // drain: let the copies this warp issued land before it leaves
+        for (int q = s; q < stages && q < s + c.ns; ++q) mbar_wait(&bars[q % c.ns], (q / c.ns) & 1);
+    }
+    if constexpr (SMODE == SMODE_PAIR) {
+        if (!c.local || !a.combined) return;
+        // block-local combine over the pairs this block owns: each token's
+        // k route rows summed in route order in fp32 (read back from L2),
+        // then the shared expert's row and the residual (combine_finish)
+        __threadfence_block();
+        __syncthreads();
+        const int items = own * 32 * a.n_tok;
+        for (int i = threadIdx.x; i < items; i += blockDim.x) {
+            const int ri = i & 31, rest = i >> 5;
+            const int tok = rest % a.n_tok, jp = rest / a.n_tok;
+            const int row = (static_cast<int>(blockIdx.x) + jp * G) * 32 + ri;
+            float sacc = 0.0f;
+            for (int r = 0; r < a.top_k; ++r)
+                sacc += Act<TA>::to_f(__ldcg(reinterpret_cast<const unsigned short *>(
+                    a.out + ((size_t)tok * a.top_k + r) * rows + row)));
+            const bool sh = a.shared_base > 0;
+            const uint16_t sv = sh ? __ldcg(reinterpret_cast<const unsigned short *>(
+                                         a.out + ((size_t)a.shared_base + tok) * rows + row))
+                                   : 0;
+            const uint16_t rv = a.residual ? a.residual[(size_t)tok * rows + row] : 0;
+            a.combined[(size_t)tok * rows + row] =
+                Act<TA>::from_f(combine_finish<TA>(sacc, sh, sv, a.residual != nullptr, rv));
+        }
+    }
+}
+
+int g_sms = 0;
+int sm_count() {
+    if (g_sms == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&g_sms, cudaDevAttrMultiProcessorCount, dev);
+        if (g_sms <= 0) g_sms = 148;
+    }
+    return g_sms;
+}
+
+template <typename TA, int BITS, int GS, int SMODE>
+cudaError_t launch_stream_t(const GemvArgs &a, const StreamCfg &c, int max_chunks, cudaStream_t st) {
+    auto kern = stream_kernel<TA, BITS, GS, SMODE>;
+    static int configured = 0;
+    if (c.smem > configured) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, c.smem);
+        if (e != cudaSuccess) return e;
+        configured = c.smem;
+    }
+    long grid;
+    if (c.local) {
+        grid = c.grid;
+    } else {
+        const long units_max = (long)max_chunks * c.pairs;
+        grid = (units_max + c.nc - 1) / c.nc;
+        if (grid > sm_count()) grid = sm_count();
+        if (grid < 1) grid = 1;
+    }
+    return launch_pdl(kern, dim3(static_cast<unsigned>(grid)), dim3(c.nc * 32), c.smem, st, a, c);
+}
+
+template <typename TA, int SMODE>
+cudaError_t launch_stream_bits(int bits, int gs, const GemvArgs &a, const StreamCfg &c, int max_chunks,
+                               cudaStream_t st) {
+#define LMOE_SCASE(B, Gs) \
+    if (bits == B && gs == Gs) return launch_stream_t<TA, B, Gs, SMODE>(a, c, max_chunks, st);
+    LMOE_SCASE(2, 64)
+    LMOE_SCASE(2, 128)
+    LMOE_SCASE(4, 32)
+    LMOE_SCASE(4, 64)
+    LMOE_SCASE(4, 128)
+    LMOE_SCASE(8, 32)
+    LMOE_SCASE(8, 64)
+    LMOE_SCASE(8, 128)
+#undef LMOE_SCASE
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace
+
+// Shared-memory plan: ns stages of NM tiles per warp; as many warps (<= 8)
+// as fit next to each other in 227 KB, at least 2 stages each.
+bool stream_config(int smode, int rows, int K, int bits, int gs, bool local, StreamCfg *out) {
+    StreamGeo sg;
+    if (!stream_geo(rows, K, bits, gs, &sg) || sg.tg.SB != 16) return false;
+    StreamCfg c;
+    c.nm = smode == SMODE_GATEUP ? 4 : 2;
+    c.TB = sg.tg.TB;
+    c.RB = sg.tg.RB;
+    c.SB = sg.tg.SB;
+    c.sb_l2 = sg.tg.sb_l2;
+    c.fm_c = sg.tg.fm_c;
+    c.fm_s = sg.tg.fm_s;
+    c.CK = sg.CK;
+    c.nck = sg.nck;
+    c.pairs = sg.pairs;
+    c.blk = sg.block;
+    c.stage_bytes = c.nm * c.TB;
+    c.off_bars = 0;
+    c.off_ptab = 1024;
+    c.off_stage = 2048;
+    const int budget = 227 * 1024 - c.off_stage;
+    c.ns = kStrStages;
+    c.nc = budget / (c.ns * c.stage_bytes);
+    if (c.nc < 4) {
+        c.ns = 3;
+        c.nc = budget / (c.ns * c.stage_bytes);
+    }
+    if (c.nc > kStrMaxWarps) c.nc = kStrMaxWarps;
+    if (c.nc < 1 || c.nc * c.ns * 8 > c.off_ptab) return false;  // mbarriers below the panel table
+    c.smem = c.off_stage + c.nc * c.ns * c.stage_bytes;
+    c.local = local ? 1 : 0;
+    c.grid = 0;
+    *out = c;
+    return true;
+}
+
+cudaError_t launch_stream(int smode, int act_f16, int bits, int gs, const GemvArgs &a, const StreamCfg &c,
+                          int max_chunks, cudaStream_t st) {
+    if (act_f16) {
+        if (smode == SMODE_GATEUP) return launch_stream_bits<__half, SMODE_GATEUP>(bits, gs, a, c, max_chunks, st);
+        return launch_stream_bits<__half, SMODE_PAIR>(bits, gs, a, c, max_chunks, st);
+    }
+    if (smode == SMODE_GATEUP) return launch_stream_bits<__nv_bfloat16, SMODE_GATEUP>(bits, gs, a, c, max_chunks, st);
+    return launch_stream_bits<__nv_bfloat16, SMODE_PAIR>(bits, gs, a, c, max_chunks, st);
+}
+
+}  // namespace lmoe

@@ -196,6 +196,35 @@ class V4ArenaMoE(ArenaMoE):
             self._kernels[tier] = k
         return k
 
+    def _prefetch_routes(self, x, input_ids, blocks):
+        """The next layers' routing for their cross-layer prefetch
+        (arena.py:520-541), launched on the device; each result is copied to
+        pinned host memory behind an event, so only that small copy is ever
+        waited on.  Candidates are cut to the ``k`` highest gates."""
+        pend = []
+        for blk, k in blocks:
+            pi, pg = blk.route(x, input_ids)
+            pi = pi.reshape(-1, self.top_k)
+            if k and k < self.top_k:
+                order = torch.argsort(-pg.reshape(-1, self.top_k).float(), dim=-1)
+                pi = torch.gather(pi, -1, order[:, :k])
+            if pi.is_cuda:
+                host = torch.empty(pi.shape, dtype=pi.dtype, pin_memory=True)
+                host.copy_(pi, non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record()
+                pend.append((blk, host, ev))
+            else:
+                pend.append((blk, pi, None))
+        return pend
+
+    def _submit_prefetch(self, pend):
+        for blk, host, ev in pend:
+            if ev is not None:
+                ev.synchronize()
+            self.store.submit(blk.layer, [int(e) for e in host.reshape(-1).tolist()], prefetch=True)
+        self.last_prefetch = [blk.layer for blk, _, _ in pend]
+
     def __call__(self, x, input_ids=None):
         shape = x.shape
         flat = x.reshape(-1, shape[-1])
@@ -206,14 +235,25 @@ class V4ArenaMoE(ArenaMoE):
             self._resident = self.store.layer_resident(self.layer)
             self._ver = ver
         tier = self._tier
-        direct = (self._resident and isinstance(self.gate, V4Gate) and self.nxt is None and self.nxt2 is None)
-        if direct:
+        blocks = [(b, k) for b, k in ((self.nxt, self.prefetch_k), (self.nxt2, self.prefetch_k2)) if b is not None]
+        # a next layer whose experts are all resident needs no prefetch (its
+        # submit would claim nothing)
+        blocks = [(b, k) for b, k in blocks if not self.store.layer_resident(b.layer)]
+        if self._resident and isinstance(self.gate, V4Gate):
+            # device path: router, dispatch and experts in one call with the
+            # slot table on the device, no host synchronisation for this layer
+            pend = self._prefetch_routes(x, input_ids, blocks) if blocks else []
             self.store.sync_table()
             out = self.kernel(tier)(flat, hash_idx=self.gate.hash_idx(input_ids)).reshape(shape)
+            if pend:
+                self._submit_prefetch(pend)
+            self.last_path = "device"
             return out if out.dtype == x.dtype else out.to(x.dtype)
+        self.last_path = "host"
         inds, gates = self.route(x, input_ids)
         ii = inds.reshape(-1, self.top_k)
-        experts = [e for row in ii.tolist() for e in row]  # host sync, as arena.py:513
+        ii_host = ii.tolist()  # host sync, as arena.py:513
+        experts = [e for row in ii_host for e in row]
         if self.store.tier_overlap:
             placed, reads = self.store.submit(self.layer, experts)
         else:
@@ -222,21 +262,52 @@ class V4ArenaMoE(ArenaMoE):
         if missing:
             raise RuntimeError(f"arena could not place demanded experts {missing} of layer {self.layer}: every "
                                "usable slot is pinned; raise the ceiling")
-        for blk, k in ((self.nxt, self.prefetch_k), (self.nxt2, self.prefetch_k2)):
-            if blk is None:
-                continue
-            pi, pg = blk.route(x, input_ids)
-            pi = pi.reshape(-1, self.top_k)
-            if k and k < self.top_k:
-                order = torch.argsort(-pg.reshape(-1, self.top_k), dim=-1)
-                pi = torch.gather(pi, -1, order[:, :k])
-            self.store.submit(blk.layer, [e for row in pi.tolist() for e in row], prefetch=True)
-        if reads is not None:
-            for t in self.store.tiers:
-                self.store.wait(reads[t])
+        if blocks:
+            self._submit_prefetch(self._prefetch_routes(x, input_ids, blocks))
         self.store.sync_table()
-        out = self.kernel(tier).routed(flat, ii, gates.reshape(-1, self.top_k))
+        w = gates.reshape(-1, self.top_k)
+        out = self._apply(flat, ii, ii_host, placed, w, reads)
         return out.reshape(shape).to(x.dtype)
+
+    def _apply(self, flat, ii, ii_host, placed, w, reads):
+        """``ArenaMoE._apply`` (arena.py:549-672) on the device kernels."""
+        T, k = len(ii_host), self.top_k
+        present = [t for t in self.store.tiers if any(placed[e][0] == t for row in ii_host for e in row)]
+        ii = ii.to(torch.int32)
+        if len(present) == 1:
+            t = present[0]
+            pending = getattr(reads, "pending_experts", ()) if reads else ()
+            if self.overlap_hits and T == 1 and pending and len(pending) < k:
+                # resident experts first, then the ones still being filled
+                # (arena.py:575-618); the per-route products are combined
+                # once in route order, so the result equals the fused path
+                ready = torch.tensor([[e not in pending for e in ii_host[0]]], device=ii.device)
+                prod = torch.empty((k, flat.shape[1]), dtype=flat.dtype, device=flat.device)
+                kern = self.kernel(t)
+                kern.products(flat, torch.where(ready, ii, -1), w, prod)
+                self.store.wait(reads[t])
+                kern.products(flat, torch.where(ready, -1, ii), w, prod)
+                self.last_apply = "overlap"
+                return ops.combine_routes(prod, k)
+            if reads is not None:
+                self.store.wait(reads[t])
+            self.last_apply = "single"
+            return self.kernel(t).routed(flat, ii, w)
+        # Several tiers (arena.py:625-672): each tier's own routes, unweighted
+        # rows, then the fp32 sum of y * g in tier order and route order,
+        # with g the weights rounded to the activation dtype; one rounding.
+        tier_pos = {t: i for i, t in enumerate(present)}
+        tier_of = torch.tensor([[tier_pos[placed[e][0]] for e in row] for row in ii_host], device=ii.device)
+        order = torch.tensor([sorted(range(k), key=lambda j, row=row: (tier_pos[placed[row[j]][0]], j))
+                              for row in ii_host], dtype=torch.int32, device=ii.device)
+        prod = torch.empty((T * k, flat.shape[1]), dtype=flat.dtype, device=flat.device)
+        for i, t in enumerate(present):
+            if reads is not None:
+                self.store.wait(reads[t])
+            self.kernel(t).products(flat, torch.where(tier_of == i, ii, -1), None, prod)
+        g = w.to(flat.dtype).float()
+        self.last_apply = "tiers"
+        return ops.combine_routes(prod, k, w=g, order=order)
 
     def _gather(self, tier, inputs, indices):
         """Expert products for [T, k] slot indices (dsv4_arena.py:168-235):

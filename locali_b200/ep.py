@@ -167,7 +167,7 @@ class ExpertParallelMoE:
     def __call__(self, x: torch.Tensor, residual: torch.Tensor | None = None,
                  out: torch.Tensor | None = None, normed: torch.Tensor | None = None) -> torch.Tensor:
         """``out = residual + moe(x)`` (without residual: ``moe(x)``); with
-        ``normed``, also its weightless RMSNorm (the next layer's input)."""
+        ``normed``, also its weightless LayerNorm (the next layer's input)."""
         flat = x.reshape(-1, x.shape[-1])
         if flat.dtype != self.r.act_dtype:
             flat = flat.to(self.r.act_dtype)

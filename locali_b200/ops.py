@@ -372,6 +372,22 @@ class MoEKernel:
     def route(self, x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
         return route(self._x(x), self.router, self.ws)
 
+    def products(self, x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor | None,
+                 out: torch.Tensor) -> torch.Tensor:
+        """``lmoe_moe_products``: into ``out`` [T*top_k, hidden], the rounded
+        ``y * w`` row (``y`` when ``w`` is None) of every route whose expert
+        id is >= 0; rows of the routes marked -1 are left untouched."""
+        flat = self._x(x)
+        T = flat.shape[0]
+        idx = idx.reshape(T, -1).to(torch.int32).contiguous()
+        if idx.shape[1] != self.router.top_k:
+            raise ValueError("routing width must equal top_k")
+        wf = None if w is None else w.reshape(T, -1).to(torch.float32).contiguous()
+        self.ws.ensure(self.workspace_bytes(T))
+        check(lmoe().lmoe_moe_products(ctypes.byref(self.desc), flat.data_ptr(), T, idx.data_ptr(), _ptr(wf),
+                                       out.data_ptr(), self.ws.ptr(), self.ws.nbytes, _stream()), "lmoe_moe_products")
+        return out
+
     def routed(self, x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor,
                out: torch.Tensor | None = None) -> torch.Tensor:
         flat = self._x(x)
@@ -386,6 +402,23 @@ class MoEKernel:
         check(lmoe().lmoe_moe_routed(ctypes.byref(self.desc), flat.data_ptr(), T, idx.data_ptr(), w.data_ptr(),
                                      out.data_ptr(), self.ws.ptr(), self.ws.nbytes, _stream()), "lmoe_moe_routed")
         return out.reshape(x.shape)
+
+
+def combine_routes(products: torch.Tensor, top_k: int, w: torch.Tensor | None = None,
+                   order: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``lmoe_combine_routes``: per token, the fp32 sum of its ``top_k`` route
+    rows (times ``w`` when given), in ``order`` ([T, top_k] route positions;
+    route order by default), rounded once."""
+    _need_cuda(products)
+    R, H = products.shape
+    T = R // top_k
+    if out is None:
+        out = torch.empty((T, H), dtype=products.dtype, device=products.device)
+    wf = None if w is None else w.reshape(-1).to(torch.float32).contiguous()
+    of = None if order is None else order.reshape(-1).to(torch.int32).contiguous()
+    check(lmoe().lmoe_combine_routes(products.data_ptr(), _ptr(wf), _ptr(of), T, int(top_k), H,
+                                     _ACT[products.dtype], out.data_ptr(), _stream()), "lmoe_combine_routes")
+    return out
 
 
 def static_status() -> None:

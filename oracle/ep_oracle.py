@@ -130,8 +130,11 @@ def combine(back: np.ndarray, slot_of: np.ndarray, dtype: str = "bf16", residual
     return out
 
 
-def rms_normed(out: np.ndarray, dtype: str = "bf16", eps: float = 1e-6) -> np.ndarray:
-    """Weightless RMSNorm of the combined rows (fp32 statistics), rounded."""
+def normed(out: np.ndarray, dtype: str = "bf16", eps: float = 1e-6) -> np.ndarray:
+    """Weightless LayerNorm of the combined rows (mean and variance over the
+    row), rounded: the next layer's MoE input the expert-parallel combine
+    writes."""
     o = np.asarray(out, np.float64)
-    inv = 1.0 / np.sqrt(np.mean(o * o, axis=-1, keepdims=True) + eps)
-    return O.round_act((o * inv).astype(np.float32), dtype)
+    mean = np.mean(o, axis=-1, keepdims=True)
+    var = np.mean((o - mean) ** 2, axis=-1, keepdims=True)
+    return O.round_act(((o - mean) / np.sqrt(var + eps)).astype(np.float32), dtype)

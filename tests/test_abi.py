@@ -78,17 +78,21 @@ def test_strerror_and_version(built):
 
 
 def test_tile_geometry(built):
-    """Pre-tiled format: 16-row tiles of codes + scales + biases, 128-byte padded."""
+    """Pre-tiled stream format: 16-row tiles of 8-group K chunks (codes +
+    scales + biases, 128-byte padded), tiles paired, per slot in (pair, chunk)
+    order."""
     lib = _lib.lmoe()
-    # 2-bit g64, K=4096: codes 16*1024, scales and biases 16*128 each
-    assert lib.lmoe_tile_bytes(2048, 4096, 2, 64) == 128 * (16 * 1024 + 2 * 16 * 128)
-    # 4-bit g32, K=2048: codes 16*1024, scale rows of 128 bytes
-    assert lib.lmoe_tile_bytes(4096, 2048, 4, 32) == 256 * (16 * 1024 + 2 * 16 * 128)
-    # small K: 16*32 codes + 2*16*2 scale bytes -> padded to 640
-    assert lib.lmoe_tile_bytes(16, 128, 2, 128) == 640
+    # 2-bit g64, K=4096: chunks of 512 columns; a chunk tile holds codes
+    # 16*128, scales and biases 16*16 each (2560 B), 8 chunks x 128 tiles
+    assert lib.lmoe_tile_bytes(2048, 4096, 2, 64) == 128 * 8 * (16 * 128 + 2 * 16 * 16)
+    # 4-bit g32, K=2048: chunks of 256 columns, same tile bytes
+    assert lib.lmoe_tile_bytes(4096, 2048, 4, 32) == 256 * 8 * (16 * 128 + 2 * 16 * 16)
+    # hidden 7168 at 2 bits: 14 chunks
+    assert lib.lmoe_tile_bytes(2048, 7168, 2, 64) == 128 * 14 * (16 * 128 + 2 * 16 * 16)
+    assert lib.lmoe_tile_bytes(16, 128, 2, 128) == 0       # K below one 8-group chunk; 16 rows are not a pair
     assert lib.lmoe_tile_bytes(2048, 4096, 3, 64) == 0     # bits not compiled
-    assert lib.lmoe_tile_bytes(2040, 4096, 2, 64) == 0     # rows not a multiple of 16
-    assert lib.lmoe_tile_bytes(2048, 3072, 2, 64) == 0     # rows of 768 B: not a power-of-two chunk count
+    assert lib.lmoe_tile_bytes(2040, 4096, 2, 64) == 0     # rows not a multiple of 32 (tile pairs)
+    assert lib.lmoe_tile_bytes(2048, 3520, 2, 64) == 0     # K not a multiple of the 512-column chunk
     q = _lib.QProj(None, None, None, 2, 64, None)
     assert lib.lmoe_tile_pack(ctypes.byref(q), 1, 16, 256, 0, 1, None, None) == _lib.LMOE_EINVAL
 

@@ -65,7 +65,7 @@ class OracleRank:
         o = EO.combine(back.numpy(), slot_of.numpy(), "bf16", None if residual is None else t2np(residual))
         out.copy_(torch.from_numpy(o).to(out.dtype))
         if normed is not None:
-            normed.copy_(torch.from_numpy(EO.rms_normed(o)).to(normed.dtype))
+            normed.copy_(torch.from_numpy(EO.normed(o)).to(normed.dtype))
 
 
 def _layer():

@@ -139,7 +139,7 @@ def test_ep_loopback_prefill_path_and_residual(built):
 def test_ep_one_rank_residual_and_norm(built, path, T):
     """At one rank the expert-parallel step sums each token's routes in the
     single-GPU combine's order, so with the residual it equals the fused
-    block entry bit for bit; the normed output is the weightless RMSNorm of
+    block entry bit for bit; the normed output is the weightless LayerNorm of
     that result (the next layer's input)."""
     cfg = synth.config("c2", n_experts=32)
     layer = synth.make_layer(cfg, seed=17, device="cuda")
@@ -154,7 +154,7 @@ def test_ep_one_rank_residual_and_norm(built, path, T):
     torch.cuda.synchronize()
     r.check()
     assert torch.equal(out, want)
-    ref = EO.rms_normed(t2np(out))
+    ref = EO.normed(t2np(out))
     assert O.rel_l2(t2np(xn), ref) < 2e-3
     assert float(np.mean(t2np(xn) != ref)) < 0.02
 

@@ -75,6 +75,8 @@ def test_kernel_matches_reference_kernel(built, case, tiled):
     up = ops.QProjArrays(words(inp["wu"]), act(inp["su"]), act(inp["bu"]), 2, GS)
     gate = ops.QProjArrays(words(inp["wg"]), act(inp["sg"]), act(inp["bg"]), 2, GS)
     if tiled:
+        if up.tile_bytes() == 0:
+            pytest.skip(f"K={K} is below one 8-group chunk of g{GS}: no stream tile layout")
         up.pack_tiles()
         gate.pack_tiles()
     ex = ops.ExpertArrays(gate, up, gate)  # down is not read by this call
