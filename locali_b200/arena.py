@@ -352,6 +352,17 @@ class ArenaStore:
             by_tier[t].append(fill)
             self.bytes_read += self.item[t]
             self._set_table((layer, e), s)
+        if not prefetch:
+            # The placement follows the reference policy (arena.py:305-354),
+            # which pins the previous demand's slots but not this call's hits:
+            # in an arena too small for both, a miss can evict a hit of the
+            # same call and take its slot.  The reference would then compute
+            # with the refilled slot; refuse instead of computing garbage.
+            lost = [e for e, (t, s) in out.items() if self._table_host[layer, e] != s]
+            if lost:
+                raise RuntimeError(f"layer {layer}: demanded experts {sorted(lost)} were evicted by other experts of "
+                                   "the same layer (the arena is too small beside the pinned slots); raise the "
+                                   "ceiling")
         for t in self.tiers:
             by_tier[t] = by_tier[t] + waits[t]
         by_tier.pending_experts = frozenset(

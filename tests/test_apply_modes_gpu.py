@@ -121,7 +121,8 @@ def test_overlap_hits_equals_one_call_path(built, tmp_path):
 def test_device_path_prefetches_next_layer(built, tmp_path):
     cfg, layers, idx_path = _pack(tmp_path, n_layers=2, E=8, k=2)
     per = cfg.expert_bytes() / 1e9
-    store = V4ArenaStore(idx_path, native_scheduler=False, ceiling_gb=per * 12.5, threads=2, device="cuda")
+    # room for layer 0 (8 experts, pinned) and all of layer 1's demand
+    store = V4ArenaStore(idx_path, native_scheduler=False, ceiling_gb=per * 16.5, threads=2, device="cuda")
     try:
         store.make_resident([0])
         assert store.layer_resident(0) and not store.layer_resident(1)

@@ -126,3 +126,23 @@ def test_bad_policy_rejected(pack):
     _, _, idx = pack
     with pytest.raises(ValueError):
         ArenaStore(idx, cache_policy="fifo", device="cpu")
+
+
+def test_demand_that_evicts_its_own_hit_is_refused(pack):
+    """The reference policy pins the previous demand's slots, not this call's
+    hits; when this call's misses can only take a hit's slot, the store
+    refuses instead of handing out a slot that another expert refills."""
+    cfg, layers, idx = pack
+    probe = ArenaStore(idx, ceiling_gb=1.0, threads=1, device="cpu")
+    per = _item_gb(probe)
+    probe.close()
+    store = ArenaStore(idx, ceiling_gb=per * 5.5, threads=1, device="cpu")  # 4 usable slots
+    try:
+        assert store.slots["cold"] == 5
+        store.slots_for(0, [0, 1])          # pinned: layer 0's two slots
+        store.slots_for(1, [4, 5])          # fills the two free slots; pins them
+        store.slots_for(0, [0, 1])          # hits; pins layer 0 again
+        with pytest.raises(RuntimeError, match="evicted by other experts of the same layer"):
+            store.slots_for(1, [4, 5, 2])   # 4, 5 hit; 2 can only evict 4 or 5
+    finally:
+        store.close()
