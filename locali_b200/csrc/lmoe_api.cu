@@ -233,14 +233,15 @@ int chunk_for(int mode, int bits, int gs, int K, int cap) {
 // The stream GEMVs run a projection when its pre-tiled copy is present (in
 // the stream format; view() keeps the pointer only for that geometry); the
 // row-major bulk-copy GEMV runs it otherwise.
-bool gateup_streamed(const lmoe_experts &ex, StreamCfg *c) {
+// ntok: routes per chunk the launch serves (the stages hold their rows).
+bool gateup_streamed(const lmoe_experts &ex, int ntok, StreamCfg *c) {
     const QView g = view(ex.gate, ex.n_slots, ex.inter, ex.hidden), u = view(ex.up, ex.n_slots, ex.inter, ex.hidden);
     return g.tiles && u.tiles && ex.gate.bits == ex.up.bits && ex.gate.group_size == ex.up.group_size &&
-           stream_config(SMODE_GATEUP, ex.inter, ex.hidden, ex.gate.bits, ex.gate.group_size, false, c);
+           stream_config(SMODE_GATEUP, ex.inter, ex.hidden, ex.gate.bits, ex.gate.group_size, false, ntok, c);
 }
-bool down_streamed(const lmoe_experts &ex, bool local, StreamCfg *c) {
+bool down_streamed(const lmoe_experts &ex, bool local, int ntok, StreamCfg *c) {
     return view(ex.down, ex.n_slots, ex.hidden, ex.inter).tiles &&
-           stream_config(SMODE_PAIR, ex.hidden, ex.inter, ex.down.bits, ex.down.group_size, local, c);
+           stream_config(SMODE_PAIR, ex.hidden, ex.inter, ex.down.bits, ex.down.group_size, local, ntok, c);
 }
 
 // Routes per chunk: up to 8 (one MMA n-tile), also bounded by the stage plan
@@ -249,11 +250,11 @@ int layer_chunk(const lmoe_layer *l, int T) {
     const lmoe_experts &ex = l->experts;
     StreamCfg sc;
     int c = T < kChunkTok ? T : kChunkTok;
-    if (!gateup_streamed(ex, &sc)) {
+    if (!gateup_streamed(ex, c, &sc)) {
         const int a = chunk_for(MODE_GATEUP, ex.gate.bits, ex.gate.group_size, ex.hidden, T);
         if (a < c) c = a;
     }
-    if (!down_streamed(ex, false, &sc)) {
+    if (c >= 1 && !down_streamed(ex, false, c, &sc)) {
         const int b = chunk_for(MODE_DOWN, ex.down.bits, ex.down.group_size, ex.inter, T);
         if (b < c) c = b;
     }
@@ -298,7 +299,7 @@ int run_experts(const lmoe_layer *l, const Layout &L, void *ws, int T, const flo
     const int f16 = ex.dtype == LMOE_F16;
     int rc;
     StreamCfg sc;
-    if (gateup_streamed(ex, &sc)) {
+    if (gateup_streamed(ex, ntok_max, &sc)) {
         rc = cuda_rc(launch_stream(SMODE_GATEUP, f16, ex.gate.bits, ex.gate.group_size, gu, sc, L.max_chunks, st));
     } else {
         // row-major arrays through the bulk-copy GEMV
@@ -321,13 +322,13 @@ int run_experts(const lmoe_layer *l, const Layout &L, void *ws, int T, const flo
     dn.n_tok = T;
     dn.shared_base = extra.shared_base;
     dn.residual = extra.residual;
-    if (down_streamed(ex, false, &sc)) {
+    if (down_streamed(ex, false, ntok_max, &sc)) {
         // Few tokens: blocks own row pairs and combine locally.  More
         // tokens (or no combine): units spread over every SM, then the
         // route-order combine kernel (the same arithmetic).
         StreamCfg lc;
         const int grid = down2_grid(sc.pairs);
-        if (out && T <= kDown2MaxTokens && grid > 0 && down_streamed(ex, true, &lc)) {
+        if (out && T <= kDown2MaxTokens && grid > 0 && down_streamed(ex, true, ntok_max, &lc)) {
             lc.grid = grid;
             dn.counters = nullptr;
             return cuda_rc(launch_stream(SMODE_PAIR, f16, ex.down.bits, ex.down.group_size, dn, lc, L.max_chunks, st));
@@ -1014,7 +1015,7 @@ int lmoe_gateup_swiglu(const lmoe_experts *experts, const void *x, int32_t token
     rc = cuda_rc(launch_panel(pa, st));
     if (rc) return rc;
     StreamCfg sc;
-    const bool streamed = gateup_streamed(*experts, &sc);
+    const bool streamed = gateup_streamed(*experts, R < kChunkTok ? R : kChunkTok, &sc);
     const int ntok_max = streamed ? (R < kChunkTok ? R : kChunkTok)
                                   : chunk_for(MODE_GATEUP, experts->gate.bits, experts->gate.group_size, H, tokens);
     if (ntok_max < 1) return LMOE_EUNSUPPORTED;
@@ -1067,7 +1068,8 @@ int lmoe_gather_qmm(const lmoe_qproj *proj, int32_t n_slots, int32_t rows, int32
     if (rc) return rc;
     const QView qv = view(*proj, n_slots, rows, cols);
     StreamCfg sc;
-    const bool streamed = qv.tiles && stream_config(SMODE_PAIR, rows, cols, proj->bits, proj->group_size, false, &sc);
+    const bool streamed = qv.tiles && stream_config(SMODE_PAIR, rows, cols, proj->bits, proj->group_size, false,
+                                                    routes < kChunkTok ? routes : kChunkTok, &sc);
     const int ntok_max = streamed ? (routes < kChunkTok ? routes : kChunkTok)
                                   : chunk_for(MODE_QMM, proj->bits, proj->group_size, cols, routes);
     if (ntok_max < 1) return LMOE_EUNSUPPORTED;

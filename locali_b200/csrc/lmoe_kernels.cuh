@@ -268,11 +268,15 @@ struct StreamCfg {
     int32_t TB, RB, SB, sb_l2, fm_c, fm_s;
     int32_t CK, nck, pairs;
     int64_t blk;
+    // activation rows staged with the weights: per token, the round's panel
+    // chunk (xbytes) at off_x + n * xbytes and its 16-column sums (sbytes)
+    // at off_s + n * sbytes, for up to ntok_cap tokens
+    int32_t xbytes, sbytes, off_x, off_s, ntok_cap;
     int32_t off_bars, off_ptab, off_stage, smem;
     int32_t local;  // 1: the block owns pairs blockIdx.x + i * gridDim.x (block-local combine)
     int32_t grid;   // grid of a local launch
 };
-bool stream_config(int smode, int rows, int K, int bits, int gs, bool local, StreamCfg *out);
+bool stream_config(int smode, int rows, int K, int bits, int gs, bool local, int ntok_cap, StreamCfg *out);
 cudaError_t launch_stream(int smode, int act_f16, int bits, int gs, const GemvArgs &a, const StreamCfg &c,
                           int max_chunks, cudaStream_t st);
 cudaError_t launch_stream_pack(const QView &q, int bits, int gs, int slot_begin, int slot_count, uint8_t *out,

@@ -5,11 +5,13 @@
 // range -- of gate and up together (GATEUP, four matrices: gate rows
 // 32p..32p+31 and the same up rows) or of one projection (PAIR: down, or a
 // plain gather_qmm).  The warp streams the unit's K chunks (8 quantisation
-// groups each, one bulk copy of 2 tiles per projection) through its own ring
-// of shared-memory stages, issuing the copy of stage i + NS as soon as it has
-// consumed stage i; nothing is shared between warps until the optional
-// block-local combine at the end.  So warps drift freely (no block-wide
-// lockstep on the stages) and there is no cross-warp reduction per unit.
+// groups each: one bulk copy of 2 tiles per projection, plus the chunk of
+// each routed token's activation panel row and its 16-column sums) through
+// its own ring of shared-memory stages, issuing stage i + NS as soon as it
+// has consumed stage i.  The next unit's chunk metadata is loaded into
+// registers one unit ahead, so issuing never waits on global memory.  No
+// stage, barrier or reduction is shared between warps, so warps drift
+// freely; the only block-wide step is the optional combine at the end.
 //
 // Arithmetic per group (dsv4_kernels.py:152-154): acc += scale * sum(x * q)
 // + bias * sum(x), fp32; codes become exact small integers with one LOP3 per
@@ -71,6 +73,13 @@ __global__ void __launch_bounds__(256) stream_pack_kernel(const QView q, const S
     for (int o = tg.tB + 16 * tg.SB + 16 * threadIdx.x; o < tg.TB; o += 16 * blockDim.x)
         *reinterpret_cast<uint4 *>(dst + o) = make_uint4(0u, 0u, 0u, 0u);
 }
+
+// Chunk metadata of one unit, held in registers (lane n < ntok: route n)
+struct UnitMeta {
+    int slot, ntok, p;
+    int route, row;
+    float w;
+};
 
 }  // namespace
 
@@ -137,35 +146,65 @@ __global__ void __launch_bounds__(kStrMaxWarps * 32, 1) stream_kernel(const Gemv
     const int step = c.local ? c.nc : G * c.nc;
     const int my_units = first < units ? (units - first + step - 1) / step : 0;
     const int stages = my_units * nck;
-    auto unit_of = [&](int j, int &ch, int &p) {
+
+    // metadata of unit j (all lanes; lane n < ntok holds route n)
+    auto load_meta = [&](int j, UnitMeta &m) {
+        m.ntok = 0;
+        m.route = -1;
+        m.row = 0;
+        m.w = 1.0f;
+        if (j >= my_units) return;
         const int u = first + j * step;
-        ch = u / own;
+        const int ch = u / own;
         const int i = u - ch * own;
-        p = c.local ? static_cast<int>(blockIdx.x) + i * G : i;
+        m.p = c.local ? static_cast<int>(blockIdx.x) + i * G : i;
+        const Chunk chk = a.chunks[ch];
+        m.slot = chk.slot;
+        if (m.slot < 0 || m.slot >= a.n_slots) {
+            set_error(a.err, -3);
+            m.slot = 0;
+        }
+        m.ntok = chk.ntok;
+        if (m.ntok < 0 || m.ntok > c.ntok_cap) {
+            set_error(a.err, -3);
+            m.ntok = m.ntok < 0 ? 0 : c.ntok_cap;
+        }
+        if (lane < m.ntok) {
+            m.route = a.sorted_routes[chk.route_start + lane];
+            if (a.route_w) m.w = a.route_w[m.route];
+            m.row = SMODE == SMODE_GATEUP ? route_row(m.route, a.route_div, a.shared_base) : m.route;
+        }
     };
     const uint64_t pol = evict_first_policy();
-    // lane 0 issues stage s (unit s / nck, round s % nck) into slot s % ns
-    auto issue = [&](int s) {
-        int ch, p;
-        unit_of(s / nck, ch, p);
-        const int r = s - (s / nck) * nck;
-        int slot = a.chunks[ch].slot;
-        if (slot < 0 || slot >= a.n_slots) {
-            set_error(a.err, -3);
-            slot = 0;
-        }
+    // stage s (round r of a unit with metadata m) into slot s % ns: lane 0
+    // arms the barrier with the stage's bytes and copies the weight tiles;
+    // lane n < ntok copies token n's panel chunk and sums
+    auto issue = [&](int s, int r, const UnitMeta &m) {
         uint8_t *dst = ring + (size_t)(s % c.ns) * c.stage_bytes;
         uint64_t *bar = &bars[s % c.ns];
-        const size_t off = (size_t)slot * a.q0.tile_slot_stride + ((size_t)p * nck + r) * c.blk;
-        mbar_expect_tx(bar, static_cast<uint32_t>(NM / 2 * c.blk));
-        bulk_g2s_hint(dst, a.q0.tiles + off, static_cast<uint32_t>(c.blk), bar, pol);
-        if (SMODE == SMODE_GATEUP)
-            bulk_g2s_hint(dst + c.blk, a.q1.tiles + (size_t)slot * a.q1.tile_slot_stride +
-                                           ((size_t)p * nck + r) * c.blk,
+        if (lane == 0) {
+            const uint32_t bytes = static_cast<uint32_t>(NM / 2 * c.blk + (int64_t)m.ntok * (c.xbytes + c.sbytes));
+            mbar_expect_tx(bar, bytes);
+            const size_t off = ((size_t)m.p * nck + r) * c.blk;
+            bulk_g2s_hint(dst, a.q0.tiles + (size_t)m.slot * a.q0.tile_slot_stride + off,
                           static_cast<uint32_t>(c.blk), bar, pol);
+            if (SMODE == SMODE_GATEUP)
+                bulk_g2s_hint(dst + c.blk, a.q1.tiles + (size_t)m.slot * a.q1.tile_slot_stride + off,
+                              static_cast<uint32_t>(c.blk), bar, pol);
+        }
+        __syncwarp();
+        if (lane < m.ntok) {
+            bulk_g2s(dst + c.off_x + lane * c.xbytes, a.panel + (size_t)m.row * K + (size_t)r * c.CK,
+                     static_cast<uint32_t>(c.xbytes), bar);
+            bulk_g2s(dst + c.off_s + lane * c.sbytes, a.sum16 + ((size_t)m.row * (K / 16) + (size_t)r * (c.CK / 16)) * 2,
+                     static_cast<uint32_t>(c.sbytes), bar);
+        }
     };
-    if (lane == 0)
-        for (int s = 0; s < c.ns && s < stages; ++s) issue(s);
+
+    UnitMeta cur, nxt;
+    load_meta(0, cur);
+    load_meta(1, nxt);
+    for (int s = 0; s < c.ns && s < stages; ++s) issue(s, s % nck, s < nck ? cur : nxt);
 
     // per-lane row bases of the swizzled tiles: matrix m, row half h
     int crow[NROW], cfx[NROW], srow[NROW], sfx[NROW];
@@ -183,26 +222,12 @@ __global__ void __launch_bounds__(kStrMaxWarps * 32, 1) stream_kernel(const Gemv
     bool failed = false;
     int s = 0;  // stage counter of this warp
     for (int j = 0; j < my_units && !failed; ++j) {
-        int ch, p;
-        unit_of(j, ch, p);
-        const Chunk chk = a.chunks[ch];
-        int ntok = chk.ntok;
-        if (ntok < 0 || ntok > a.ntok_max) {
-            set_error(a.err, -3);
-            ntok = ntok < 0 ? 0 : a.ntok_max;
+        if (j > 0) {
+            cur = nxt;
+            load_meta(j + 1, nxt);  // needed ns stages before its first round
         }
-        // lane n < ntok: route n of the chunk, its weight and activation row
-        int my_route = -1, my_row = -1;
-        float my_w = 1.0f;
-        if (lane < ntok) {
-            my_route = a.sorted_routes[chk.route_start + lane];
-            if (a.route_w) my_w = a.route_w[my_route];
-            my_row = SMODE == SMODE_GATEUP ? route_row(my_route, a.route_div, a.shared_base) : my_route;
-        }
+        const int ntok = cur.ntok, p = cur.p;
         const bool gpath = ntok == 1;
-        // token column of this lane in the token-column path (n = g)
-        const int col_row = __shfl_sync(LMOE_FULL, my_row, g < ntok ? g : 0);
-        const int row0 = __shfl_sync(LMOE_FULL, my_row, 0);
         float racc[NM][4];
 #pragma unroll
         for (int m = 0; m < NM; ++m)
@@ -217,18 +242,16 @@ __global__ void __launch_bounds__(kStrMaxWarps * 32, 1) stream_kernel(const Gemv
                 break;
             }
             const uint8_t *sb = ring + (size_t)slot_i * c.stage_bytes;
-            const int kbase = r * c.CK;  // first column of this round
+            const uint8_t *xs8 = sb + c.off_x;  // token n's panel chunk at n * xbytes
+            const float2 *xsum = reinterpret_cast<const float2 *>(sb + c.off_s);
             if (gpath) {
                 // ---- one token: columns = the round's 8 groups; lane t
                 // covers words [t * NW, (t + 1) * NW) = groups 2t, 2t + 1
-                const uint16_t *xp = a.panel + (size_t)row0 * K + kbase;
-                const float2 *xs = reinterpret_cast<const float2 *>(a.sum16) + (size_t)row0 * (K / 16) + kbase / 16;
-                // group sums of the token (4 lanes per group)
                 float2 gx = make_float2(0.0f, 0.0f);
                 {
-                    const int n = lane >> 2, sub = lane & 3;
+                    const int n = lane >> 2, sub = lane & 3;  // 4 lanes per group
                     for (int q = sub; q < S; q += 4) {
-                        const float2 v = __ldg(xs + n * S + q);
+                        const float2 v = xsum[n * S + q];
                         gx.x += v.x;
                         gx.y += v.y;
                     }
@@ -264,7 +287,7 @@ __global__ void __launch_bounds__(kStrMaxWarps * 32, 1) stream_kernel(const Gemv
                         raw[rr][2] = v.z;
                         raw[rr][3] = v.w;
                     }
-                    const uint16_t *bp = xp + w0 * SPW * 4;
+                    const uint8_t *bp = xs8 + w0 * SPW * 8;
                     uint4 bq = make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
@@ -274,7 +297,7 @@ __global__ void __launch_bounds__(kStrMaxWarps * 32, 1) stream_kernel(const Gemv
 #pragma unroll
                         for (int s2 = 0; s2 < SPW; ++s2) {
                             const int js = i * SPW + s2;
-                            if ((js & 1) == 0 && act) bq = __ldg(reinterpret_cast<const uint4 *>(bp + js * 4));
+                            if ((js & 1) == 0 && act) bq = sld<uint4>(bp + js * 8);
                             const uint32_t b0 = (js & 1) ? bq.z : bq.x;
                             const uint32_t b1 = (js & 1) ? bq.w : bq.y;
 #pragma unroll
@@ -313,8 +336,7 @@ __global__ void __launch_bounds__(kStrMaxWarps * 32, 1) stream_kernel(const Gemv
                 // ---- several tokens: columns = tokens (lane column g);
                 // per group, lane t's slice of WPS words per row
                 const bool has_b = g < ntok;
-                const uint16_t *xp = a.panel + (size_t)col_row * K + kbase;
-                const float2 *xs = reinterpret_cast<const float2 *>(a.sum16) + (size_t)col_row * (K / 16) + kbase / 16;
+                const uint8_t *xrow = xs8 + (has_b ? g : 0) * c.xbytes;
 #pragma unroll 1
                 for (int G8 = 0; G8 < 8; ++G8) {
                     typename PX::W pw[NROW][WPS];
@@ -350,19 +372,16 @@ __global__ void __launch_bounds__(kStrMaxWarps * 32, 1) stream_kernel(const Gemv
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
                         const int n = 2 * t + h;
-                        const int rn = __shfl_sync(LMOE_FULL, my_row, n < ntok ? n : 0);
                         if (n < ntok) {
-                            const float2 *p2 =
-                                reinterpret_cast<const float2 *>(a.sum16) + (size_t)rn * (K / 16) + kbase / 16 + G8 * S;
+                            const float2 *p2 = reinterpret_cast<const float2 *>(sb + c.off_s + n * c.sbytes) + G8 * S;
 #pragma unroll
                             for (int q = 0; q < S; ++q) {
-                                const float2 v = __ldg(p2 + q);
+                                const float2 v = p2[q];
                                 xt[h].x += v.x;
                                 xt[h].y += v.y;
                             }
                         }
                     }
-                    (void)xs;
                     float d[NM][4];
 #pragma unroll
                     for (int m = 0; m < NM; ++m)
@@ -372,8 +391,7 @@ __global__ void __launch_bounds__(kStrMaxWarps * 32, 1) stream_kernel(const Gemv
 #pragma unroll
                     for (int k = 0; k < S; ++k) {
                         const int wi = k / SPW, s2 = k % SPW;
-                        if ((k & 1) == 0 && has_b)
-                            bq = __ldg(reinterpret_cast<const uint4 *>(xp + ((G8 * 4 + t) * S + k) * 4));
+                        if ((k & 1) == 0 && has_b) bq = sld<uint4>(xrow + ((G8 * 4 + t) * S + k) * 8);
                         const uint32_t b0 = (k & 1) ? bq.z : bq.x;
                         const uint32_t b1 = (k & 1) ? bq.w : bq.y;
 #pragma unroll
@@ -404,7 +422,11 @@ __global__ void __launch_bounds__(kStrMaxWarps * 32, 1) stream_kernel(const Gemv
             // asynchronous refill, then queue stage s + ns into it
             fence_proxy_async();
             __syncwarp();
-            if (lane == 0 && s + c.ns < stages) issue(s + c.ns);
+            const int sn = s + c.ns;
+            if (sn < stages) {
+                const int jn = sn / nck;  // j or j + 1 (ns <= nck)
+                issue(sn, sn - jn * nck, jn == j ? cur : nxt);
+            }
         }
         if (failed) break;
 
@@ -420,7 +442,7 @@ __global__ void __launch_bounds__(kStrMaxWarps * 32, 1) stream_kernel(const Gemv
                     const float h = swiglu_h<TA>(racc[ti][e], racc[2 + ti][e], a.limit, a.swiglu_mode);
                     const int n = 2 * t + (e & 1);
                     const int row = rt * 16 + g + 8 * (e >> 1);
-                    const int route = __shfl_sync(LMOE_FULL, my_route, n < ntok ? n : 0);
+                    const int route = __shfl_sync(LMOE_FULL, cur.route, n < ntok ? n : 0);
                     hv[e] = 0.0f;
                     hp[e] = 0.0f;
                     if (n < ntok) {
@@ -449,8 +471,8 @@ __global__ void __launch_bounds__(kStrMaxWarps * 32, 1) stream_kernel(const Gemv
                         p0 += __shfl_xor_sync(LMOE_FULL, p0, o);
                         p1 += __shfl_xor_sync(LMOE_FULL, p1, o);
                     }
-                    const int r0 = __shfl_sync(LMOE_FULL, my_route, 2 * t < ntok ? 2 * t : 0);
-                    const int r1 = __shfl_sync(LMOE_FULL, my_route, 2 * t + 1 < ntok ? 2 * t + 1 : 0);
+                    const int r0 = __shfl_sync(LMOE_FULL, cur.route, 2 * t < ntok ? 2 * t : 0);
+                    const int r1 = __shfl_sync(LMOE_FULL, cur.route, 2 * t + 1 < ntok ? 2 * t + 1 : 0);
                     if (g == 0) {
                         if (2 * t < ntok)
                             *reinterpret_cast<float2 *>(a.out_sum16 + ((size_t)r0 * RT + rt) * 2) = make_float2(s0, p0);
@@ -467,8 +489,8 @@ __global__ void __launch_bounds__(kStrMaxWarps * 32, 1) stream_kernel(const Gemv
                 for (int e = 0; e < 4; ++e) {
                     const int n = 2 * t + (e & 1);
                     const int row = (2 * p + m) * 16 + g + 8 * (e >> 1);
-                    const int route = __shfl_sync(LMOE_FULL, my_route, n < ntok ? n : 0);
-                    const float wr = __shfl_sync(LMOE_FULL, my_w, n < ntok ? n : 0);
+                    const int route = __shfl_sync(LMOE_FULL, cur.route, n < ntok ? n : 0);
+                    const float wr = __shfl_sync(LMOE_FULL, cur.w, n < ntok ? n : 0);
                     if (n < ntok) {
                         const float y = Act<TA>::round(racc[m][e]);
                         const float wv = a.route_w ? Act<TA>::round(wr) : 1.0f;
@@ -528,6 +550,7 @@ cudaError_t launch_stream_t(const GemvArgs &a, const StreamCfg &c, int max_chunk
         if (e != cudaSuccess) return e;
         configured = c.smem;
     }
+    if (a.ntok_max > c.ntok_cap) return cudaErrorInvalidValue;
     long grid;
     if (c.local) {
         grid = c.grid;
@@ -537,6 +560,7 @@ cudaError_t launch_stream_t(const GemvArgs &a, const StreamCfg &c, int max_chunk
         if (grid > sm_count()) grid = sm_count();
         if (grid < 1) grid = 1;
     }
+    if (grid < 1) return cudaErrorInvalidValue;
     return launch_pdl(kern, dim3(static_cast<unsigned>(grid)), dim3(c.nc * 32), c.smem, st, a, c);
 }
 
@@ -559,11 +583,14 @@ cudaError_t launch_stream_bits(int bits, int gs, const GemvArgs &a, const Stream
 
 }  // namespace
 
-// Shared-memory plan: ns stages of NM tiles per warp; as many warps (<= 8)
-// as fit next to each other in 227 KB, at least 2 stages each.
-bool stream_config(int smode, int rows, int K, int bits, int gs, bool local, StreamCfg *out) {
+// Shared-memory plan: ns stages per warp, each NM weight tiles plus the
+// round's activation chunk and sums of up to ntok_cap tokens; as many warps
+// (<= 8) as fit in 227 KB.  ns <= chunks per row, so the stage a warp issues
+// after consuming one belongs to its current unit or the next.
+bool stream_config(int smode, int rows, int K, int bits, int gs, bool local, int ntok_cap, StreamCfg *out) {
     StreamGeo sg;
     if (!stream_geo(rows, K, bits, gs, &sg) || sg.tg.SB != 16) return false;
+    if (ntok_cap < 1 || ntok_cap > kChunkTok) return false;
     StreamCfg c;
     c.nm = smode == SMODE_GATEUP ? 4 : 2;
     c.TB = sg.tg.TB;
@@ -576,15 +603,24 @@ bool stream_config(int smode, int rows, int K, int bits, int gs, bool local, Str
     c.nck = sg.nck;
     c.pairs = sg.pairs;
     c.blk = sg.block;
-    c.stage_bytes = c.nm * c.TB;
+    c.ntok_cap = ntok_cap;
+    c.xbytes = c.CK * 2;       // activation chunk of one token
+    c.sbytes = (c.CK / 16) * 8;  // its 16-column (sum x, sum panel) pairs
+    c.off_x = c.nm * c.TB;
+    c.off_s = c.off_x + ntok_cap * c.xbytes;
+    c.stage_bytes = (c.off_s + ntok_cap * c.sbytes + 127) / 128 * 128;
     c.off_bars = 0;
     c.off_ptab = 1024;
     c.off_stage = 2048;
     const int budget = 227 * 1024 - c.off_stage;
-    c.ns = kStrStages;
+    c.ns = kStrStages < c.nck ? kStrStages : c.nck;
     c.nc = budget / (c.ns * c.stage_bytes);
-    if (c.nc < 4) {
+    if (c.nc < 4 && c.ns > 3) {
         c.ns = 3;
+        c.nc = budget / (c.ns * c.stage_bytes);
+    }
+    if (c.nc < 2 && c.ns > 2) {
+        c.ns = 2;
         c.nc = budget / (c.ns * c.stage_bytes);
     }
     if (c.nc > kStrMaxWarps) c.nc = kStrMaxWarps;
