@@ -267,6 +267,11 @@ struct Extra {
     int shared_base = 0;
     const uint16_t *residual = nullptr;
     uint16_t *yw = nullptr;  // caller buffer for the per-route rows (default: the workspace's)
+    // single token: the gate/up kernel selects the routing from the
+    // router's scores (route_impl ran without its finisher)
+    const float2 *tk_scores = nullptr;
+    int32_t *idx_user = nullptr;
+    float *w_user = nullptr;
 };
 
 // gate/up + SwiGLU then down + combine over an already dispatched layer.
@@ -300,8 +305,25 @@ int run_experts(const lmoe_layer *l, const Layout &L, void *ws, int T, const flo
     int rc;
     StreamCfg sc;
     if (gateup_streamed(ex, ntok_max, &sc)) {
+        if (extra.tk_scores) {
+            const lmoe_router &r = l->router;
+            gu.tk_scores = extra.tk_scores;
+            gu.tk_E = r.n_experts;
+            gu.tk_k = k;
+            gu.tk_norm = r.norm_topk;
+            gu.tk_scaling = r.routed_scaling;
+            gu.tk_expert_slot = l->expert_slot;
+            gu.tk_idx = at<int32_t>(ws, L.idx);
+            gu.tk_w = at<float>(ws, L.w);
+            gu.tk_idx_user = extra.idx_user;
+            gu.tk_w_user = extra.w_user;
+            gu.tk_sorted = at<int32_t>(ws, L.sorted);
+            gu.tk_chunks = at<Chunk>(ws, L.chunks);
+            gu.tk_nchunks = at<int32_t>(ws, L.nchunks);
+        }
         rc = cuda_rc(launch_stream(SMODE_GATEUP, f16, ex.gate.bits, ex.gate.group_size, gu, sc, L.max_chunks, st));
     } else {
+        if (extra.tk_scores) return LMOE_EINVAL;  // fusion is only planned for the stream kernel
         // row-major arrays through the bulk-copy GEMV
         if (!ex.gate.weight || !ex.up.weight) return LMOE_EINVAL;
         gu.q0.tiles = gu.q1.tiles = nullptr;
@@ -568,9 +590,28 @@ int lmoe_workspace_status(void *workspace, void *stream) {
 
 // Router (+ top-k, + dispatch when `l` is given).  In the decode regime the
 // router kernel's last block runs top-k (and dispatch) itself: one launch.
+// Element-wise scores (score, score + bias) follow the logit partials.
+static float2 *router_scores(const Layout &L, void *ws, int ksplit, int T, int E) {
+    return reinterpret_cast<float2 *>(at<float>(ws, L.partial) + (((size_t)ksplit * T * E + 1) & ~size_t(1)));
+}
+
+// Single-token decode whose top-k runs inside the stream gate/up kernel:
+// element-wise scoring (no softmax over the experts, no hash routing), one
+// logit split, no shared-expert routes, and the streamed gate/up kernel.
+static bool topk_fusable(const lmoe_layer *l, int T, const int32_t *hash_idx, bool shared, int pf) {
+    if (T != 1 || hash_idx || shared || pf) return false;
+    const lmoe_router &r = l->router;
+    if (r.scoring == LMOE_SCORE_SOFTMAX || r.n_experts > 32 * kRouterMaxEPL || r.top_k > 16) return false;
+    if (router_ksplit(1, r.n_experts, l->experts.hidden, l->experts.dtype == LMOE_F16) != 1) return false;
+    StreamCfg sc;
+    return gateup_streamed(l->experts, layer_chunk(l, 1), &sc);
+}
+
+// fused: the top-k and dispatch are left to the stream gate/up kernel
+// (topk_fusable holds); only the logit blocks run here.
 static int route_impl(const lmoe_router &r, int H, int dtype, const lmoe_layer *l, const Layout &L, const void *x,
                       int T, int32_t *idx_user, float *w_user, void *ws, cudaStream_t st,
-                      const int32_t *hash_idx = nullptr) {
+                      const int32_t *hash_idx = nullptr, bool fused = false) {
     const int k = r.top_k;
     const int R = T * k;
     const int ksplit = router_ksplit(T, r.n_experts, H, dtype == LMOE_F16);
@@ -593,9 +634,8 @@ static int route_impl(const lmoe_router &r, int H, int dtype, const lmoe_layer *
     // element-wise scorings are finished by the logit blocks themselves,
     // unless the logits are split over the hidden dimension (then the top-k
     // sums the splits and scores)
-    a.scores = (r.scoring == LMOE_SCORE_SOFTMAX || ksplit > 1)
-                   ? nullptr
-                   : reinterpret_cast<float2 *>(a.partial + (((size_t)ksplit * T * r.n_experts + 1) & ~size_t(1)));
+    a.scores = (r.scoring == LMOE_SCORE_SOFTMAX || ksplit > 1) ? nullptr
+                                                                 : router_scores(L, ws, ksplit, T, r.n_experts);
     if (l) {
         // this call's combine counters start at zero whatever the workspace
         // held before (another token count or entry point)
@@ -632,6 +672,12 @@ static int route_impl(const lmoe_router &r, int H, int dtype, const lmoe_layer *
     const bool small_disp = l && R <= kDispatchSmallMaxRoutes && a.E + 1 <= kDispatchSmallMaxBuckets;
     a.finish = small_topk ? 1 : 0;
     a.do_dispatch = (small_topk && small_disp) ? 1 : 0;
+    if (fused) {
+        if (!l || !a.scores || T != 1) return LMOE_EINVAL;
+        a.finish = 0;
+        a.do_dispatch = 0;
+        return cuda_rc(launch_router(a, ksplit, st));
+    }
     int rc;
     if (!small_topk && !a.act_f16) {
         // many tokens: logits on the tensor cores; the decode GEMVs' panel
@@ -743,11 +789,19 @@ static int layer_entry(const lmoe_layer *layer, const void *x, int32_t tokens, c
     if (ws_bytes < L.total) return LMOE_EWORKSPACE;
     if (residual && !aligned16(residual)) return LMOE_EINVAL;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // the routing is only complete after gate/up when the top-k is fused:
+    // a caller that waits on ev_routed gets the separate finisher
+    const bool fused = !ev_routed && topk_fusable(layer, tokens, hash_idx, shared_slot >= 0, pf);
     rc = route_impl(layer->router, layer->experts.hidden, layer->experts.dtype, layer, L, x, tokens, idx, w,
-                    workspace, st, hash_idx);
+                    workspace, st, hash_idx, fused);
     if (rc) return rc;
     Extra ex;
     ex.residual = static_cast<const uint16_t *>(residual);
+    if (fused) {
+        ex.tk_scores = router_scores(L, workspace, 1, tokens, layer->router.n_experts);
+        ex.idx_user = idx;
+        ex.w_user = w;
+    }
     if (shared) {
         ex.shared_base = tokens * layer->router.top_k;
         const int ct = pf ? kPfNmax : layer_chunk(layer, tokens);

@@ -220,6 +220,17 @@ struct GemvArgs {
     // the combine adds its row after rounding the routed sum, then residual
     int32_t shared_base;
     const uint16_t *residual;  // [tokens, rows] or nullptr
+    // single-token layers (stream gate/up): every block selects the top-k
+    // from the router's (score, biased score) itself instead of the router's
+    // last block; block 0 writes the routing and the dispatch for the down
+    // kernel and the caller.  tk_scores == nullptr: chunks come from memory.
+    const float2 *tk_scores;
+    int32_t tk_E, tk_k, tk_norm;
+    float tk_scaling;
+    const int32_t *tk_expert_slot;
+    int32_t *tk_idx, *tk_idx_user, *tk_sorted, *tk_nchunks;
+    float *tk_w, *tk_w_user;
+    Chunk *tk_chunks;
 #ifdef LMOE_PROFILE_TRACE
     // per-unit timeline (nanoseconds, %globaltimer) of a profiling build:
     // [block][unit slot][8]

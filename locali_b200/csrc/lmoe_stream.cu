@@ -81,6 +81,111 @@ struct UnitMeta {
     float w;
 };
 
+// Top-k of a single token by one warp from the router's (score, biased
+// score) (arena.py:501-506): selection on the biased score, ties to the
+// lower id; each lane keeps its best candidate and only the winner of a round
+// rescans.  Weights: raw scores normalised by their fp32 sum in selection
+// order + 1e-20, times the routed scaling.  The dispatch of the k distinct
+// experts: chunk i = the route of the i-th smallest expert id.  The same
+// winners, order and weights as the router's own finisher.  Every block
+// computes it (into shared memory); block 0 also writes the routing and the
+// dispatch to memory for the down kernel and the caller.
+__device__ void fused_topk(const GemvArgs &a, Chunk *s_ch, int32_t *s_rt) {
+    const int lane = threadIdx.x & 31;
+    const int E = a.tk_E, k = a.tk_k;
+    float bs[16], sc[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        const int e = lane + 32 * i;
+        bs[i] = -INFINITY;
+        sc[i] = 0.0f;
+        if (e < E) {
+            const float2 v = __ldcg(a.tk_scores + e);
+            sc[i] = v.x;
+            bs[i] = v.y;
+        }
+    }
+    float lbv = -INFINITY, lbs = 0.0f;
+    int lbe = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+        if (bs[i] > lbv) {
+            lbv = bs[i];
+            lbe = lane + 32 * i;
+            lbs = sc[i];
+        }
+    int my_e = -1;
+    float my_s = 0.0f;
+#pragma unroll 1
+    for (int j = 0; j < k; ++j) {
+        float bv = lbv;
+        int be = lbe;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(LMOE_FULL, bv, o);
+            const int oe = __shfl_xor_sync(LMOE_FULL, be, o);
+            if (ov > bv || (ov == bv && oe < be)) {
+                bv = ov;
+                be = oe;
+            }
+        }
+        const float ws = __shfl_sync(LMOE_FULL, lbs, be & 31);
+        if (lane == j) {
+            my_e = be;
+            my_s = ws;
+        }
+        if (lbe == be) {  // the winner drops it and rescans
+            lbv = -INFINITY;
+            lbe = 0x7fffffff;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                if (lane + 32 * i == be) bs[i] = -INFINITY;
+                if (bs[i] > lbv) {
+                    lbv = bs[i];
+                    lbe = lane + 32 * i;
+                    lbs = sc[i];
+                }
+            }
+        }
+    }
+    float ssum = 0.0f;  // fp32, in selection order
+    int pos = 0;        // rank of this lane's expert id among the winners
+#pragma unroll 1
+    for (int j = 0; j < k; ++j) {
+        ssum += __shfl_sync(LMOE_FULL, my_s, j);
+        pos += __shfl_sync(LMOE_FULL, my_e, j) < my_e;
+    }
+    if (lane >= k) return;
+    float wv = a.tk_norm ? my_s / (ssum + 1e-20f) : my_s;
+    wv *= a.tk_scaling;
+    int slot = 0;
+    if (my_e < 0 || my_e >= E) {
+        set_error(a.err, -3);
+    } else {
+        slot = a.tk_expert_slot ? a.tk_expert_slot[my_e] : my_e;
+        if (slot < 0 || slot >= a.n_slots) {
+            set_error(a.err, -3);
+            slot = 0;
+        }
+    }
+    Chunk ch;
+    ch.slot = slot;
+    ch.route_start = pos;
+    ch.ntok = 1;
+    ch.expert = my_e;
+    s_ch[pos] = ch;
+    s_rt[pos] = lane;
+    if (blockIdx.x == 0) {
+        a.tk_idx[lane] = my_e;
+        a.tk_w[lane] = wv;
+        if (a.tk_idx_user) a.tk_idx_user[lane] = my_e;
+        if (a.tk_w_user) a.tk_w_user[lane] = wv;
+        a.tk_sorted[pos] = lane;
+        a.tk_chunks[pos] = ch;
+        if (lane == 0) *a.tk_nchunks = k;
+    }
+}
+
 }  // namespace
 
 cudaError_t launch_stream_pack(const QView &q, int bits, int gs, int slot_begin, int slot_count, uint8_t *out,
@@ -136,7 +241,21 @@ __global__ void __launch_bounds__(kStrMaxWarps * 32, 1) stream_kernel(const Gemv
 
     pdl_wait();  // chunk table and activation rows come from the preceding kernels
     pdl_trigger();
-    const int nch = *a.n_chunks;
+    const Chunk *chunk_tab = a.chunks;
+    const int32_t *route_tab = a.sorted_routes;
+    int nch;
+    if (SMODE == SMODE_GATEUP && a.tk_scores) {
+        // single token: the routing is selected here (see fused_topk)
+        Chunk *s_ch = reinterpret_cast<Chunk *>(smem + c.off_ptab + 256);
+        int32_t *s_rt = reinterpret_cast<int32_t *>(smem + c.off_ptab + 512);
+        if (warp == 0) fused_topk(a, s_ch, s_rt);
+        __syncthreads();
+        chunk_tab = s_ch;
+        route_tab = s_rt;
+        nch = a.tk_k;
+    } else {
+        nch = *a.n_chunks;
+    }
     // this warp's units: global (u = gw + j * total warps) or, with the
     // block-local combine, the block's own pairs (p = blockIdx.x + i * G)
     const int G = static_cast<int>(gridDim.x);
@@ -158,7 +277,7 @@ __global__ void __launch_bounds__(kStrMaxWarps * 32, 1) stream_kernel(const Gemv
         const int ch = u / own;
         const int i = u - ch * own;
         m.p = c.local ? static_cast<int>(blockIdx.x) + i * G : i;
-        const Chunk chk = a.chunks[ch];
+        const Chunk chk = chunk_tab[ch];
         m.slot = chk.slot;
         if (m.slot < 0 || m.slot >= a.n_slots) {
             set_error(a.err, -3);
@@ -170,7 +289,7 @@ __global__ void __launch_bounds__(kStrMaxWarps * 32, 1) stream_kernel(const Gemv
             m.ntok = m.ntok < 0 ? 0 : c.ntok_cap;
         }
         if (lane < m.ntok) {
-            m.route = a.sorted_routes[chk.route_start + lane];
+            m.route = route_tab[chk.route_start + lane];
             if (a.route_w) m.w = a.route_w[m.route];
             m.row = SMODE == SMODE_GATEUP ? route_row(m.route, a.route_div, a.shared_base) : m.route;
         }
