@@ -81,7 +81,7 @@ def test_fused_topk_host_and_static_entries(built):
     kern.ws.check()
     assert torch.equal(got_h, want.cpu())
     assert torch.equal(got_s, want)
-    assert ops.static_status() == 0
+    ops.static_status()  # raises on a device error flag
 
 
 def test_fused_topk_unmapped_expert_sets_status(built):
