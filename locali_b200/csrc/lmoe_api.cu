@@ -233,15 +233,16 @@ int chunk_for(int mode, int bits, int gs, int K, int cap) {
 // The stream GEMVs run a projection when its pre-tiled copy is present (in
 // the stream format; view() keeps the pointer only for that geometry); the
 // row-major bulk-copy GEMV runs it otherwise.
-// ntok: routes per chunk the launch serves (the stages hold their rows).
-bool gateup_streamed(const lmoe_experts &ex, int ntok, StreamCfg *c) {
+// ntok: routes per chunk the launch serves; prow: panel rows it may read
+// (tokens for gate/up, routes for down), resident in shared memory.
+bool gateup_streamed(const lmoe_experts &ex, int ntok, int prow, StreamCfg *c) {
     const QView g = view(ex.gate, ex.n_slots, ex.inter, ex.hidden), u = view(ex.up, ex.n_slots, ex.inter, ex.hidden);
     return g.tiles && u.tiles && ex.gate.bits == ex.up.bits && ex.gate.group_size == ex.up.group_size &&
-           stream_config(SMODE_GATEUP, ex.inter, ex.hidden, ex.gate.bits, ex.gate.group_size, false, ntok, c);
+           stream_config(SMODE_GATEUP, ex.inter, ex.hidden, ex.gate.bits, ex.gate.group_size, false, ntok, prow, c);
 }
-bool down_streamed(const lmoe_experts &ex, bool local, int ntok, StreamCfg *c) {
+bool down_streamed(const lmoe_experts &ex, bool local, int ntok, int prow, StreamCfg *c) {
     return view(ex.down, ex.n_slots, ex.hidden, ex.inter).tiles &&
-           stream_config(SMODE_PAIR, ex.hidden, ex.inter, ex.down.bits, ex.down.group_size, local, ntok, c);
+           stream_config(SMODE_PAIR, ex.hidden, ex.inter, ex.down.bits, ex.down.group_size, local, ntok, prow, c);
 }
 
 // Routes per chunk: up to 8 (one MMA n-tile), also bounded by the stage plan
@@ -250,11 +251,11 @@ int layer_chunk(const lmoe_layer *l, int T) {
     const lmoe_experts &ex = l->experts;
     StreamCfg sc;
     int c = T < kChunkTok ? T : kChunkTok;
-    if (!gateup_streamed(ex, c, &sc)) {
+    if (!gateup_streamed(ex, c, T, &sc)) {
         const int a = chunk_for(MODE_GATEUP, ex.gate.bits, ex.gate.group_size, ex.hidden, T);
         if (a < c) c = a;
     }
-    if (c >= 1 && !down_streamed(ex, false, c, &sc)) {
+    if (c >= 1 && !down_streamed(ex, false, c, T * (l->router.top_k + 1), &sc)) {
         const int b = chunk_for(MODE_DOWN, ex.down.bits, ex.down.group_size, ex.inter, T);
         if (b < c) c = b;
     }
@@ -304,7 +305,7 @@ int run_experts(const lmoe_layer *l, const Layout &L, void *ws, int T, const flo
     const int f16 = ex.dtype == LMOE_F16;
     int rc;
     StreamCfg sc;
-    if (gateup_streamed(ex, ntok_max, &sc)) {
+    if (gateup_streamed(ex, ntok_max, T, &sc)) {
         if (extra.tk_scores) {
             const lmoe_router &r = l->router;
             gu.tk_scores = extra.tk_scores;
@@ -344,13 +345,14 @@ int run_experts(const lmoe_layer *l, const Layout &L, void *ws, int T, const flo
     dn.n_tok = T;
     dn.shared_base = extra.shared_base;
     dn.residual = extra.residual;
-    if (down_streamed(ex, false, ntok_max, &sc)) {
+    const int dprow = T * k + (extra.shared_base > 0 ? T : 0);  // h panel rows: routed + shared routes
+    if (down_streamed(ex, false, ntok_max, dprow, &sc)) {
         // Few tokens: blocks own row pairs and combine locally.  More
         // tokens (or no combine): units spread over every SM, then the
         // route-order combine kernel (the same arithmetic).
         StreamCfg lc;
         const int grid = down2_grid(sc.pairs);
-        if (out && T <= kDown2MaxTokens && grid > 0 && down_streamed(ex, true, ntok_max, &lc)) {
+        if (out && T <= kDown2MaxTokens && grid > 0 && down_streamed(ex, true, ntok_max, dprow, &lc)) {
             lc.grid = grid;
             dn.counters = nullptr;
             return cuda_rc(launch_stream(SMODE_PAIR, f16, ex.down.bits, ex.down.group_size, dn, lc, L.max_chunks, st));
@@ -604,7 +606,7 @@ static bool topk_fusable(const lmoe_layer *l, int T, const int32_t *hash_idx, bo
     if (r.scoring == LMOE_SCORE_SOFTMAX || r.n_experts > 32 * kRouterMaxEPL || r.top_k > 16) return false;
     if (router_ksplit(1, r.n_experts, l->experts.hidden, l->experts.dtype == LMOE_F16) != 1) return false;
     StreamCfg sc;
-    return gateup_streamed(l->experts, layer_chunk(l, 1), &sc);
+    return gateup_streamed(l->experts, layer_chunk(l, 1), 1, &sc);
 }
 
 // fused: the top-k and dispatch are left to the stream gate/up kernel
@@ -1069,7 +1071,7 @@ int lmoe_gateup_swiglu(const lmoe_experts *experts, const void *x, int32_t token
     rc = cuda_rc(launch_panel(pa, st));
     if (rc) return rc;
     StreamCfg sc;
-    const bool streamed = gateup_streamed(*experts, R < kChunkTok ? R : kChunkTok, &sc);
+    const bool streamed = gateup_streamed(*experts, R < kChunkTok ? R : kChunkTok, tokens, &sc);
     const int ntok_max = streamed ? (R < kChunkTok ? R : kChunkTok)
                                   : chunk_for(MODE_GATEUP, experts->gate.bits, experts->gate.group_size, H, tokens);
     if (ntok_max < 1) return LMOE_EUNSUPPORTED;
@@ -1123,7 +1125,7 @@ int lmoe_gather_qmm(const lmoe_qproj *proj, int32_t n_slots, int32_t rows, int32
     const QView qv = view(*proj, n_slots, rows, cols);
     StreamCfg sc;
     const bool streamed = qv.tiles && stream_config(SMODE_PAIR, rows, cols, proj->bits, proj->group_size, false,
-                                                    routes < kChunkTok ? routes : kChunkTok, &sc);
+                                                    routes < kChunkTok ? routes : kChunkTok, routes, &sc);
     const int ntok_max = streamed ? (routes < kChunkTok ? routes : kChunkTok)
                                   : chunk_for(MODE_QMM, proj->bits, proj->group_size, cols, routes);
     if (ntok_max < 1) return LMOE_EUNSUPPORTED;

@@ -279,15 +279,22 @@ struct StreamCfg {
     int32_t TB, RB, SB, sb_l2, fm_c, fm_s;
     int32_t CK, nck, pairs;
     int64_t blk;
-    // activation rows staged with the weights: per token, the round's panel
-    // chunk (xbytes) at off_x + n * xbytes and its 16-column sums (sbytes)
-    // at off_s + n * sbytes, for up to ntok_cap tokens
-    int32_t xbytes, sbytes, off_x, off_s, ntok_cap;
-    int32_t off_bars, off_ptab, off_stage, smem;
+    int32_t ntok_cap;
+    // activation rows resident in shared memory for the whole launch: the
+    // first prow panel rows (res_x bytes) and their 16-column sums (res_s)
+    int32_t prow, res_x, res_s;
+    // work split: the kp warps of a group share each unit's K range (spp
+    // rounds each, partial sums reduced through shared memory); ng groups
+    // per block (nc = kp * ng warps)
+    int32_t kp, ng, spp, max_chunks;
+    int32_t off_ptab, off_part, off_res, off_stage, smem;
     int32_t local;  // 1: the block owns pairs blockIdx.x + i * gridDim.x (block-local combine)
     int32_t grid;   // grid of a local launch
 };
-bool stream_config(int smode, int rows, int K, int bits, int gs, bool local, int ntok_cap, StreamCfg *out);
+// prow: panel rows the launch may read (tokens for gate/up, routes for the
+// paired projections); false when the geometry or the resident rows do not fit
+bool stream_config(int smode, int rows, int K, int bits, int gs, bool local, int ntok_cap, int prow,
+                   StreamCfg *out);
 cudaError_t launch_stream(int smode, int act_f16, int bits, int gs, const GemvArgs &a, const StreamCfg &c,
                           int max_chunks, cudaStream_t st);
 cudaError_t launch_stream_pack(const QView &q, int bits, int gs, int slot_begin, int slot_count, uint8_t *out,

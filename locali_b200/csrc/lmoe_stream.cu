@@ -1,17 +1,20 @@
 // Decode-regime expert GEMVs over the stream format (StreamGeo), sm_100a.
 //
-// Every consumer warp owns whole units and feeds itself: a unit is one chunk
-// (<= 8 routes of one expert) x one pair of 16-row tiles over the full K
-// range -- of gate and up together (GATEUP, four matrices: gate rows
-// 32p..32p+31 and the same up rows) or of one projection (PAIR: down, or a
-// plain gather_qmm).  The warp streams the unit's K chunks (8 quantisation
-// groups each: one bulk copy of 2 tiles per projection, plus the chunk of
-// each routed token's activation panel row and its 16-column sums) through
-// its own ring of shared-memory stages, issuing stage i + NS as soon as it
-// has consumed stage i.  The next unit's chunk metadata is loaded into
-// registers one unit ahead, so issuing never waits on global memory.  No
-// stage, barrier or reduction is shared between warps, so warps drift
-// freely; the only block-wide step is the optional combine at the end.
+// A unit is one chunk (<= 8 routes of one expert) x one pair of 16-row tiles
+// over the full K range -- of gate and up together (GATEUP, four matrices:
+// gate rows 32p..32p+31 and the same up rows) or of one projection (PAIR:
+// down, or a plain gather_qmm).  Units go to groups of kp warps; the warps
+// of a group split each unit's K chunks (8 quantisation groups each) into kp
+// contiguous parts, and every warp streams its part through its own ring of
+// shared-memory stages: each lane cp.async-copies its share of the stage's
+// weight blocks and closes them into one cp.async group, so a stage is ready
+// when the lanes' groups have landed (no mbarrier, no elected issuing lane).
+// With kp > 1 the partial sums meet in a double-buffered shared buffer at a
+// named barrier of the group, and one warp of it (rotating) adds them in
+// part order and runs the epilogue.  Units are spread over all blocks
+// (group g of block b takes units b + G*g, b + G*(g + ng), ...).  The
+// activation rows every unit of the launch may read (tokens for gate/up,
+// routes for the paired projections) stay resident in shared memory.
 //
 // Arithmetic per group (dsv4_kernels.py:152-154): acc += scale * sum(x * q)
 // + bias * sum(x), fp32; codes become exact small integers with one LOP3 per
@@ -28,8 +31,11 @@
 // row pairs it owns (its grid divides the pair count), adds the shared
 // expert's row and the residual (combine_finish).
 //
-// All waits are bounded (mbar_wait): a wait that gives up sets LMOE_ECUDA in
-// the status word and the warp drains its copies in flight before leaving.
+// The kernel has no spin waits: cp.async groups complete or fault, and the
+// named barriers join warps that take the same number of units.
+#include <cstdlib>
+#include <cstring>
+
 #include "lmoe_kernels.cuh"
 
 namespace lmoe {
@@ -81,16 +87,24 @@ struct UnitMeta {
     float w;
 };
 
+// Single-token routing held in registers (lane j < k: the j-th winner's
+// expert id, weight, arena slot, and its rank among the winners' ids, which
+// is its chunk in the dispatch; other lanes hold pos = -1).
+struct TopkRegs {
+    int e, pos, slot;
+    float w;
+};
+
 // Top-k of a single token by one warp from the router's (score, biased
 // score) (arena.py:501-506): selection on the biased score, ties to the
 // lower id; each lane keeps its best candidate and only the winner of a round
 // rescans.  Weights: raw scores normalised by their fp32 sum in selection
 // order + 1e-20, times the routed scaling.  The dispatch of the k distinct
 // experts: chunk i = the route of the i-th smallest expert id.  The same
-// winners, order and weights as the router's own finisher.  Every block
-// computes it (into shared memory); block 0 also writes the routing and the
+// winners, order and weights as the router's own finisher.  Every warp of
+// the launch computes it; warp 0 of block 0 also writes the routing and the
 // dispatch to memory for the down kernel and the caller.
-__device__ void fused_topk(const GemvArgs &a, Chunk *s_ch, int32_t *s_rt) {
+__device__ TopkRegs fused_topk(const GemvArgs &a) {
     const int lane = threadIdx.x & 31;
     const int E = a.tk_E, k = a.tk_k;
     float bs[16], sc[16];
@@ -155,7 +169,12 @@ __device__ void fused_topk(const GemvArgs &a, Chunk *s_ch, int32_t *s_rt) {
         ssum += __shfl_sync(LMOE_FULL, my_s, j);
         pos += __shfl_sync(LMOE_FULL, my_e, j) < my_e;
     }
-    if (lane >= k) return;
+    TopkRegs r;
+    r.e = my_e;
+    r.pos = -1;
+    r.slot = 0;
+    r.w = 0.0f;
+    if (lane >= k) return r;
     float wv = a.tk_norm ? my_s / (ssum + 1e-20f) : my_s;
     wv *= a.tk_scaling;
     int slot = 0;
@@ -168,22 +187,28 @@ __device__ void fused_topk(const GemvArgs &a, Chunk *s_ch, int32_t *s_rt) {
             slot = 0;
         }
     }
-    Chunk ch;
-    ch.slot = slot;
-    ch.route_start = pos;
-    ch.ntok = 1;
-    ch.expert = my_e;
-    s_ch[pos] = ch;
-    s_rt[pos] = lane;
-    if (blockIdx.x == 0) {
+    r.pos = pos;
+    r.slot = slot;
+    r.w = wv;
+    if (blockIdx.x == 0 && threadIdx.x < 32) {
         a.tk_idx[lane] = my_e;
         a.tk_w[lane] = wv;
         if (a.tk_idx_user) a.tk_idx_user[lane] = my_e;
         if (a.tk_w_user) a.tk_w_user[lane] = wv;
         a.tk_sorted[pos] = lane;
+        Chunk ch;
+        ch.slot = slot;
+        ch.route_start = pos;
+        ch.ntok = 1;
+        ch.expert = my_e;
         a.tk_chunks[pos] = ch;
         if (lane == 0) *a.tk_nchunks = k;
     }
+    return r;
+}
+
+__device__ __forceinline__ void group_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
 }  // namespace
@@ -220,54 +245,61 @@ __global__ void __launch_bounds__(kStrMaxWarps * 32, 1) stream_kernel(const Gemv
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + c.off_bars) + warp * c.ns;
+    const int kp = c.kp, spp = c.spp;
+    const int gi = warp / kp, q = warp - gi * kp;  // warp group, K part
     uint8_t *ring = smem + c.off_stage + (size_t)warp * c.ns * c.stage_bytes;
+    float4 *part = reinterpret_cast<float4 *>(smem + c.off_part) + (size_t)gi * 2 * kp * NM * 32;
+    const uint8_t *xres = smem + c.off_res;  // panel rows [prow][K]
+    const float2 *sres = reinterpret_cast<const float2 *>(smem + c.off_res + c.res_x);  // [prow][K / 16]
     const int K = a.q0.cols;
+    const int K16 = K >> 4;
     const int rows = a.q0.rows;
     const int RT = rows >> 4;
     const int nck = c.nck;
 
-    if (lane == 0)
-        for (int s = 0; s < c.ns; ++s) mbar_init(&bars[s], 1);
     uint16_t *ptab = reinterpret_cast<uint16_t *>(smem + c.off_ptab);
     if (SMODE == SMODE_GATEUP && a.out_panel)
         for (int i = threadIdx.x; i < a.out_gs; i += blockDim.x) {
-            int p;
-            const int pos = panel_pos(i, a.out_bits, a.out_gs, &p);
-            ptab[i] = static_cast<uint16_t>(pos | (p << 8));
+            int pe;
+            const int pos = panel_pos(i, a.out_bits, a.out_gs, &pe);
+            ptab[i] = static_cast<uint16_t>(pos | (pe << 8));
         }
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    __syncthreads();
 
     pdl_wait();  // chunk table and activation rows come from the preceding kernels
     pdl_trigger();
-    const Chunk *chunk_tab = a.chunks;
-    const int32_t *route_tab = a.sorted_routes;
+    const bool fused = SMODE == SMODE_GATEUP && a.tk_scores != nullptr;
+    TopkRegs tk;
+    tk.e = -1;
+    tk.pos = -1;
+    tk.slot = 0;
+    tk.w = 0.0f;
     int nch;
-    if (SMODE == SMODE_GATEUP && a.tk_scores) {
+    if (fused) {
         // single token: the routing is selected here (see fused_topk)
-        Chunk *s_ch = reinterpret_cast<Chunk *>(smem + c.off_ptab + 256);
-        int32_t *s_rt = reinterpret_cast<int32_t *>(smem + c.off_ptab + 512);
-        if (warp == 0) fused_topk(a, s_ch, s_rt);
-        __syncthreads();
-        chunk_tab = s_ch;
-        route_tab = s_rt;
+        tk = fused_topk(a);
         nch = a.tk_k;
     } else {
         nch = *a.n_chunks;
     }
-    // this warp's units: global (u = gw + j * total warps) or, with the
-    // block-local combine, the block's own pairs (p = blockIdx.x + i * G)
+    if (nch < 0 || nch > c.max_chunks) {
+        set_error(a.err, -3);
+        nch = nch < 0 ? 0 : c.max_chunks;
+    }
+    // this group's units u = first + j * step (unit u: chunk u / own, row
+    // pair u % own of the chunk): spread over every block, or, with the
+    // block-local combine, the block's own pairs p = blockIdx.x + i * G
     const int G = static_cast<int>(gridDim.x);
     const int own = c.local ? (c.pairs - static_cast<int>(blockIdx.x) + G - 1) / G : c.pairs;
     const int units = nch * own;
-    const int first = c.local ? warp : static_cast<int>(blockIdx.x) * c.nc + warp;
-    const int step = c.local ? c.nc : G * c.nc;
+    const int first = c.local ? gi : static_cast<int>(blockIdx.x) + G * gi;
+    const int step = c.local ? c.ng : G * c.ng;
     const int my_units = first < units ? (units - first + step - 1) / step : 0;
-    const int stages = my_units * nck;
+    const int stages = my_units * spp;
 
     // metadata of unit j (all lanes; lane n < ntok holds route n)
     auto load_meta = [&](int j, UnitMeta &m) {
+        m.slot = 0;
+        m.p = 0;
         m.ntok = 0;
         m.route = -1;
         m.row = 0;
@@ -277,7 +309,18 @@ __global__ void __launch_bounds__(kStrMaxWarps * 32, 1) stream_kernel(const Gemv
         const int ch = u / own;
         const int i = u - ch * own;
         m.p = c.local ? static_cast<int>(blockIdx.x) + i * G : i;
-        const Chunk chk = chunk_tab[ch];
+        if (fused) {
+            const unsigned bal = __ballot_sync(LMOE_FULL, tk.pos == ch);
+            const int src = bal ? __ffs(bal) - 1 : 0;
+            m.slot = __shfl_sync(LMOE_FULL, tk.slot, src);
+            m.ntok = 1;
+            if (lane == 0) {
+                m.route = src;
+                m.row = route_row(src, a.route_div, a.shared_base);
+            }
+            return;
+        }
+        const Chunk chk = a.chunks[ch];
         m.slot = chk.slot;
         if (m.slot < 0 || m.slot >= a.n_slots) {
             set_error(a.err, -3);
@@ -289,118 +332,129 @@ __global__ void __launch_bounds__(kStrMaxWarps * 32, 1) stream_kernel(const Gemv
             m.ntok = m.ntok < 0 ? 0 : c.ntok_cap;
         }
         if (lane < m.ntok) {
-            m.route = route_tab[chk.route_start + lane];
+            m.route = a.sorted_routes[chk.route_start + lane];
             if (a.route_w) m.w = a.route_w[m.route];
             m.row = SMODE == SMODE_GATEUP ? route_row(m.route, a.route_div, a.shared_base) : m.route;
+            if (m.row < 0 || m.row >= c.prow) {
+                set_error(a.err, -3);
+                m.row = 0;
+            }
         }
     };
     const uint64_t pol = evict_first_policy();
-    // stage s (round r of a unit with metadata m) into slot s % ns: lane 0
-    // arms the barrier with the stage's bytes and copies the weight tiles;
-    // lane n < ntok copies token n's panel chunk and sums
+    const int n16 = static_cast<int>(c.blk >> 4);  // 16-byte chunks of one weight block
+    // stage s (round r of a unit with metadata m) into slot s % ns: every
+    // lane copies its share of the stage's weight blocks with cp.async and
+    // closes them into one group (the stage's only completion record)
     auto issue = [&](int s, int r, const UnitMeta &m) {
         uint8_t *dst = ring + (size_t)(s % c.ns) * c.stage_bytes;
-        uint64_t *bar = &bars[s % c.ns];
-        if (lane == 0) {
-            const uint32_t bytes = static_cast<uint32_t>(NM / 2 * c.blk + (int64_t)m.ntok * (c.xbytes + c.sbytes));
-            mbar_expect_tx(bar, bytes);
-            const size_t off = ((size_t)m.p * nck + r) * c.blk;
-            bulk_g2s_hint(dst, a.q0.tiles + (size_t)m.slot * a.q0.tile_slot_stride + off,
-                          static_cast<uint32_t>(c.blk), bar, pol);
-            if (SMODE == SMODE_GATEUP)
-                bulk_g2s_hint(dst + c.blk, a.q1.tiles + (size_t)m.slot * a.q1.tile_slot_stride + off,
-                              static_cast<uint32_t>(c.blk), bar, pol);
+        const size_t off = ((size_t)m.p * nck + r) * c.blk;
+        const uint8_t *s0 = a.q0.tiles + (size_t)m.slot * a.q0.tile_slot_stride + off;
+        for (int i = lane; i < n16; i += 32) cp_async16(dst + 16 * i, s0 + 16 * i, pol);
+        if (SMODE == SMODE_GATEUP) {
+            const uint8_t *s1 = a.q1.tiles + (size_t)m.slot * a.q1.tile_slot_stride + off;
+            for (int i = lane; i < n16; i += 32) cp_async16(dst + c.blk + 16 * i, s1 + 16 * i, pol);
         }
-        __syncwarp();
-        if (lane < m.ntok) {
-            bulk_g2s(dst + c.off_x + lane * c.xbytes, a.panel + (size_t)m.row * K + (size_t)r * c.CK,
-                     static_cast<uint32_t>(c.xbytes), bar);
-            bulk_g2s(dst + c.off_s + lane * c.sbytes, a.sum16 + ((size_t)m.row * (K / 16) + (size_t)r * (c.CK / 16)) * 2,
-                     static_cast<uint32_t>(c.sbytes), bar);
-        }
+        cp_async_commit();
     };
 
     UnitMeta cur, nxt;
     load_meta(0, cur);
     load_meta(1, nxt);
-    for (int s = 0; s < c.ns && s < stages; ++s) issue(s, s % nck, s < nck ? cur : nxt);
+    // one group per ring slot from the start (empty past the last stage), so
+    // before stage s exactly s + ns groups are committed
+    for (int i = 0; i < c.ns; ++i) {
+        if (i < stages)
+            issue(i, q * spp + i, cur);  // ns <= spp: all of unit 0
+        else
+            cp_async_commit();
+    }
+    // the activation rows, resident while the first stages stream in
+    {
+        const uint4 *src = reinterpret_cast<const uint4 *>(a.panel);
+        uint4 *dst = reinterpret_cast<uint4 *>(smem + c.off_res);
+        for (int i = threadIdx.x; i < (c.res_x >> 4); i += blockDim.x) dst[i] = __ldcg(src + i);
+        const uint4 *ss = reinterpret_cast<const uint4 *>(a.sum16);
+        uint4 *sd = reinterpret_cast<uint4 *>(smem + c.off_res + c.res_x);
+        for (int i = threadIdx.x; i < (c.res_s >> 4); i += blockDim.x) sd[i] = __ldcg(ss + i);
+    }
+    __syncthreads();
 
     // per-lane row bases of the swizzled tiles: matrix m, row half h
-    int crow[NROW], cfx[NROW], srow[NROW], sfx[NROW];
+    int crow[NROW], srow[NROW], sfx[NROW];
 #pragma unroll
     for (int r = 0; r < NROW; ++r) {
         const int rr = g + 8 * (r & 1);
         crow[r] = (r >> 1) * c.TB + rr * c.RB;
-        cfx[r] = ((rr & 7) & c.fm_c) << 4;
         srow[r] = (r >> 1) * c.TB + rr * c.SB;
         sfx[r] = (c.sb_l2 >= 0 ? (rr & c.fm_s) : 0) << 4;
     }
+    const int cfx = (g & c.fm_c) << 4;  // code rows g and g + 8 share the swizzle
     const int tS = 16 * c.RB;  // scale block of a tile (TileGeo)
     const int tB = tS + 16 * c.SB;
 
-    bool failed = false;
     int s = 0;  // stage counter of this warp
-    for (int j = 0; j < my_units && !failed; ++j) {
+    for (int j = 0; j < my_units; ++j) {
         if (j > 0) {
             cur = nxt;
             load_meta(j + 1, nxt);  // needed ns stages before its first round
         }
         const int ntok = cur.ntok, p = cur.p;
         const bool gpath = ntok == 1;
+        // resident panel rows of the unit's tokens
+        const int row0 = __shfl_sync(LMOE_FULL, cur.row, 0);
+        const int rowg = __shfl_sync(LMOE_FULL, cur.row, g < ntok ? g : 0);
+        const int rown0 = __shfl_sync(LMOE_FULL, cur.row, 2 * t < ntok ? 2 * t : 0);
+        const int rown1 = __shfl_sync(LMOE_FULL, cur.row, 2 * t + 1 < ntok ? 2 * t + 1 : 0);
         float racc[NM][4];
 #pragma unroll
         for (int m = 0; m < NM; ++m)
 #pragma unroll
             for (int e = 0; e < 4; ++e) racc[m][e] = 0.0f;
 
-        for (int r = 0; r < nck; ++r, ++s) {
-            const int slot_i = s % c.ns;
-            if (!mbar_wait(&bars[slot_i], (s / c.ns) & 1)) {
-                if (lane == 0) set_error(a.err, -4);
-                failed = true;
-                break;
-            }
-            const uint8_t *sb = ring + (size_t)slot_i * c.stage_bytes;
-            const uint8_t *xs8 = sb + c.off_x;  // token n's panel chunk at n * xbytes
-            const float2 *xsum = reinterpret_cast<const float2 *>(sb + c.off_s);
+        for (int ii = 0; ii < spp; ++ii, ++s) {
+            const int r = q * spp + ii;  // round of this stage
+            cp_async_wait_pending(c.ns - 1);
+            __syncwarp();  // every lane's copies of the stage have landed
+            const uint8_t *sb = ring + (size_t)(s % c.ns) * c.stage_bytes;
             if (gpath) {
                 // ---- one token: columns = the round's 8 groups; lane t
                 // covers words [t * NW, (t + 1) * NW) = groups 2t, 2t + 1
+                const uint8_t *xs8 = xres + ((size_t)row0 * K + (size_t)r * c.CK) * 2;
+                const float2 *xsum = sres + (size_t)row0 * K16 + (size_t)r * (c.CK / 16);
                 float2 gx = make_float2(0.0f, 0.0f);
                 {
                     const int n = lane >> 2, sub = lane & 3;  // 4 lanes per group
-                    for (int q = sub; q < S; q += 4) {
-                        const float2 v = xsum[n * S + q];
+                    for (int qq = sub; qq < S; qq += 4) {
+                        const float2 v = xsum[n * S + qq];
                         gx.x += v.x;
                         gx.y += v.y;
                     }
                 }
-                uint16_t sbr[NM][2][4];
+                // scales / biases of groups 2t and 2t + 1 (adjacent: one word)
+                uint32_t sw[NM][2], bw[NM][2];
 #pragma unroll
                 for (int m = 0; m < NM; ++m)
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
                         const int rr = 2 * m + h;
-                        const int os0 = srow[rr] + ((2 * (2 * t)) ^ sfx[rr]);
-                        const int os1 = srow[rr] + ((2 * (2 * t + 1)) ^ sfx[rr]);
-                        sbr[m][h][0] = sld<uint16_t>(sb + tS + os0);
-                        sbr[m][h][1] = sld<uint16_t>(sb + tB + os0);
-                        sbr[m][h][2] = sld<uint16_t>(sb + tS + os1);
-                        sbr[m][h][3] = sld<uint16_t>(sb + tB + os1);
+                        const int os = srow[rr] + ((4 * t) ^ sfx[rr]);
+                        sw[m][h] = sld<uint32_t>(sb + tS + os);
+                        bw[m][h] = sld<uint32_t>(sb + tB + os);
                     }
                 float d[NM][4];
 #pragma unroll
                 for (int m = 0; m < NM; ++m)
 #pragma unroll
                     for (int e = 0; e < 4; ++e) d[m][e] = 0.0f;
-#pragma unroll
+#pragma unroll 1
                 for (int qc = 0; qc < NW / 4; ++qc) {
                     const int w0 = t * NW + 4 * qc;  // first code word of this chunk in the row
                     const bool act = (g == w0 / WPG);
                     uint32_t raw[NROW][4];
 #pragma unroll
                     for (int rr = 0; rr < NROW; ++rr) {
-                        const uint4 v = sld<uint4>(sb + crow[rr] + ((w0 * 4) ^ cfx[rr]));
+                        const uint4 v = sld<uint4>(sb + crow[rr] + ((w0 * 4) ^ cfx));
                         raw[rr][0] = v.x;
                         raw[rr][1] = v.y;
                         raw[rr][2] = v.z;
@@ -437,8 +491,10 @@ __global__ void __launch_bounds__(kStrMaxWarps * 32, 1) stream_kernel(const Gemv
                 for (int m = 0; m < NM; ++m)
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
-                        const float s0 = Act<TA>::to_f(sbr[m][h][0]), b0 = Act<TA>::to_f(sbr[m][h][1]);
-                        const float s1 = Act<TA>::to_f(sbr[m][h][2]), b1 = Act<TA>::to_f(sbr[m][h][3]);
+                        const float s0 = Act<TA>::to_f(static_cast<uint16_t>(sw[m][h] & 0xffffu));
+                        const float s1 = Act<TA>::to_f(static_cast<uint16_t>(sw[m][h] >> 16));
+                        const float b0 = Act<TA>::to_f(static_cast<uint16_t>(bw[m][h] & 0xffffu));
+                        const float b1 = Act<TA>::to_f(static_cast<uint16_t>(bw[m][h] >> 16));
                         float e0 = d[m][2 * h], e1 = d[m][2 * h + 1];
                         if constexpr (OFFSET) {
                             e0 = fmaf(-kM, P0, e0);
@@ -455,7 +511,7 @@ __global__ void __launch_bounds__(kStrMaxWarps * 32, 1) stream_kernel(const Gemv
                 // ---- several tokens: columns = tokens (lane column g);
                 // per group, lane t's slice of WPS words per row
                 const bool has_b = g < ntok;
-                const uint8_t *xrow = xs8 + (has_b ? g : 0) * c.xbytes;
+                const uint8_t *xrow = xres + ((size_t)rowg * K + (size_t)r * c.CK) * 2;
 #pragma unroll 1
                 for (int G8 = 0; G8 < 8; ++G8) {
                     typename PX::W pw[NROW][WPS];
@@ -465,23 +521,23 @@ __global__ void __launch_bounds__(kStrMaxWarps * 32, 1) stream_kernel(const Gemv
                     for (int rr = 0; rr < NROW; ++rr) {
                         uint32_t wd[WPS];
                         if constexpr (WPS == 1) {
-                            wd[0] = sld<uint32_t>(sb + crow[rr] + (goff ^ cfx[rr]));
+                            wd[0] = sld<uint32_t>(sb + crow[rr] + (goff ^ cfx));
                         } else if constexpr (WPS == 2) {
-                            const uint2 v = sld<uint2>(sb + crow[rr] + (goff ^ cfx[rr]));
+                            const uint2 v = sld<uint2>(sb + crow[rr] + (goff ^ cfx));
                             wd[0] = v.x;
                             wd[1] = v.y;
                         } else {
 #pragma unroll
-                            for (int q = 0; q < WPS / 4; ++q) {
-                                const uint4 v = sld<uint4>(sb + crow[rr] + ((goff + 16 * q) ^ cfx[rr]));
-                                wd[4 * q] = v.x;
-                                wd[4 * q + 1] = v.y;
-                                wd[4 * q + 2] = v.z;
-                                wd[4 * q + 3] = v.w;
+                            for (int qq = 0; qq < WPS / 4; ++qq) {
+                                const uint4 v = sld<uint4>(sb + crow[rr] + ((goff + 16 * qq) ^ cfx));
+                                wd[4 * qq] = v.x;
+                                wd[4 * qq + 1] = v.y;
+                                wd[4 * qq + 2] = v.z;
+                                wd[4 * qq + 3] = v.w;
                             }
                         }
 #pragma unroll
-                        for (int q = 0; q < WPS; ++q) pw[rr][q] = PX::prep(wd[q]);
+                        for (int qq = 0; qq < WPS; ++qq) pw[rr][qq] = PX::prep(wd[qq]);
                         const int os = srow[rr] + ((2 * G8) ^ sfx[rr]);
                         sv[rr] = sld<uint16_t>(sb + tS + os);
                         bv[rr] = sld<uint16_t>(sb + tB + os);
@@ -492,10 +548,11 @@ __global__ void __launch_bounds__(kStrMaxWarps * 32, 1) stream_kernel(const Gemv
                     for (int h = 0; h < 2; ++h) {
                         const int n = 2 * t + h;
                         if (n < ntok) {
-                            const float2 *p2 = reinterpret_cast<const float2 *>(sb + c.off_s + n * c.sbytes) + G8 * S;
+                            const float2 *p2 =
+                                sres + (size_t)(h ? rown1 : rown0) * K16 + (size_t)r * (c.CK / 16) + G8 * S;
 #pragma unroll
-                            for (int q = 0; q < S; ++q) {
-                                const float2 v = p2[q];
+                            for (int qq = 0; qq < S; ++qq) {
+                                const float2 v = p2[qq];
                                 xt[h].x += v.x;
                                 xt[h].y += v.y;
                             }
@@ -537,17 +594,43 @@ __global__ void __launch_bounds__(kStrMaxWarps * 32, 1) stream_kernel(const Gemv
                     }
                 }
             }
-            // release the slot: order this warp's reads of it before the
-            // asynchronous refill, then queue stage s + ns into it
-            fence_proxy_async();
+            // release the slot (every lane is done reading it), then queue
+            // stage s + ns into it
             __syncwarp();
             const int sn = s + c.ns;
             if (sn < stages) {
-                const int jn = sn / nck;  // j or j + 1 (ns <= nck)
-                issue(sn, sn - jn * nck, jn == j ? cur : nxt);
+                const int jn = sn / spp;  // j or j + 1 (ns <= spp)
+                issue(sn, q * spp + (sn - jn * spp), jn == j ? cur : nxt);
+            } else {
+                cp_async_commit();
             }
         }
-        if (failed) break;
+
+        // ---- K parts: each warp leaves its partial sums in the group's
+        // buffer for this unit; one warp (rotating) adds them in part order
+        if (kp > 1) {
+            float4 *pb = part + (size_t)((j & 1) * kp + q) * NM * 32;
+#pragma unroll
+            for (int m = 0; m < NM; ++m) pb[m * 32 + lane] = make_float4(racc[m][0], racc[m][1], racc[m][2], racc[m][3]);
+            group_sync(1 + gi, kp * 32);
+            if (q != j % kp) continue;
+            const float4 *p0 = part + (size_t)(j & 1) * kp * NM * 32;
+#pragma unroll
+            for (int m = 0; m < NM; ++m) {
+                float4 v = p0[m * 32 + lane];
+                for (int qq = 1; qq < kp; ++qq) {
+                    const float4 w = p0[(qq * NM + m) * 32 + lane];
+                    v.x += w.x;
+                    v.y += w.y;
+                    v.z += w.z;
+                    v.w += w.w;
+                }
+                racc[m][0] = v.x;
+                racc[m][1] = v.y;
+                racc[m][2] = v.z;
+                racc[m][3] = v.w;
+            }
+        }
 
         // ---- epilogue of the unit (racc: rows g / g + 8 x token columns 2t, 2t + 1)
         if constexpr (SMODE == SMODE_GATEUP) {
@@ -618,10 +701,7 @@ __global__ void __launch_bounds__(kStrMaxWarps * 32, 1) stream_kernel(const Gemv
                 }
         }
     }
-    if (failed) {
-        // drain: let the copies this warp issued land before it leaves
-        for (int q = s; q < stages && q < s + c.ns; ++q) mbar_wait(&bars[q % c.ns], (q / c.ns) & 1);
-    }
+    cp_async_wait_pending(0);  // only empty groups remain
     if constexpr (SMODE == SMODE_PAIR) {
         if (!c.local || !a.combined) return;
         // block-local combine over the pairs this block owns: each token's
@@ -660,27 +740,99 @@ int sm_count() {
     return g_sms;
 }
 
+constexpr int kStrSmem = 227 * 1024;
+
+inline int align128(int v) { return (v + 127) & ~127; }
+
+// Shared-memory plan for kp warps per unit and ns stages per warp: the
+// panel-position table (256 B), each group's double-buffered partials, the
+// resident activation rows, then the warps' rings; as many warps (a multiple
+// of kp, <= 8) as fit.
+bool plan_fit(StreamCfg &c, int kp, int ns) {
+    const int part_w = kp > 1 ? 2 * c.nm * 32 * 16 : 0;
+    for (int nc = kStrMaxWarps - kStrMaxWarps % kp; nc >= kp; nc -= kp) {
+        const int off_part = 256;
+        const int off_res = align128(off_part + nc * part_w);
+        const long off_stage = align128(off_res + c.res_x + c.res_s);
+        const long smem = off_stage + (long)nc * ns * c.stage_bytes;
+        if (smem > kStrSmem) continue;
+        c.kp = kp;
+        c.ng = nc / kp;
+        c.nc = nc;
+        c.ns = ns;
+        c.spp = c.nck / kp;
+        c.off_ptab = 0;
+        c.off_part = off_part;
+        c.off_res = off_res;
+        c.off_stage = static_cast<int>(off_stage);
+        c.smem = static_cast<int>(smem);
+        return true;
+    }
+    return false;
+}
+
+// Work split for a launch of at most `units` units (local: per block): the
+// K-part count whose slowest warp streams the fewest stages (a one-stage
+// ring counts half again: nothing overlaps its waits), ties to fewer parts.
+// LMOE_STREAM_KP (1, 2, 4 or 8) forces the part count when it fits.
+bool stream_plan(StreamCfg &c, long units, int sms) {
+    static int forced = -1;
+    if (forced < 0) {
+        const char *e = getenv("LMOE_STREAM_KP");
+        forced = e ? atoi(e) : 0;
+    }
+    StreamCfg best = c;
+    double best_cost = 0.0;
+    bool have = false;
+    for (int kp = 1; kp <= 8; kp <<= 1) {
+        if (c.nck % kp) continue;
+        if (forced > 0 && kp != forced) continue;
+        const int spp = c.nck / kp;
+        StreamCfg x = c;
+        int ns = spp < (kp == 1 ? 3 : 2) ? spp : (kp == 1 ? 3 : 2);
+        while (ns >= 1 && !plan_fit(x, kp, ns)) --ns;
+        if (ns < 1) continue;
+        long grid, rounds;
+        if (x.local) {
+            grid = x.grid;
+            rounds = (units + x.ng - 1) / x.ng;
+        } else {
+            grid = (units + x.ng - 1) / x.ng;
+            if (grid > sms) grid = sms;
+            if (grid < 1) grid = 1;
+            rounds = (units + grid * x.ng - 1) / (grid * x.ng);
+        }
+        x.grid = static_cast<int>(grid);
+        double cost = (double)rounds * spp * (x.ns == 1 && spp > 1 ? 1.5 : 1.0);
+        if (kp > 1) cost += 0.5 * rounds;  // the partials' reduction
+        if (!have || cost < best_cost) {
+            best = x;
+            best_cost = cost;
+            have = true;
+        }
+    }
+    if (!have) return false;
+    c = best;
+    return true;
+}
+
 template <typename TA, int BITS, int GS, int SMODE>
-cudaError_t launch_stream_t(const GemvArgs &a, const StreamCfg &c, int max_chunks, cudaStream_t st) {
+cudaError_t launch_stream_t(const GemvArgs &a, const StreamCfg &c0, int max_chunks, cudaStream_t st) {
     auto kern = stream_kernel<TA, BITS, GS, SMODE>;
+    if (a.ntok_max > c0.ntok_cap || max_chunks < 1) return cudaErrorInvalidValue;
+    StreamCfg c = c0;
+    c.max_chunks = max_chunks;
+    const long units = c.local ? (long)max_chunks * ((c.pairs + c.grid - 1) / (c.grid > 0 ? c.grid : 1))
+                               : (long)max_chunks * c.pairs;
+    if (c.local && c.grid < 1) return cudaErrorInvalidValue;
+    if (!stream_plan(c, units, sm_count())) return cudaErrorInvalidValue;
     static int configured = 0;
     if (c.smem > configured) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, c.smem);
         if (e != cudaSuccess) return e;
         configured = c.smem;
     }
-    if (a.ntok_max > c.ntok_cap) return cudaErrorInvalidValue;
-    long grid;
-    if (c.local) {
-        grid = c.grid;
-    } else {
-        const long units_max = (long)max_chunks * c.pairs;
-        grid = (units_max + c.nc - 1) / c.nc;
-        if (grid > sm_count()) grid = sm_count();
-        if (grid < 1) grid = 1;
-    }
-    if (grid < 1) return cudaErrorInvalidValue;
-    return launch_pdl(kern, dim3(static_cast<unsigned>(grid)), dim3(c.nc * 32), c.smem, st, a, c);
+    return launch_pdl(kern, dim3(static_cast<unsigned>(c.grid)), dim3(c.nc * 32), c.smem, st, a, c);
 }
 
 template <typename TA, int SMODE>
@@ -702,15 +854,16 @@ cudaError_t launch_stream_bits(int bits, int gs, const GemvArgs &a, const Stream
 
 }  // namespace
 
-// Shared-memory plan: ns stages per warp, each NM weight tiles plus the
-// round's activation chunk and sums of up to ntok_cap tokens; as many warps
-// (<= 8) as fit in 227 KB.  ns <= chunks per row, so the stage a warp issues
-// after consuming one belongs to its current unit or the next.
-bool stream_config(int smode, int rows, int K, int bits, int gs, bool local, int ntok_cap, StreamCfg *out) {
+// Geometry and the shared-memory footprint: a stage holds the round's weight
+// blocks (gate and up, or one projection); the activation rows the launch
+// may read stay resident.  The work split is chosen at launch (stream_plan).
+bool stream_config(int smode, int rows, int K, int bits, int gs, bool local, int ntok_cap, int prow,
+                   StreamCfg *out) {
     StreamGeo sg;
     if (!stream_geo(rows, K, bits, gs, &sg) || sg.tg.SB != 16) return false;
-    if (ntok_cap < 1 || ntok_cap > kChunkTok) return false;
+    if (ntok_cap < 1 || ntok_cap > kChunkTok || prow < 1) return false;
     StreamCfg c;
+    std::memset(&c, 0, sizeof(c));
     c.nm = smode == SMODE_GATEUP ? 4 : 2;
     c.TB = sg.tg.TB;
     c.RB = sg.tg.RB;
@@ -723,30 +876,16 @@ bool stream_config(int smode, int rows, int K, int bits, int gs, bool local, int
     c.pairs = sg.pairs;
     c.blk = sg.block;
     c.ntok_cap = ntok_cap;
-    c.xbytes = c.CK * 2;       // activation chunk of one token
-    c.sbytes = (c.CK / 16) * 8;  // its 16-column (sum x, sum panel) pairs
-    c.off_x = c.nm * c.TB;
-    c.off_s = c.off_x + ntok_cap * c.xbytes;
-    c.stage_bytes = (c.off_s + ntok_cap * c.sbytes + 127) / 128 * 128;
-    c.off_bars = 0;
-    c.off_ptab = 1024;
-    c.off_stage = 2048;
-    const int budget = 227 * 1024 - c.off_stage;
-    c.ns = kStrStages < c.nck ? kStrStages : c.nck;
-    c.nc = budget / (c.ns * c.stage_bytes);
-    if (c.nc < 4 && c.ns > 3) {
-        c.ns = 3;
-        c.nc = budget / (c.ns * c.stage_bytes);
-    }
-    if (c.nc < 2 && c.ns > 2) {
-        c.ns = 2;
-        c.nc = budget / (c.ns * c.stage_bytes);
-    }
-    if (c.nc > kStrMaxWarps) c.nc = kStrMaxWarps;
-    if (c.nc < 1 || c.nc * c.ns * 8 > c.off_ptab) return false;  // mbarriers below the panel table
-    c.smem = c.off_stage + c.nc * c.ns * c.stage_bytes;
+    c.prow = prow;
+    const long rx = (long)prow * K * 2, rs = (long)prow * (K / 16) * 8;
+    if (rx + rs > kStrSmem) return false;
+    c.res_x = static_cast<int>(rx);
+    c.res_s = static_cast<int>(rs);
+    c.stage_bytes = align128(static_cast<int>(c.nm / 2 * c.blk));
     c.local = local ? 1 : 0;
     c.grid = 0;
+    StreamCfg probe = c;
+    if (!plan_fit(probe, 1, 1)) return false;  // at least one warp with one stage
     *out = c;
     return true;
 }
