@@ -207,8 +207,17 @@ __device__ TopkRegs fused_topk(const GemvArgs &a) {
     return r;
 }
 
+// Named barrier of one warp group (id 1..15; 0 is the block barrier).  The
+// non-.aligned form: no assumption that a warp arrives converged.
 __device__ __forceinline__ void group_sync(int id, int threads) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+    __syncwarp();
+    asm volatile("barrier.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+__device__ __forceinline__ uint32_t dynamic_smem_bytes() {
+    uint32_t v;
+    asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(v));
+    return v;
 }
 
 }  // namespace
@@ -243,6 +252,23 @@ __global__ void __launch_bounds__(kStrMaxWarps * 32, 1) stream_kernel(const Gemv
     static_assert(NW % 4 == 0, "a lane's words per round must be whole 16-byte chunks");
 
     extern __shared__ __align__(128) uint8_t smem[];
+    // the launch plan must describe this block: otherwise flag it and leave
+    // (uniformly, before any barrier)
+    {
+        const int part_w = c.kp > 1 ? 2 * NM * 32 * 16 : 0;
+        const bool ok = static_cast<int>(blockDim.x) == c.nc * 32 && c.kp >= 1 && c.kp * c.ng == c.nc &&
+                        c.spp * c.kp == c.nck && c.ns >= 1 && c.ns <= 4 && c.ns <= c.spp &&
+                        (c.kp == 1 || c.ng <= 15) && c.off_ptab + 256 <= c.off_part &&
+                        c.off_part + c.nc * part_w <= c.off_res && c.off_res + c.res_x + c.res_s <= c.off_stage &&
+                        (long)c.off_stage + (long)c.nc * c.ns * c.stage_bytes <= (long)c.smem &&
+                        (uint32_t)c.smem <= dynamic_smem_bytes() && c.stage_bytes >= 2 * c.TB &&
+                        (SMODE != SMODE_GATEUP || a.out_gs <= 128) && (c.off_res & 15) == 0 &&
+                        (c.res_x & 15) == 0 && (c.stage_bytes & 15) == 0 && (c.off_stage & 15) == 0;
+        if (!ok) {
+            if (threadIdx.x == 0) set_error(a.err, -4);
+            return;
+        }
+    }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
     const int kp = c.kp, spp = c.spp;
@@ -350,6 +376,17 @@ __global__ void __launch_bounds__(kStrMaxWarps * 32, 1) stream_kernel(const Gemv
     // its pair block); PAIR: the pair block of tiles 2p, 2p + 1.
     auto issue = [&](int s, int r, const UnitMeta &m) {
         uint8_t *dst = ring + (size_t)(s % c.ns) * c.stage_bytes;
+        // every copy stays inside its slot's tiles and this warp's ring slot
+        const size_t span = SMODE == SMODE_GATEUP ? ((size_t)(m.p >> 1) * nck + r) * c.blk + (m.p & 1) * c.TB + c.TB
+                                                  : ((size_t)m.p * nck + r + 1) * c.blk;
+        if (m.slot < 0 || m.slot >= a.n_slots || r < 0 || r >= nck || m.p < 0 || m.p >= c.upc ||
+            span > (size_t)a.q0.tile_slot_stride ||
+            (SMODE == SMODE_GATEUP && span > (size_t)a.q1.tile_slot_stride) ||
+            dst < smem + c.off_stage || dst + c.stage_bytes > smem + c.off_stage + (size_t)c.nc * c.ns * c.stage_bytes) {
+            set_error(a.err, -4);
+            cp_async_commit();
+            return;
+        }
         if (SMODE == SMODE_GATEUP) {
             const size_t off = ((size_t)(m.p >> 1) * nck + r) * c.blk + (size_t)(m.p & 1) * c.TB;
             const uint8_t *s0 = a.q0.tiles + (size_t)m.slot * a.q0.tile_slot_stride + off;
@@ -359,10 +396,12 @@ __global__ void __launch_bounds__(kStrMaxWarps * 32, 1) stream_kernel(const Gemv
                 const int o = 16 * (i - which * (n16 / 2));
                 cp_async16(dst + which * c.TB + o, (which ? s1 : s0) + o, pol);
             }
+            __syncwarp();
         } else {
             const size_t off = ((size_t)m.p * nck + r) * c.blk;
             const uint8_t *s0 = a.q0.tiles + (size_t)m.slot * a.q0.tile_slot_stride + off;
             for (int i = lane; i < n16; i += 32) cp_async16(dst + 16 * i, s0 + 16 * i, pol);
+            __syncwarp();
         }
         cp_async_commit();
     };
