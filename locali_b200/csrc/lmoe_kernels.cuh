@@ -272,13 +272,12 @@ bool gemv_config(int mode, int bits, int gs, int K, int ntok_max, GemvCfg *out);
 // panel.  SMODE_PAIR: units of one projection's tile pair, y * w per route,
 // optional block-local combine.
 enum StreamMode { SMODE_GATEUP = 0, SMODE_PAIR = 1 };
-constexpr int kStrMaxWarps = 16;  // warps per block (each feeds itself)
+constexpr int kStrMaxWarps = 8;  // consumer warps per block (each feeds itself)
 constexpr int kStrStages = 4;    // ring stages per warp
 struct StreamCfg {
     int32_t nm, nc, ns, stage_bytes;
     int32_t TB, RB, SB, sb_l2, fm_c, fm_s;
     int32_t CK, nck, pairs;
-    int32_t upc;  // units per chunk: 16-row tiles (GATEUP) or tile pairs (PAIR)
     int64_t blk;
     int32_t ntok_cap;
     // activation rows resident in shared memory for the whole launch: the

@@ -207,17 +207,8 @@ __device__ TopkRegs fused_topk(const GemvArgs &a) {
     return r;
 }
 
-// Named barrier of one warp group (id 1..15; 0 is the block barrier).  The
-// non-.aligned form: no assumption that a warp arrives converged.
 __device__ __forceinline__ void group_sync(int id, int threads) {
-    __syncwarp();
-    asm volatile("barrier.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
-
-__device__ __forceinline__ uint32_t dynamic_smem_bytes() {
-    uint32_t v;
-    asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(v));
-    return v;
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
 }  // namespace
@@ -240,8 +231,8 @@ template <typename TA, int BITS, int GS, int SMODE>
 __global__ void __launch_bounds__(kStrMaxWarps * 32, 1) stream_kernel(const GemvArgs a, const StreamCfg c) {
     using Gm = Geo<BITS, GS>;
     using PX = PairX<TA, BITS>;
-    constexpr int NM = 2;         // matrices per stage: gate + up tile, or the pair's two tiles
-    constexpr int NROW = 2 * NM;  // (matrix, row half) pairs per lane
+    constexpr int NM = SMODE == SMODE_GATEUP ? 4 : 2;  // matrices per stage
+    constexpr int NROW = 2 * NM;                      // (matrix, row half) pairs per lane
     constexpr int WPS = Gm::kWps;                     // words per lane slice of one group
     constexpr int SPW = Gm::kStepsPerWord;            // k16 steps per code word
     constexpr int S = Gm::kSteps;                     // k16 steps per group
@@ -252,23 +243,6 @@ __global__ void __launch_bounds__(kStrMaxWarps * 32, 1) stream_kernel(const Gemv
     static_assert(NW % 4 == 0, "a lane's words per round must be whole 16-byte chunks");
 
     extern __shared__ __align__(128) uint8_t smem[];
-    // the launch plan must describe this block: otherwise flag it and leave
-    // (uniformly, before any barrier)
-    {
-        const int part_w = c.kp > 1 ? 2 * NM * 32 * 16 : 0;
-        const bool ok = static_cast<int>(blockDim.x) == c.nc * 32 && c.kp >= 1 && c.kp * c.ng == c.nc &&
-                        c.spp * c.kp == c.nck && c.ns >= 1 && c.ns <= 4 && c.ns <= c.spp &&
-                        (c.kp == 1 || c.ng <= 15) && c.off_ptab + 256 <= c.off_part &&
-                        c.off_part + c.nc * part_w <= c.off_res && c.off_res + c.res_x + c.res_s <= c.off_stage &&
-                        (long)c.off_stage + (long)c.nc * c.ns * c.stage_bytes <= (long)c.smem &&
-                        (uint32_t)c.smem <= dynamic_smem_bytes() && c.stage_bytes >= 2 * c.TB &&
-                        (SMODE != SMODE_GATEUP || a.out_gs <= 128) && (c.off_res & 15) == 0 &&
-                        (c.res_x & 15) == 0 && (c.stage_bytes & 15) == 0 && (c.off_stage & 15) == 0;
-        if (!ok) {
-            if (threadIdx.x == 0) set_error(a.err, -4);
-            return;
-        }
-    }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
     const int kp = c.kp, spp = c.spp;
@@ -311,11 +285,11 @@ __global__ void __launch_bounds__(kStrMaxWarps * 32, 1) stream_kernel(const Gemv
         set_error(a.err, -3);
         nch = nch < 0 ? 0 : c.max_chunks;
     }
-    // this group's units u = first + j * step (unit u: chunk u / own, tile
-    // or pair u % own of the chunk): spread over every block, or, with the
+    // this group's units u = first + j * step (unit u: chunk u / own, row
+    // pair u % own of the chunk): spread over every block, or, with the
     // block-local combine, the block's own pairs p = blockIdx.x + i * G
     const int G = static_cast<int>(gridDim.x);
-    const int own = c.local ? (c.upc - static_cast<int>(blockIdx.x) + G - 1) / G : c.upc;
+    const int own = c.local ? (c.pairs - static_cast<int>(blockIdx.x) + G - 1) / G : c.pairs;
     const int units = nch * own;
     const int first = c.local ? gi : static_cast<int>(blockIdx.x) + G * gi;
     const int step = c.local ? c.ng : G * c.ng;
@@ -368,40 +342,18 @@ __global__ void __launch_bounds__(kStrMaxWarps * 32, 1) stream_kernel(const Gemv
         }
     };
     const uint64_t pol = evict_first_policy();
-    const int n16 = c.stage_bytes >> 4;  // 16-byte chunks of a stage (two tiles)
+    const int n16 = static_cast<int>(c.blk >> 4);  // 16-byte chunks of one weight block
     // stage s (round r of a unit with metadata m) into slot s % ns: every
-    // lane copies its share of the stage's weight tiles with cp.async and
-    // closes them into one group (the stage's only completion record).
-    // GATEUP: tile p of gate, then the same tile of up (each the half of
-    // its pair block); PAIR: the pair block of tiles 2p, 2p + 1.
+    // lane copies its share of the stage's weight blocks with cp.async and
+    // closes them into one group (the stage's only completion record)
     auto issue = [&](int s, int r, const UnitMeta &m) {
         uint8_t *dst = ring + (size_t)(s % c.ns) * c.stage_bytes;
-        // every copy stays inside its slot's tiles and this warp's ring slot
-        const size_t span = SMODE == SMODE_GATEUP ? ((size_t)(m.p >> 1) * nck + r) * c.blk + (m.p & 1) * c.TB + c.TB
-                                                  : ((size_t)m.p * nck + r + 1) * c.blk;
-        if (m.slot < 0 || m.slot >= a.n_slots || r < 0 || r >= nck || m.p < 0 || m.p >= c.upc ||
-            span > (size_t)a.q0.tile_slot_stride ||
-            (SMODE == SMODE_GATEUP && span > (size_t)a.q1.tile_slot_stride) ||
-            dst < smem + c.off_stage || dst + c.stage_bytes > smem + c.off_stage + (size_t)c.nc * c.ns * c.stage_bytes) {
-            set_error(a.err, -4);
-            cp_async_commit();
-            return;
-        }
+        const size_t off = ((size_t)m.p * nck + r) * c.blk;
+        const uint8_t *s0 = a.q0.tiles + (size_t)m.slot * a.q0.tile_slot_stride + off;
+        for (int i = lane; i < n16; i += 32) cp_async16(dst + 16 * i, s0 + 16 * i, pol);
         if (SMODE == SMODE_GATEUP) {
-            const size_t off = ((size_t)(m.p >> 1) * nck + r) * c.blk + (size_t)(m.p & 1) * c.TB;
-            const uint8_t *s0 = a.q0.tiles + (size_t)m.slot * a.q0.tile_slot_stride + off;
             const uint8_t *s1 = a.q1.tiles + (size_t)m.slot * a.q1.tile_slot_stride + off;
-            for (int i = lane; i < n16; i += 32) {
-                const int which = i >= n16 / 2;
-                const int o = 16 * (i - which * (n16 / 2));
-                cp_async16(dst + which * c.TB + o, (which ? s1 : s0) + o, pol);
-            }
-            __syncwarp();
-        } else {
-            const size_t off = ((size_t)m.p * nck + r) * c.blk;
-            const uint8_t *s0 = a.q0.tiles + (size_t)m.slot * a.q0.tile_slot_stride + off;
-            for (int i = lane; i < n16; i += 32) cp_async16(dst + 16 * i, s0 + 16 * i, pol);
-            __syncwarp();
+            for (int i = lane; i < n16; i += 32) cp_async16(dst + c.blk + 16 * i, s1 + 16 * i, pol);
         }
         cp_async_commit();
     };
@@ -682,13 +634,14 @@ __global__ void __launch_bounds__(kStrMaxWarps * 32, 1) stream_kernel(const Gemv
 
         // ---- epilogue of the unit (racc: rows g / g + 8 x token columns 2t, 2t + 1)
         if constexpr (SMODE == SMODE_GATEUP) {
-            // matrices: 0 = gate tile p, 1 = the same up tile
-            {
-                const int rt = p;
+            // matrices: 0 / 1 = gate tiles 2p / 2p + 1, 2 / 3 = the same up tiles
+#pragma unroll
+            for (int ti = 0; ti < 2; ++ti) {
+                const int rt = 2 * p + ti;
                 float hv[4], hp[4];
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
-                    const float h = swiglu_h<TA>(racc[0][e], racc[1][e], a.limit, a.swiglu_mode);
+                    const float h = swiglu_h<TA>(racc[ti][e], racc[2 + ti][e], a.limit, a.swiglu_mode);
                     const int n = 2 * t + (e & 1);
                     const int row = rt * 16 + g + 8 * (e >> 1);
                     const int route = __shfl_sync(LMOE_FULL, cur.route, n < ntok ? n : 0);
@@ -833,7 +786,7 @@ bool stream_plan(StreamCfg &c, long units, int sms) {
     bool have = false;
     for (int kp = 1; kp <= 8; kp <<= 1) {
         if (c.nck % kp) continue;
-        if (forced > 0 && c.nck % forced == 0 && kp != forced) continue;
+        if (forced > 0 && kp != forced) continue;
         const int spp = c.nck / kp;
         StreamCfg x = c;
         int ns = spp < (kp == 1 ? 3 : 2) ? spp : (kp == 1 ? 3 : 2);
@@ -869,8 +822,8 @@ cudaError_t launch_stream_t(const GemvArgs &a, const StreamCfg &c0, int max_chun
     if (a.ntok_max > c0.ntok_cap || max_chunks < 1) return cudaErrorInvalidValue;
     StreamCfg c = c0;
     c.max_chunks = max_chunks;
-    const long units = c.local ? (long)max_chunks * ((c.upc + c.grid - 1) / (c.grid > 0 ? c.grid : 1))
-                               : (long)max_chunks * c.upc;
+    const long units = c.local ? (long)max_chunks * ((c.pairs + c.grid - 1) / (c.grid > 0 ? c.grid : 1))
+                               : (long)max_chunks * c.pairs;
     if (c.local && c.grid < 1) return cudaErrorInvalidValue;
     if (!stream_plan(c, units, sm_count())) return cudaErrorInvalidValue;
     static int configured = 0;
@@ -911,7 +864,7 @@ bool stream_config(int smode, int rows, int K, int bits, int gs, bool local, int
     if (ntok_cap < 1 || ntok_cap > kChunkTok || prow < 1) return false;
     StreamCfg c;
     std::memset(&c, 0, sizeof(c));
-    c.nm = 2;
+    c.nm = smode == SMODE_GATEUP ? 4 : 2;
     c.TB = sg.tg.TB;
     c.RB = sg.tg.RB;
     c.SB = sg.tg.SB;
@@ -921,7 +874,6 @@ bool stream_config(int smode, int rows, int K, int bits, int gs, bool local, int
     c.CK = sg.CK;
     c.nck = sg.nck;
     c.pairs = sg.pairs;
-    c.upc = smode == SMODE_GATEUP ? 2 * sg.pairs : sg.pairs;
     c.blk = sg.block;
     c.ntok_cap = ntok_cap;
     c.prow = prow;
@@ -929,7 +881,7 @@ bool stream_config(int smode, int rows, int K, int bits, int gs, bool local, int
     if (rx + rs > kStrSmem) return false;
     c.res_x = static_cast<int>(rx);
     c.res_s = static_cast<int>(rs);
-    c.stage_bytes = align128(static_cast<int>(c.blk));  // two tiles
+    c.stage_bytes = align128(static_cast<int>(c.nm / 2 * c.blk));
     c.local = local ? 1 : 0;
     c.grid = 0;
     StreamCfg probe = c;
