@@ -237,6 +237,13 @@ struct FoldOffset<__nv_bfloat16> {
 template <typename TA, int BITS>
 struct PairX;
 
+// (v & mask) | magic as one three-input logic operation (LUT 0xEA = a & b | c).
+__device__ __forceinline__ uint32_t and_or(uint32_t v, uint32_t mask, uint32_t magic) {
+    uint32_t r;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(v), "r"(mask), "r"(magic));
+    return r;
+}
+
 template <typename TA>
 struct PairX<TA, 2> {
     struct W {
@@ -245,7 +252,7 @@ struct PairX<TA, 2> {
     __device__ __forceinline__ static W prep(uint32_t w) { return W{w, w >> 6, w >> 12}; }
     __device__ __forceinline__ static uint32_t get(const W &w, int m) {
         const uint32_t v = m < 3 ? w.v0 : (m < 6 ? w.v1 : w.v2);
-        const uint32_t r = (v & (0x00030003u << (2 * (m % 3)))) | Act<TA>::kMagic;
+        const uint32_t r = and_or(v, 0x00030003u << (2 * (m % 3)), Act<TA>::kMagic);
         return FoldOffset<TA>::value ? r : Act<TA>::sub_magic(r);
     }
 };
@@ -255,7 +262,7 @@ struct PairX<TA, 4> {
     using W = uint32_t;
     __device__ __forceinline__ static W prep(uint32_t w) { return w; }
     __device__ __forceinline__ static uint32_t get(W w, int m) {
-        const uint32_t r = ((w >> (4 * m)) & 0x000F000Fu) | Act<TA>::kMagic;
+        const uint32_t r = and_or(w >> (4 * m), 0x000F000Fu, Act<TA>::kMagic);
         return FoldOffset<TA>::value ? r : Act<TA>::sub_magic(r);
     }
 };
