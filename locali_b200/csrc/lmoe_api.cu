@@ -298,6 +298,7 @@ int run_experts(const lmoe_layer *l, const Layout &L, void *ws, int T, const flo
     gu.limit = l->swiglu_limit;
     gu.swiglu_mode = l->swiglu_mode;
     gu.shared_base = extra.shared_base;  // the shared expert's routes read token rows
+    gu.chunks_est = T * k + (extra.shared_base > 0 ? T : 0);
 #ifdef LMOE_PROFILE_TRACE
     gu.trace = g_trace;
     gu.trace_units = g_trace_units;
@@ -345,6 +346,7 @@ int run_experts(const lmoe_layer *l, const Layout &L, void *ws, int T, const flo
     dn.n_tok = T;
     dn.shared_base = extra.shared_base;
     dn.residual = extra.residual;
+    dn.chunks_est = gu.chunks_est;
     const int dprow = T * k + (extra.shared_base > 0 ? T : 0);  // h panel rows: routed + shared routes
     if (down_streamed(ex, false, ntok_max, dprow, &sc)) {
         // Few tokens: blocks own row pairs and combine locally.  More
@@ -1088,6 +1090,7 @@ int lmoe_gateup_swiglu(const lmoe_experts *experts, const void *x, int32_t token
     gu.out_panel = 0;
     gu.limit = limit;
     gu.swiglu_mode = swiglu_mode;
+    gu.chunks_est = R;
     if (streamed)
         return cuda_rc(launch_stream(SMODE_GATEUP, pa.act_f16, experts->gate.bits, experts->gate.group_size, gu, sc,
                                      L.max_chunks, st));
@@ -1138,6 +1141,7 @@ int lmoe_gather_qmm(const lmoe_qproj *proj, int32_t n_slots, int32_t rows, int32
     q.sum16 = pa.sum16;
     q.route_div = 1;
     q.out = static_cast<uint16_t *>(y);
+    q.chunks_est = routes;
     if (streamed)  // y per route (no weights: the plain gather_qmm output)
         return cuda_rc(launch_stream(SMODE_PAIR, pa.act_f16, proj->bits, proj->group_size, q, sc, L.max_chunks, st));
     if (!proj->weight) return LMOE_EINVAL;

@@ -204,6 +204,7 @@ struct GemvArgs {
     const int32_t *sorted_routes;
     int32_t n_slots;
     int32_t ntok_max;
+    int32_t chunks_est;  // host-side planning hint: chunks this launch expects (0: the table's capacity)
     uint16_t *out;
     float *out_sum16;  // [routes, rows/16, 2]
     int32_t out_panel, out_bits, out_gs;
