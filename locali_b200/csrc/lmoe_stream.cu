@@ -342,7 +342,6 @@ __global__ void __launch_bounds__(kStrMaxWarps * 32, 1) stream_kernel(const Gemv
         }
     };
     const uint64_t pol = evict_first_policy();
-    const uint64_t pol_keep = evict_last_policy();  // activation rows: read by every block
     const int n16 = static_cast<int>(c.blk >> 4);  // 16-byte chunks of one weight block
     // stage s (round r of a unit with metadata m) into slot s % ns: every
     // lane copies its share of the stage's weight blocks with cp.async and
@@ -359,31 +358,47 @@ __global__ void __launch_bounds__(kStrMaxWarps * 32, 1) stream_kernel(const Gemv
         cp_async_commit();
     };
 
-    // the activation rows, resident for the whole launch: every thread's
-    // share as cp.async copies in this thread's first group (all of them in
-    // flight at once)
-    {
-        const uint8_t *src = reinterpret_cast<const uint8_t *>(a.panel);
-        const uint8_t *ss = reinterpret_cast<const uint8_t *>(a.sum16);
-        uint8_t *dst = smem + c.off_res;
-        for (int i = threadIdx.x; i < (c.res_x >> 4); i += blockDim.x) cp_async16(dst + 16 * i, src + 16 * i, pol_keep);
-        for (int i = threadIdx.x; i < (c.res_s >> 4); i += blockDim.x)
-            cp_async16(dst + c.res_x + 16 * i, ss + 16 * i, pol_keep);
-        cp_async_commit();
-    }
     UnitMeta cur, nxt;
     load_meta(0, cur);
     load_meta(1, nxt);
     // one group per ring slot from the start (empty past the last stage), so
-    // before stage s exactly 1 + s + ns groups are committed
+    // before stage s exactly s + ns groups are committed
     for (int i = 0; i < c.ns; ++i) {
         if (i < stages)
             issue(i, q * spp + i, cur);  // ns <= spp: all of unit 0
         else
             cp_async_commit();
     }
-    cp_async_wait_pending(c.ns);  // this thread's resident rows have landed
-    __syncthreads();              // and everyone's
+    // the activation rows, resident while the first stages stream in: each
+    // thread loads up to 8 of its 16-byte pieces before storing any, so their
+    // latencies overlap
+    {
+        const uint4 *src = reinterpret_cast<const uint4 *>(a.panel);
+        uint4 *dst = reinterpret_cast<uint4 *>(smem + c.off_res);
+        const uint4 *ss = reinterpret_cast<const uint4 *>(a.sum16);
+        uint4 *sd = reinterpret_cast<uint4 *>(smem + c.off_res + c.res_x);
+        const int nx = c.res_x >> 4, n = nx + (c.res_s >> 4);
+        const int T = static_cast<int>(blockDim.x);
+        for (int base = threadIdx.x; base < n; base += 8 * T) {
+            uint4 v[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const int i = base + k * T;
+                if (i < n) v[k] = i < nx ? __ldcg(src + i) : __ldcg(ss + (i - nx));
+            }
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const int i = base + k * T;
+                if (i < n) {
+                    if (i < nx)
+                        dst[i] = v[k];
+                    else
+                        sd[i - nx] = v[k];
+                }
+            }
+        }
+    }
+    __syncthreads();
 
     // per-lane row bases of the swizzled tiles: matrix m, row half h
     int crow[NROW], srow[NROW], sfx[NROW];
@@ -827,10 +842,8 @@ cudaError_t launch_stream_t(const GemvArgs &a, const StreamCfg &c0, int max_chun
     if (a.ntok_max > c0.ntok_cap || max_chunks < 1) return cudaErrorInvalidValue;
     StreamCfg c = c0;
     c.max_chunks = max_chunks;
-    // chunks to plan for: each holds at least one route, so the caller's
-    // route count bounds them as well as the table's capacity
-    const long est = a.chunks_est > 0 && a.chunks_est < max_chunks ? a.chunks_est : max_chunks;
-    const long units = c.local ? est * ((c.pairs + c.grid - 1) / (c.grid > 0 ? c.grid : 1)) : est * c.pairs;
+    const long units = c.local ? (long)max_chunks * ((c.pairs + c.grid - 1) / (c.grid > 0 ? c.grid : 1))
+                               : (long)max_chunks * c.pairs;
     if (c.local && c.grid < 1) return cudaErrorInvalidValue;
     if (!stream_plan(c, units, sm_count())) return cudaErrorInvalidValue;
     static int configured = 0;
