@@ -842,8 +842,10 @@ cudaError_t launch_stream_t(const GemvArgs &a, const StreamCfg &c0, int max_chun
     if (a.ntok_max > c0.ntok_cap || max_chunks < 1) return cudaErrorInvalidValue;
     StreamCfg c = c0;
     c.max_chunks = max_chunks;
-    const long units = c.local ? (long)max_chunks * ((c.pairs + c.grid - 1) / (c.grid > 0 ? c.grid : 1))
-                               : (long)max_chunks * c.pairs;
+    // chunks to plan for: each holds at least one route, so the caller's
+    // route count bounds them as well as the table's capacity
+    const long est = a.chunks_est > 0 && a.chunks_est < max_chunks ? a.chunks_est : max_chunks;
+    const long units = c.local ? est * ((c.pairs + c.grid - 1) / (c.grid > 0 ? c.grid : 1)) : est * c.pairs;
     if (c.local && c.grid < 1) return cudaErrorInvalidValue;
     if (!stream_plan(c, units, sm_count())) return cudaErrorInvalidValue;
     static int configured = 0;
