@@ -207,8 +207,12 @@ __device__ TopkRegs fused_topk(const GemvArgs &a) {
     return r;
 }
 
+// Named barrier of one warp group.  The warp reconverges first and the
+// barrier is the non-aligned form, so it stays defined even where the
+// compiler has not reconverged the warp after a lane-dependent loop.
 __device__ __forceinline__ void group_sync(int id, int threads) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+    __syncwarp();
+    asm volatile("barrier.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
 }  // namespace
