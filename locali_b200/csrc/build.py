@@ -24,7 +24,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
               "-Wno-deprecated-gpu-targets"]
 
-LMOE_SOURCES = ["lmoe_route.cu", "lmoe_gemv.cu", "lmoe_stream.cu", "lmoe_prefill.cu", "lmoe_ep.cu", "lmoe_api.cu"]
+LMOE_SOURCES = ["lmoe_route.cu", "lmoe_gemv.cu", "lmoe_stream.cu", "lmoe_vec.cu", "lmoe_prefill.cu", "lmoe_ep.cu", "lmoe_api.cu"]
 LMOE_DEPS = LMOE_SOURCES + ["lmoe_common.cuh", "lmoe_kernels.cuh"]
 LMOE_LIB = PKG / "liblmoe.so"
 CORE_LIB = PKG / "liblocali_core.so"

@@ -33,6 +33,9 @@ struct Layout {
            nchunks = 0, chunks = 0, xpanel = 0, xsum = 0, hpanel = 0, hsum = 0, yw = 0,
            cnt = 0, dblk = 0, total = 0;
     int max_chunks = 0;
+    // single-token kernel (lmoe_vec.cu): its counter (right after cnt, so the
+    // per-call zeroing covers it: zero_end) and the int8 pieces of h and x
+    size_t vcnt = 0, vhq = 0, vhs = 0, zero_end = 0;
     // prefill path: tiled activation panels of the tcgen05 grouped GEMM
     size_t pfx = 0, pfh = 0;
     int pf_rows = 0, pf_chunks = 0;
@@ -47,8 +50,15 @@ int max_chunks_for(int buckets, int R) {
 // Layout shared by all entry points.  x_rows: rows of the input panel;
 // R: routes; K: input width; I: intermediate width (0 if unused);
 // H_out: output width of the combine (0 if unused); T: tokens.
+// Scratch of the single-token kernel (zero sizes: not used by the layout):
+// counter words (right after cnt, so the per-call zeroing covers them), the
+// int8 pieces of h then x, and their (sum, factor) arrays.
+struct VecSizes {
+    size_t cnt_words = 0, hq_bytes = 0, hs_bytes = 0;
+};
+
 Layout make_layout(int T, int R, int K, int I, int H_out, int buckets, int E_router,
-                   int ksplit, int x_rows) {
+                   int ksplit, int x_rows, const VecSizes &vs = VecSizes()) {
     Layout L;
     size_t off = 0;
     auto take = [&](size_t bytes) {
@@ -64,6 +74,8 @@ Layout make_layout(int T, int R, int K, int I, int H_out, int buckets, int E_rou
     // prefix of the same zero region.  Everything after is rewritten by each
     // call before it is read.
     L.cnt = take((size_t)T * (H_out / 16) * 4);
+    if (vs.cnt_words) L.vcnt = take(vs.cnt_words * 4);
+    L.zero_end = off;
     // logits, then (score, biased score) per (token, expert)
     L.partial = take((size_t)ksplit * T * E_router * 4 + 8 + (size_t)T * E_router * 8);
     L.idx = take((size_t)R * 4);
@@ -80,17 +92,49 @@ Layout make_layout(int T, int R, int K, int I, int H_out, int buckets, int E_rou
     L.hpanel = take((size_t)R * I * 2);
     L.hsum = take((size_t)R * (I / 16) * 8);
     L.yw = take((size_t)R * H_out * 2);
+    if (vs.hq_bytes) {
+        L.vhq = take(vs.hq_bytes);
+        L.vhs = take(vs.hs_bytes);
+    }
     L.total = off;
     return L;
 }
 
 // shared: one more route per token for the block's shared expert (its
 // routes follow the T * top_k routed ones)
+// Single-token layers whose geometry the integer tensor-pipe kernel
+// (lmoe_vec.cu) covers: gate and up alike, one group size for all three
+// projections, the stream format's geometry, at most 32 routes.  Whether the
+// stream copies exist is checked per call; the workspace is sized on the
+// geometry alone.
+bool vec_geometry(const lmoe_layer *l, int R, VecCfg *cfg) {
+    const lmoe_experts &ex = l->experts;
+    if (ex.gate.bits != ex.up.bits || ex.gate.group_size != ex.up.group_size) return false;
+    VecCfg c;
+    if (!vec_layer_config(ex.hidden, ex.inter, ex.gate.bits, ex.gate.group_size, ex.down.bits, ex.down.group_size,
+                          R, &c))
+        return false;
+    if (cfg) *cfg = c;
+    return true;
+}
+
+VecSizes vec_sizes(const lmoe_layer *l, int T, int R) {
+    VecSizes vs;
+    VecCfg c;
+    if (T != 1 || !vec_geometry(l, R, &c)) return vs;
+    const lmoe_experts &ex = l->experts;
+    vs.cnt_words = 1;
+    vs.hq_bytes = al((size_t)R * ex.inter * 2) + al((size_t)ex.hidden * 2);
+    vs.hs_bytes = al((size_t)R * (ex.inter / 32) * 8 + 16) + al((size_t)(ex.hidden / ex.gate.group_size) * 8 + 16);
+    return vs;
+}
+
 Layout layer_layout(const lmoe_layer *l, int T, bool shared = false) {
     const int H = l->experts.hidden, I = l->experts.inter;
     const int R = T * l->router.top_k + (shared ? T : 0);
     return make_layout(T, R, H, I, H, l->router.n_experts + 1, l->router.n_experts,
-                       router_ksplit(T, l->router.n_experts, H, l->experts.dtype == LMOE_F16), T);
+                       router_ksplit(T, l->router.n_experts, H, l->experts.dtype == LMOE_F16), T,
+                       vec_sizes(l, T, R));
 }
 
 // Layout of the prefill path: the shared routing regions and the y*w rows
@@ -273,7 +317,97 @@ struct Extra {
     const float2 *tk_scores = nullptr;
     int32_t *idx_user = nullptr;
     float *w_user = nullptr;
+    // the layer's natural activation rows (single-token kernel), or nullptr,
+    // and whether the router already wrote their int8 pieces
+    const uint16_t *x = nullptr;
+    bool x_ready = false;
 };
+
+// The single-token kernel runs this call: its scratch is in the layout, x
+// is 16-byte aligned and every projection has its stream copy.
+bool vec_ready(const lmoe_layer *l, const Layout &L, const void *x, int shared_base, VecCfg *cfg) {
+    const lmoe_experts &ex = l->experts;
+    const int k = l->router.top_k, R = k + (shared_base > 0 ? 1 : 0);
+    if (!x || !aligned16(x) || !L.vhq) return false;
+    if (shared_base > 0 && shared_base != k) return false;
+    if (!view(ex.gate, ex.n_slots, ex.inter, ex.hidden).tiles || !view(ex.up, ex.n_slots, ex.inter, ex.hidden).tiles ||
+        !view(ex.down, ex.n_slots, ex.hidden, ex.inter).tiles)
+        return false;
+    return vec_geometry(l, R, cfg);
+}
+// x's int8 pieces and (sum, factor) follow those of h in their regions
+uint8_t *vec_xq(const Layout &L, const lmoe_layer *l, int R, void *ws) {
+    return at<uint8_t>(ws, L.vhq) + al((size_t)R * l->experts.inter * 2);
+}
+float2 *vec_xs(const Layout &L, const lmoe_layer *l, int R, void *ws) {
+    return reinterpret_cast<float2 *>(at<uint8_t>(ws, L.vhs) + al((size_t)R * (l->experts.inter / 32) * 8 + 16));
+}
+
+// Single-token layer on the integer tensor-pipe kernel (lmoe_vec.cu): gate/up
+// + SwiGLU into h (natural layout, in the h panel's region) and its int8
+// pieces, then down + combine, in one launch.  Returns 1 (not taken) when the
+// layer or call does not qualify: the caller then runs the stream / bulk-copy
+// GEMVs.
+int run_vec(const lmoe_layer *l, const Layout &L, void *ws, const float *route_w, void *out, cudaStream_t st,
+            cudaEvent_t ev_gateup, const Extra &extra) {
+    const lmoe_experts &ex = l->experts;
+    const int H = ex.hidden, I = ex.inter, k = l->router.top_k;
+    const int R = k + (extra.shared_base > 0 ? 1 : 0);
+    VecCfg c;
+    if (!vec_ready(l, L, extra.x, extra.shared_base, &c)) return 1;
+    const QView qg = view(ex.gate, ex.n_slots, I, H), qu = view(ex.up, ex.n_slots, I, H);
+    const QView qd = view(ex.down, ex.n_slots, H, I);
+    VecArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.q0 = qg;
+    a.q1 = qu;
+    a.q2 = qd;
+    a.x = extra.x;
+    a.chunks = at<Chunk>(ws, L.chunks);
+    a.n_chunks = at<int32_t>(ws, L.nchunks);
+    a.sorted_routes = at<int32_t>(ws, L.sorted);
+    a.n_slots = ex.n_slots;
+    a.max_chunks = L.max_chunks;
+    a.routes = R;
+    a.shared_base = extra.shared_base;
+    if (extra.tk_scores) {
+        const lmoe_router &r = l->router;
+        a.tk_scores = extra.tk_scores;
+        a.tk_E = r.n_experts;
+        a.tk_k = k;
+        a.tk_norm = r.norm_topk;
+        a.tk_scaling = r.routed_scaling;
+        a.tk_expert_slot = l->expert_slot;
+        a.tk_idx = at<int32_t>(ws, L.idx);
+        a.tk_w = at<float>(ws, L.w);
+        a.tk_idx_user = extra.idx_user;
+        a.tk_w_user = extra.w_user;
+        a.tk_sorted = at<int32_t>(ws, L.sorted);
+        a.tk_chunks = at<Chunk>(ws, L.chunks);
+        a.tk_nchunks = at<int32_t>(ws, L.nchunks);
+    }
+    a.hq = at<uint8_t>(ws, L.vhq);
+    a.hs = at<float2>(ws, L.vhs);
+    a.xq = vec_xq(L, l, R, ws);
+    a.xs = vec_xs(L, l, R, ws);
+    a.x_ready = extra.x_ready ? 1 : 0;
+    a.limit = l->swiglu_limit;
+    a.swiglu_mode = l->swiglu_mode;
+    a.route_w = route_w;
+    a.top_k = k;
+    a.residual = extra.residual;
+    a.out = static_cast<uint16_t *>(out);
+    // per-route rows when asked for, or when there is no combined output
+    a.yw = extra.yw ? extra.yw : (out ? nullptr : at<uint16_t>(ws, L.yw));
+    a.hready = at<uint32_t>(ws, L.vcnt);
+    a.err = at<int32_t>(ws, L.status);
+    const int rc = cuda_rc(launch_vec_layer(ex.dtype == LMOE_F16, ex.gate.bits, ex.down.bits, ex.gate.group_size, a,
+                                            c, st));
+    if (rc) return rc;
+    // one launch covers both projections: the gate/up event follows it
+    if (ev_gateup && cudaEventRecord(ev_gateup, st) != cudaSuccess) return LMOE_ECUDA;
+    return LMOE_OK;
+}
 
 // gate/up + SwiGLU then down + combine over an already dispatched layer.
 // out == nullptr: the down kernel leaves the rounded y*w rows of every
@@ -282,6 +416,11 @@ int run_experts(const lmoe_layer *l, const Layout &L, void *ws, int T, const flo
                 void *out, cudaStream_t st, cudaEvent_t ev_gateup = nullptr, Extra extra = Extra()) {
     const lmoe_experts &ex = l->experts;
     const int H = ex.hidden, I = ex.inter, k = l->router.top_k;
+    if (T == 1) {
+        const int vr = run_vec(l, L, ws, route_w, out, st, ev_gateup, extra);
+        if (vr <= 0) return vr;  // ran (or failed); 1: not taken
+        if (extra.x_ready) return LMOE_EINVAL;  // the router wrote pieces, not the panel
+    }
     const int ntok_max = layer_chunk(l, T);
     if (ntok_max < 1) return LMOE_EUNSUPPORTED;
     GemvArgs gu = gemv_base(L, ws, ex.n_slots, ntok_max);
@@ -613,9 +752,14 @@ static bool topk_fusable(const lmoe_layer *l, int T, const int32_t *hash_idx, bo
 
 // fused: the top-k and dispatch are left to the stream gate/up kernel
 // (topk_fusable holds); only the logit blocks run here.
+// vec_shared_base >= 0: the layer call's shared-expert route base (0: none);
+// when the single-token kernel will run the call, the router writes x's int8
+// pieces for it instead of the GEMV panel (*x_pieces = true).
 static int route_impl(const lmoe_router &r, int H, int dtype, const lmoe_layer *l, const Layout &L, const void *x,
                       int T, int32_t *idx_user, float *w_user, void *ws, cudaStream_t st,
-                      const int32_t *hash_idx = nullptr, bool fused = false) {
+                      const int32_t *hash_idx = nullptr, bool fused = false, int vec_shared_base = -1,
+                      bool *x_pieces = nullptr) {
+    if (x_pieces) *x_pieces = false;
     const int k = r.top_k;
     const int R = T * k;
     const int ksplit = router_ksplit(T, r.n_experts, H, dtype == LMOE_F16);
@@ -644,12 +788,21 @@ static int route_impl(const lmoe_router &r, int H, int dtype, const lmoe_layer *
         // this call's combine counters start at zero whatever the workspace
         // held before (another token count or entry point)
         a.zero = at<uint32_t>(ws, L.cnt);
-        a.zero_words = T * (l->experts.hidden / 16);
+        a.zero_words = static_cast<int32_t>((L.zero_end - L.cnt) / 4);  // combine and unit counters
         if (!L.prefill) {  // the decode GEMVs read x through the router's panel
             a.xpanel = at<uint16_t>(ws, L.xpanel);
             a.xsum16 = at<float>(ws, L.xsum);
             a.pbits = l->experts.gate.bits;
             a.pgs = l->experts.gate.group_size;
+            if (T == 1 && vec_shared_base >= 0 && vec_ready(l, L, x, vec_shared_base, nullptr)) {
+                // the single-token kernel reads x's int8 pieces instead
+                const int Rv = r.top_k + (vec_shared_base > 0 ? 1 : 0);
+                a.xq = vec_xq(L, l, Rv, ws);
+                a.xs = vec_xs(L, l, Rv, ws);
+                a.xpanel = nullptr;
+                a.xsum16 = nullptr;
+                if (x_pieces) *x_pieces = true;
+            }
         }
     }
     a.act_f16 = dtype == LMOE_F16;
@@ -796,11 +949,14 @@ static int layer_entry(const lmoe_layer *layer, const void *x, int32_t tokens, c
     // the routing is only complete after gate/up when the top-k is fused:
     // a caller that waits on ev_routed gets the separate finisher
     const bool fused = !ev_routed && topk_fusable(layer, tokens, hash_idx, shared_slot >= 0, pf);
+    bool x_pieces = false;
     rc = route_impl(layer->router, layer->experts.hidden, layer->experts.dtype, layer, L, x, tokens, idx, w,
-                    workspace, st, hash_idx, fused);
+                    workspace, st, hash_idx, fused, shared ? tokens * layer->router.top_k : 0, &x_pieces);
     if (rc) return rc;
     Extra ex;
     ex.residual = static_cast<const uint16_t *>(residual);
+    ex.x = static_cast<const uint16_t *>(x);
+    ex.x_ready = x_pieces;
     if (fused) {
         ex.tk_scores = router_scores(L, workspace, 1, tokens, layer->router.n_experts);
         ex.idx_user = idx;
@@ -995,7 +1151,7 @@ static int routed_impl(const lmoe_layer *layer, const void *x, int32_t tokens, c
     pa.rows = tokens;
     pa.K = ex.hidden;
     pa.zero = at<uint32_t>(workspace, L.cnt);  // this call's combine counters
-    pa.zero_words = tokens * (ex.hidden / 16);
+    pa.zero_words = static_cast<int32_t>((L.zero_end - L.cnt) / 4);
     pa.panel = at<uint16_t>(workspace, L.xpanel);
     pa.sum16 = at<float>(workspace, L.xsum);
     pa.bits = ex.gate.bits;
@@ -1011,6 +1167,7 @@ static int routed_impl(const lmoe_layer *layer, const void *x, int32_t tokens, c
     if (rc) return rc;
     Extra e;
     e.yw = static_cast<uint16_t *>(products);
+    e.x = static_cast<const uint16_t *>(x);
     return run_experts(layer, L, workspace, tokens, w, out, st, nullptr, e);
 }
 

@@ -127,6 +127,10 @@ struct RouterArgs {
     float scaling;
     float *partial;  // [ksplit][T][E] logits
     float2 *scores;  // [T][E] (score, score + bias) for the element-wise scorings, or nullptr
+    // single token: int8 pieces of x for the single-token layer kernel
+    // (pbits / pgs of its gate/up), or nullptr
+    uint8_t *xq;
+    float2 *xs;
     // panel producer for the gate/up consumer (optional)
     uint16_t *xpanel;
     float *xsum16;  // [T, H/16, 2]: per 16 columns, sum of x and sum of the stored panel values
@@ -268,6 +272,140 @@ constexpr int kHdrPanel = 20;
 constexpr int kHdrPanelN = 28;
 bool gemv_config(int mode, int bits, int gs, int K, int ntok_max, GemvCfg *out);
 
+// Single-token routing held in registers (lane j < k: the j-th winner's
+// expert id, weight, arena slot, and its rank among the winners' ids, which
+// is its chunk in the dispatch; other lanes hold pos = -1).
+struct TopkRegs {
+    int e, pos, slot;
+    float w;
+};
+
+// Order-preserving 32-bit key of a biased score for the warp max: larger
+// key = larger score; -0 folds into +0 (float compares treat them as equal)
+// and -inf / NaN map to 0, which is never selected.
+__device__ __forceinline__ uint32_t topk_key(float v) {
+    v = v + 0.0f;
+    if (!(v > -INFINITY)) return 0u;
+    const uint32_t b = __float_as_uint(v);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+// Top-k of a single token by one warp from the router's (score, biased
+// score) (arena.py:501-506): selection on the biased score, ties to the
+// lower id.  Each lane keeps its best candidate (first of equals in id
+// order); a round is a warp max of the keys and a warp min of the ids that
+// reach it (redux.sync), and only the winner's lane rescans.  Weights: raw
+// scores normalised by their fp32 sum in selection order + 1e-20, times the
+// routed scaling.  The dispatch of the k distinct experts: chunk i = the
+// route of the i-th smallest expert id.  The same winners, order and weights
+// as the router's own finisher.  Every warp of the launch computes it; warp
+// 0 of block 0 also writes the routing and the dispatch to memory for the
+// down kernel and the caller (write = true; a kernel that only needs the
+// winners passes false).
+template <class A>
+__device__ __forceinline__ TopkRegs fused_topk(const A &a, bool write) {
+    const int lane = threadIdx.x & 31;
+    const int E = a.tk_E, k = a.tk_k;
+    uint32_t key[16];
+    float sc[16];
+    int sl[16];  // arena slots of the candidates, loaded with the scores
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        const int e = lane + 32 * i;
+        key[i] = 0u;
+        sc[i] = 0.0f;
+        sl[i] = e;
+        if (32 * i < E && e < E) {
+            const float2 v = __ldcg(a.tk_scores + e);
+            sc[i] = v.x;
+            key[i] = topk_key(v.y);
+            if (a.tk_expert_slot) sl[i] = __ldg(a.tk_expert_slot + e);
+        }
+    }
+    uint32_t lk = 0u;
+    int lbe = 0x7fffffff, lbsl = 0;
+    float lbs = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+        if (key[i] > lk) {
+            lk = key[i];
+            lbe = lane + 32 * i;
+            lbs = sc[i];
+            lbsl = sl[i];
+        }
+    int my_e = -1, my_slot = 0;
+    float my_s = 0.0f;
+#pragma unroll 1
+    for (int j = 0; j < k; ++j) {
+        const uint32_t mk = __reduce_max_sync(0xffffffffu, lk);
+        const int be = static_cast<int>(__reduce_min_sync(0xffffffffu, lk == mk ? static_cast<uint32_t>(lbe) : 0xffffffffu));
+        const float ws = __shfl_sync(0xffffffffu, lbs, be & 31);
+        const int wsl = __shfl_sync(0xffffffffu, lbsl, be & 31);
+        if (lane == j) {
+            my_e = be;
+            my_s = ws;
+            my_slot = wsl;
+        }
+        if (lbe == be) {  // the winner drops it and rescans
+            lk = 0u;
+            lbe = 0x7fffffff;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                if (lane + 32 * i == be) key[i] = 0u;
+                if (key[i] > lk) {
+                    lk = key[i];
+                    lbe = lane + 32 * i;
+                    lbs = sc[i];
+                    lbsl = sl[i];
+                }
+            }
+        }
+    }
+    float ssum = 0.0f;  // fp32, in selection order
+    int pos = 0;        // rank of this lane's expert id among the winners
+#pragma unroll 1
+    for (int j = 0; j < k; ++j) {
+        ssum += __shfl_sync(0xffffffffu, my_s, j);
+        pos += __shfl_sync(0xffffffffu, my_e, j) < my_e;
+    }
+    TopkRegs r;
+    r.e = my_e;
+    r.pos = -1;
+    r.slot = 0;
+    r.w = 0.0f;
+    if (lane >= k) return r;
+    float wv = a.tk_norm ? my_s / (ssum + 1e-20f) : my_s;
+    wv *= a.tk_scaling;
+    int slot = 0;
+    if (my_e < 0 || my_e >= E) {
+        set_error(a.err, -3);
+    } else {
+        slot = my_slot;
+        if (slot < 0 || slot >= a.n_slots) {
+            set_error(a.err, -3);
+            slot = 0;
+        }
+    }
+    r.pos = pos;
+    r.slot = slot;
+    r.w = wv;
+    if (write && blockIdx.x == 0 && threadIdx.x < 32) {
+        a.tk_idx[lane] = my_e;
+        a.tk_w[lane] = wv;
+        if (a.tk_idx_user) a.tk_idx_user[lane] = my_e;
+        if (a.tk_w_user) a.tk_w_user[lane] = wv;
+        a.tk_sorted[pos] = lane;
+        Chunk ch;
+        ch.slot = slot;
+        ch.route_start = pos;
+        ch.ntok = 1;
+        ch.expert = my_e;
+        a.tk_chunks[pos] = ch;
+        if (lane == 0) *a.tk_nchunks = k;
+    }
+    return r;
+}
+
 // ------------------------------------------------------------ stream GEMV (lmoe_stream.cu)
 // SMODE_GATEUP: units of gate + up tile pairs, clamped SwiGLU into the down
 // panel.  SMODE_PAIR: units of one projection's tile pair, y * w per route,
@@ -317,6 +455,164 @@ inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, siz
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kern, args...);
 }
+
+// ------------------------------------------------------------ int8 activation pieces
+// A group of gs activations as two int8 pieces for the integer MMA of the
+// single-token layer (lmoe_vec.cu): with a power-of-two scale 2^S such that
+// max |x| * 2^S < 2^14, x * 2^S is an integer for every element within 2^6 of
+// the group's largest magnitude, and it splits exactly into hi * 256 + lo
+// (hi in [-64, 64], lo in [-128, 127]).  Stored in the B-operand order of
+// the consumer's code bit width, with the group's fp32 sum and the factor
+// 2^-(S + 8 - bits) that turns the MMA's integer sum back into sum(x * q).
+// Byte offset, inside one group's 2 * GS piece bytes, of element e's piece
+// pc for a consumer with BITS-bit codes.  MMA j of the group (word pair
+// j / NC, code class j % NC) reads 16 bytes: [piece 0: word 2wp, word 2wp+1]
+// [piece 1: ...], four int8 per word in byte order (byte i of a code word
+// holds codes i * NC .. i * NC + NC - 1 of it, class p being code i * NC + p).
+template <int BITS>
+__device__ __forceinline__ int piece_offset(int e, int pc) {
+    constexpr int nc = 8 / BITS, cpw = 32 / BITS;
+    const int w = e / cpw, rem = e % cpw;
+    const int i = rem / nc, p = rem % nc;
+    const int j = (w >> 1) * nc + p;
+    return ((j * 2 + pc) * 2 + (w & 1)) * 4 + i;
+}
+
+// 2^e as a float, e in [-149, 127]
+__device__ __forceinline__ float exp2i(int e) {
+    if (e >= -126) return __uint_as_float(static_cast<uint32_t>(e + 127) << 23);
+    return __uint_as_float(1u << (e + 149));
+}
+
+// One warp converts one group of GS activations (16-bit, src) into its int8
+// pieces (dst, 2 * GS bytes) and (sum of x in fp32, 2^-(S + 8 - BITS)) -> xs
+// (the factor also undoes the class fold).  Fixed-order sums: the result
+// repeats bit for bit.
+template <typename TA, int BITS, int GS>
+__device__ __forceinline__ void convert_group(const uint16_t *src, uint8_t *dst, float2 *xs, bool from_global) {
+    constexpr int PER = GS / 32;  // elements per lane
+    const int lane = threadIdx.x & 31;
+    float v[PER];
+    float amax = 0.0f, sum = 0.0f;
+#pragma unroll
+    for (int q = 0; q < PER; ++q) {
+        const int e = lane + 32 * q;
+        const uint16_t raw = from_global ? __ldcg(reinterpret_cast<const unsigned short *>(src + e)) : src[e];
+        v[q] = Act<TA>::to_f(raw);
+        amax = fmaxf(amax, fabsf(v[q]));
+        sum += v[q];
+    }
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    }
+    int S = 0;
+    if (amax > 0.0f) {
+        const int E = static_cast<int>((__float_as_uint(amax) >> 23) & 0xffu) - 127;  // amax in [2^E, 2^(E+1))
+        S = min(13 - E, 126);
+    }
+    const float scale = __uint_as_float(static_cast<uint32_t>(S + 127) << 23);
+#pragma unroll
+    for (int q = 0; q < PER; ++q) {
+        const int e = lane + 32 * q;
+        const int xi = __float2int_rn(v[q] * scale);  // |xi| <= 2^14
+        const int hi = (xi + 128) >> 8;                // [-64, 64]
+        const int lo = xi - (hi << 8);                 // [-128, 127]
+        dst[piece_offset<BITS>(e, 0)] = static_cast<uint8_t>(hi & 0xff);
+        dst[piece_offset<BITS>(e, 1)] = static_cast<uint8_t>(lo & 0xff);
+    }
+    if (lane == 0) *xs = make_float2(sum, exp2i(-(S + 8 - BITS)));
+}
+
+// The same for a consumer whose bit width and group size are known at run time.
+template <typename TA>
+__device__ __forceinline__ void convert_group_rt(int bits, int gs, const uint16_t *src, uint8_t *dst, float2 *xs,
+                                                 bool from_global) {
+#define LMOE_CG(B, Gs) \
+    if (bits == B && gs == Gs) return convert_group<TA, B, Gs>(src, dst, xs, from_global);
+    LMOE_CG(2, 32)
+    LMOE_CG(2, 64)
+    LMOE_CG(2, 128)
+    LMOE_CG(4, 32)
+    LMOE_CG(4, 64)
+    LMOE_CG(4, 128)
+    LMOE_CG(8, 32)
+    LMOE_CG(8, 64)
+    LMOE_CG(8, 128)
+#undef LMOE_CG
+}
+
+// ------------------------------------------------------------ single-token layer (lmoe_vec.cu)
+// Decode of one token over the stream format on the integer tensor pipe, in
+// one persistent launch: gate/up + SwiGLU, then down + combine.  Every chunk
+// of the dispatch holds one route.  Work items are (sub-unit, K chunk) pairs
+// dealt out in contiguous ranges to all warps of the grid; a sub-unit's
+// partial sums meet in global scratch and the last share to arrive runs its
+// epilogue.  The down projection's weights stream in while gate/up still
+// computes; a grid-wide counter of converted h groups (bounded wait) starts
+// the down products.
+constexpr int kVecWarps = 8;      // warps per block, each with its own copy ring
+constexpr int kVecMaxStages = 8;  // ring sub-slots per warp
+struct VecPhase {                  // geometry of one projection's stream format
+    int32_t nck, pairs, RB, fm_c, tS, tB, TB, ngroups;
+    int64_t blk;
+};
+struct VecArgs {
+    QView q0, q1, q2;  // stream-format tiles of gate, up and down
+    // the natural activation row [K] (the layer's single token), and its int8
+    // pieces [groups][2 gs] and (sum, factor) per group: written by the
+    // router (x_ready) or converted here from x
+    const uint16_t *x;
+    const uint8_t *xq;
+    const float2 *xs;
+    int32_t x_ready;
+    // dispatch of one token: chunk i holds the single route sorted_routes[i]
+    const Chunk *chunks;
+    const int32_t *n_chunks;
+    const int32_t *sorted_routes;
+    int32_t n_slots, max_chunks;
+    int32_t routes;       // route rows R (top_k, + 1 with the shared expert)
+    int32_t shared_base;  // > 0: route shared_base is the shared expert's (reads x)
+    // single token: routing selected from the router's (score, biased score)
+    // inside the kernel (block_topk); tk_scores == nullptr: chunks from memory
+    const float2 *tk_scores;
+    int32_t tk_E, tk_k, tk_norm;
+    float tk_scaling;
+    const int32_t *tk_expert_slot;
+    int32_t *tk_idx, *tk_idx_user, *tk_sorted, *tk_nchunks;
+    float *tk_w, *tk_w_user;
+    Chunk *tk_chunks;
+    // h's int8 pieces [R][groups][2 gs] and (sum, factor) per 32-row
+    // segment [R][inter / 32]
+    uint8_t *hq;
+    float2 *hs;
+    float limit;
+    int32_t swiglu_mode;
+    // route weights (nullptr: unit weights), residual (or nullptr), combined
+    // output row (or nullptr) and per-route rows T(T(y) * T(w)) [R][hidden]
+    // of the computed routes (or nullptr)
+    const float *route_w;
+    int32_t top_k;
+    const uint16_t *residual;
+    uint16_t *out;
+    uint16_t *yw;
+    uint32_t *hready;  // gate/up units finished (zero at the start of the call)
+    int32_t *err;
+};
+struct VecCfg {
+    VecPhase ga, dn;  // gate/up (two tiles of gate, two of up per stage) and down
+    int32_t routes;   // h rows resident in the down phase
+    int32_t sub, nq, qa, qb, warps;  // ring: nq sub-slots of sub bytes per warp; qa / qb per item
+    int32_t off_bar, off_flag, off_xbar, off_zero, off_rch, off_tk, off_xq, off_xs, off_hq, off_hs, off_pa, off_pb,
+        off_ring, smem;
+    int32_t grid;
+};
+// geometry check and shared-memory plan; false when the kernel cannot run it
+bool vec_layer_config(int hidden, int inter, int bits_g, int gs_g, int bits_d, int gs_d, int routes, VecCfg *out);
+cudaError_t launch_vec_layer(int act_f16, int bits_g, int bits_d, int gs, const VecArgs &a, const VecCfg &c,
+                             cudaStream_t st);
+
 
 // host-side launchers (lmoe_route.cu, lmoe_gemv.cu)
 cudaError_t launch_router(const RouterArgs &a, int ksplit, cudaStream_t st);

@@ -720,6 +720,15 @@ __global__ void __launch_bounds__(256) router_kernel(RouterArgs a) {
         }
     }
 
+    // ---- single token: int8 pieces of x for the single-token layer kernel,
+    // one group per warp over the grid
+    if (a.xq && tbeg == 0) {
+        const int ngr = a.H / a.pgs, nw = gridDim.x * (blockDim.x >> 5);
+        for (int gi = blockIdx.x * (blockDim.x >> 5) + warp; gi < ngr; gi += nw)
+            convert_group_rt<TA>(a.pbits, a.pgs, a.x + (size_t)gi * a.pgs, a.xq + (size_t)gi * (2 * a.pgs), a.xs + gi,
+                                 false);
+    }
+
     // ---- logits
     for (int ts = tbeg; ts < tend; ts += 8) {
         const int nt = min(8, tend - ts);

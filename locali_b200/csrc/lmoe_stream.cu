@@ -87,126 +87,6 @@ struct UnitMeta {
     float w;
 };
 
-// Single-token routing held in registers (lane j < k: the j-th winner's
-// expert id, weight, arena slot, and its rank among the winners' ids, which
-// is its chunk in the dispatch; other lanes hold pos = -1).
-struct TopkRegs {
-    int e, pos, slot;
-    float w;
-};
-
-// Top-k of a single token by one warp from the router's (score, biased
-// score) (arena.py:501-506): selection on the biased score, ties to the
-// lower id; each lane keeps its best candidate and only the winner of a round
-// rescans.  Weights: raw scores normalised by their fp32 sum in selection
-// order + 1e-20, times the routed scaling.  The dispatch of the k distinct
-// experts: chunk i = the route of the i-th smallest expert id.  The same
-// winners, order and weights as the router's own finisher.  Every warp of
-// the launch computes it; warp 0 of block 0 also writes the routing and the
-// dispatch to memory for the down kernel and the caller.
-__device__ TopkRegs fused_topk(const GemvArgs &a) {
-    const int lane = threadIdx.x & 31;
-    const int E = a.tk_E, k = a.tk_k;
-    float bs[16], sc[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-        const int e = lane + 32 * i;
-        bs[i] = -INFINITY;
-        sc[i] = 0.0f;
-        if (e < E) {
-            const float2 v = __ldcg(a.tk_scores + e);
-            sc[i] = v.x;
-            bs[i] = v.y;
-        }
-    }
-    float lbv = -INFINITY, lbs = 0.0f;
-    int lbe = 0x7fffffff;
-#pragma unroll
-    for (int i = 0; i < 16; ++i)
-        if (bs[i] > lbv) {
-            lbv = bs[i];
-            lbe = lane + 32 * i;
-            lbs = sc[i];
-        }
-    int my_e = -1;
-    float my_s = 0.0f;
-#pragma unroll 1
-    for (int j = 0; j < k; ++j) {
-        float bv = lbv;
-        int be = lbe;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(LMOE_FULL, bv, o);
-            const int oe = __shfl_xor_sync(LMOE_FULL, be, o);
-            if (ov > bv || (ov == bv && oe < be)) {
-                bv = ov;
-                be = oe;
-            }
-        }
-        const float ws = __shfl_sync(LMOE_FULL, lbs, be & 31);
-        if (lane == j) {
-            my_e = be;
-            my_s = ws;
-        }
-        if (lbe == be) {  // the winner drops it and rescans
-            lbv = -INFINITY;
-            lbe = 0x7fffffff;
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                if (lane + 32 * i == be) bs[i] = -INFINITY;
-                if (bs[i] > lbv) {
-                    lbv = bs[i];
-                    lbe = lane + 32 * i;
-                    lbs = sc[i];
-                }
-            }
-        }
-    }
-    float ssum = 0.0f;  // fp32, in selection order
-    int pos = 0;        // rank of this lane's expert id among the winners
-#pragma unroll 1
-    for (int j = 0; j < k; ++j) {
-        ssum += __shfl_sync(LMOE_FULL, my_s, j);
-        pos += __shfl_sync(LMOE_FULL, my_e, j) < my_e;
-    }
-    TopkRegs r;
-    r.e = my_e;
-    r.pos = -1;
-    r.slot = 0;
-    r.w = 0.0f;
-    if (lane >= k) return r;
-    float wv = a.tk_norm ? my_s / (ssum + 1e-20f) : my_s;
-    wv *= a.tk_scaling;
-    int slot = 0;
-    if (my_e < 0 || my_e >= E) {
-        set_error(a.err, -3);
-    } else {
-        slot = a.tk_expert_slot ? a.tk_expert_slot[my_e] : my_e;
-        if (slot < 0 || slot >= a.n_slots) {
-            set_error(a.err, -3);
-            slot = 0;
-        }
-    }
-    r.pos = pos;
-    r.slot = slot;
-    r.w = wv;
-    if (blockIdx.x == 0 && threadIdx.x < 32) {
-        a.tk_idx[lane] = my_e;
-        a.tk_w[lane] = wv;
-        if (a.tk_idx_user) a.tk_idx_user[lane] = my_e;
-        if (a.tk_w_user) a.tk_w_user[lane] = wv;
-        a.tk_sorted[pos] = lane;
-        Chunk ch;
-        ch.slot = slot;
-        ch.route_start = pos;
-        ch.ntok = 1;
-        ch.expert = my_e;
-        a.tk_chunks[pos] = ch;
-        if (lane == 0) *a.tk_nchunks = k;
-    }
-    return r;
-}
-
 // Named barrier of one warp group.  The warp reconverges first and the
 // barrier is the non-aligned form, so it stays defined even where the
 // compiler has not reconverged the warp after a lane-dependent loop.
@@ -280,7 +160,7 @@ __global__ void __launch_bounds__(kStrMaxWarps * 32, 1) stream_kernel(const Gemv
     int nch;
     if (fused) {
         // single token: the routing is selected here (see fused_topk)
-        tk = fused_topk(a);
+        tk = fused_topk(a, true);
         nch = a.tk_k;
     } else {
         nch = *a.n_chunks;
