@@ -408,8 +408,12 @@ def measure_decode(cfg, kerns, K, W, dev, world, rank, kernel_steps, path):
     t_gu = [ev[s][1].elapsed_time(ev[s][2]) for s in range(nk)]
     t_down = [ev[s][2].elapsed_time(ev[s][3]) for s in range(nk)]
     distinct = [len(torch.unique(idx_buf[s]).tolist()) for s in range(nk)]
-    gu_bytes = sum(d * cfg.gateup_bytes() for d in distinct) / nk
     gu_ms = sum(t_gu) / nk
+    # one token over the pre-tiled copy: gate/up and down run in one kernel
+    # (the event after "gate/up" follows it), so its bytes are all three
+    # projections'
+    fused = T == 1 and path != "prefill" and kerns[0].experts.gate.tiles is not None
+    gu_bytes = sum(d * (cfg.expert_bytes() if fused else cfg.gateup_bytes()) for d in distinct) / nk
     achieved = gu_bytes / (gu_ms / 1e3) / 1e9
     peak, peak_kind = measured_peak()
     layer_bytes = (sum(d * cfg.expert_bytes() for d in distinct) / nk + cfg.router_bytes()
@@ -417,11 +421,16 @@ def measure_decode(cfg, kerns, K, W, dev, world, rank, kernel_steps, path):
     layer_ms = ms / K
     if path == "auto":
         path = "prefill" if _lib.auto_takes_prefill(T, cfg.top_k, cfg.n_experts) else "decode"
-    gu_kernel = ("gemv_kernel<bf16, gate/up>" if path == "decode"
-                 else f"pf_gemm_kernel<bf16, {cfg.bits_gate}, {cfg.group_size}, gate/up> (tcgen05)")
+    if fused:
+        gu_kernel = (f"vec_layer_kernel<bf16, {cfg.bits_gate}, {cfg.bits_down}, {cfg.group_size}> "
+                     "(single-token gate/up + down + combine, integer mma.sync)")
+    elif path == "decode":
+        gu_kernel = "stream_kernel<bf16, gate/up> (decode GEMV)"
+    else:
+        gu_kernel = f"pf_gemm_kernel<bf16, {cfg.bits_gate}, {cfg.group_size}, gate/up> (tcgen05)"
     # kernels of one step: router (+ logits on tensor cores and top-k for
     # T > 64), gate/up, down+combine (prefill: panel, dispatch, 2 GEMMs, combine)
-    per_step = 3 if path == "decode" and T <= 64 else (5 if path == "decode" else 7)
+    per_step = 2 if fused else (3 if path == "decode" and T <= 64 else (5 if path == "decode" else 7))
     return {
         "value": value, "ms": ms, "ms_per_step": layer_ms, "clocks": clocks, "path": path,
         "distinct_experts_mean": sum(distinct) / nk,
@@ -430,8 +439,10 @@ def measure_decode(cfg, kerns, K, W, dev, world, rank, kernel_steps, path):
                      "algorithmic_bytes_per_launch": gu_bytes},
         "layer_roofline": {"bytes_per_step": layer_bytes, "achieved_gbs": layer_bytes / (layer_ms / 1e3) / 1e9,
                            "frac": layer_bytes / (layer_ms / 1e3) / 1e9 / peak},
-        "kernels_us": {"router_dispatch": 1e3 * sum(t_router) / nk, "gateup_swiglu": 1e3 * gu_ms,
-                       "down_combine": 1e3 * sum(t_down) / nk},
+        "kernels_us": ({"router_dispatch": 1e3 * sum(t_router) / nk, "experts_fused": 1e3 * gu_ms,
+                        "after_experts": 1e3 * sum(t_down) / nk} if fused else
+                       {"router_dispatch": 1e3 * sum(t_router) / nk, "gateup_swiglu": 1e3 * gu_ms,
+                        "down_combine": 1e3 * sum(t_down) / nk}),
         "gpu_launches": per_step * K,
     }
 

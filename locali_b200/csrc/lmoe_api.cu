@@ -123,7 +123,7 @@ VecSizes vec_sizes(const lmoe_layer *l, int T, int R) {
     VecCfg c;
     if (T != 1 || !vec_geometry(l, R, &c)) return vs;
     const lmoe_experts &ex = l->experts;
-    vs.cnt_words = 1;
+    vs.cnt_words = (size_t)R * c.dn.nck;  // finished gate/up units per (route, down K chunk)
     vs.hq_bytes = al((size_t)R * ex.inter * 2) + al((size_t)ex.hidden * 2);
     vs.hs_bytes = al((size_t)R * (ex.inter / 32) * 8 + 16) + al((size_t)(ex.hidden / ex.gate.group_size) * 8 + 16);
     return vs;

@@ -597,15 +597,15 @@ struct VecArgs {
     const uint16_t *residual;
     uint16_t *out;
     uint16_t *yw;
-    uint32_t *hready;  // gate/up units finished (zero at the start of the call)
+    uint32_t *hready;  // [R][down K chunks]: gate/up units finished (zero at the start of the call)
     int32_t *err;
 };
 struct VecCfg {
     VecPhase ga, dn;  // gate/up (two tiles of gate, two of up per stage) and down
     int32_t routes;   // h rows resident in the down phase
     int32_t sub, nq, qa, qb, warps;  // ring: nq sub-slots of sub bytes per warp; qa / qb per item
-    int32_t off_bar, off_flag, off_xbar, off_zero, off_rch, off_tk, off_xq, off_xs, off_hq, off_hs, off_pa, off_pb,
-        off_ring, smem;
+    int32_t off_bar, off_flag, off_xbar, off_zero, off_rch, off_tk, off_xq, off_xs, off_hq, off_pa, off_pb, off_ring,
+        smem;
     int32_t grid;
 };
 // geometry check and shared-memory plan; false when the kernel cannot run it

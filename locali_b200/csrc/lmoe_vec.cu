@@ -44,8 +44,7 @@
 // Between the phases each block waits (bounded) until every unit is done,
 // then bulk-copies the h pieces.  The kernel needs all its blocks resident
 // (one per SM; the grid is the SM count).  Routing: a single token's top-k
-// runs block-cooperatively (each warp ranks 32 experts, every warp merges
-// the eight short lists) from the router's scores, or the chunk table is
+// runs in one warp (fused_topk) from the router's scores, or the chunk table is
 // read; x's int8 pieces come from the router (or are converted here).
 // The sums run in a fixed order, so results repeat bit for bit.
 //
@@ -201,131 +200,13 @@ __device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t *p) {
     return v;
 }
 
-// One entry of the block top-k's per-warp lists.
-struct TkEntry {
-    uint32_t key;
-    int32_t id, slot;
-    float score;
+// The routing of one lane (chunk pos, arena slot, weight), shared by the
+// warp that ran the top-k with the rest of the block.
+struct TkShare {
+    int32_t pos, slot;
+    float w;
+    int32_t pad;
 };
-
-// Single-token top-k of the block (arena.py:501-506), the same winners,
-// order and weights as fused_topk: warp w ranks experts w*32 + lane (+256)
-// to its own top-k list in shared memory (redux max of the keys, redux min
-// of the ids reaching it), then every warp merges the eight lists the same
-// way.  Lane j < k returns the j-th winner; block 0's warp 0 writes the
-// routing and the dispatch.
-template <class A>
-__device__ __forceinline__ TopkRegs block_topk(const A &a, TkEntry *lists) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int E = a.tk_E, k = a.tk_k;
-    if (warp == 0 && lane < 16) lists[8 * 16 + lane] = TkEntry{0u, 0x7fffffff, 0, 0.0f};
-    {
-        uint32_t key[2];
-        float sc[2];
-        int sl[2];
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-            const int e = warp * 32 + lane + 256 * i;
-            key[i] = 0u;
-            sc[i] = 0.0f;
-            sl[i] = e;
-            if (e < E) {
-                const float2 v = __ldcg(a.tk_scores + e);
-                sc[i] = v.x;
-                key[i] = topk_key(v.y);
-                if (a.tk_expert_slot) sl[i] = __ldg(a.tk_expert_slot + e);
-            }
-        }
-        // lane best: larger key, then lower id (i = 0 has the lower id)
-        for (int j = 0; j < k; ++j) {
-            const bool b1 = key[1] > key[0];
-            const uint32_t lk = b1 ? key[1] : key[0];
-            const int lbe = lk ? warp * 32 + lane + (b1 ? 256 : 0) : 0x7fffffff;
-            const uint32_t mk = __reduce_max_sync(0xffffffffu, lk);
-            const int be = static_cast<int>(__reduce_min_sync(0xffffffffu, lk == mk ? static_cast<uint32_t>(lbe) : 0xffffffffu));
-            if (mk == 0u) {
-                if (lane == 0) lists[warp * 16 + j] = TkEntry{0u, 0x7fffffff, 0, 0.0f};
-                continue;
-            }
-            if (lbe == be) {
-                lists[warp * 16 + j] = TkEntry{mk, be, b1 ? sl[1] : sl[0], b1 ? sc[1] : sc[0]};
-                if (b1)
-                    key[1] = 0u;
-                else
-                    key[0] = 0u;
-            }
-        }
-    }
-    __syncthreads();
-    // merge in one pass: lane j < k of warp w takes entry (w, j) and counts
-    // the entries of all lists that beat it (larger key, or equal key and
-    // lower id); a count below k is its place in the selection order
-    TkEntry *sel = lists + 8 * 16;  // [k] winners in selection order
-    if (lane < k) {
-        const TkEntry me = lists[warp * 16 + lane];
-        if (me.key != 0u) {
-            int rank = 0;
-            for (int w2 = 0; w2 < 8; ++w2)
-#pragma unroll 4
-                for (int j2 = 0; j2 < k; ++j2) {
-                    const TkEntry o = lists[w2 * 16 + j2];
-                    rank += (o.key > me.key) || (o.key == me.key && o.key != 0u && o.id < me.id);
-                }
-            if (rank < k) sel[rank] = me;
-        }
-    }
-    __syncthreads();
-    int my_e = -1, my_slot = 0;
-    float my_s = 0.0f;
-    if (lane < k) {
-        const TkEntry w = sel[lane];
-        my_e = w.id;
-        my_s = w.score;
-        my_slot = w.slot;
-    }
-    float ssum = 0.0f;  // fp32, in selection order
-    int pos = 0;        // rank of this lane's expert id among the winners
-    for (int j = 0; j < k; ++j) {
-        ssum += __shfl_sync(0xffffffffu, my_s, j);
-        pos += __shfl_sync(0xffffffffu, my_e, j) < my_e;
-    }
-    TopkRegs r;
-    r.e = my_e;
-    r.pos = -1;
-    r.slot = 0;
-    r.w = 0.0f;
-    if (lane >= k) return r;
-    float wv = a.tk_norm ? my_s / (ssum + 1e-20f) : my_s;
-    wv *= a.tk_scaling;
-    int slot = 0;
-    if (my_e < 0 || my_e >= E) {
-        set_error(a.err, -3);
-    } else {
-        slot = my_slot;
-        if (slot < 0 || slot >= a.n_slots) {
-            set_error(a.err, -3);
-            slot = 0;
-        }
-    }
-    r.pos = pos;
-    r.slot = slot;
-    r.w = wv;
-    if (blockIdx.x == 0 && threadIdx.x < 32) {
-        a.tk_idx[lane] = my_e;
-        a.tk_w[lane] = wv;
-        if (a.tk_idx_user) a.tk_idx_user[lane] = my_e;
-        if (a.tk_w_user) a.tk_w_user[lane] = wv;
-        a.tk_sorted[pos] = lane;
-        Chunk ch;
-        ch.slot = slot;
-        ch.route_start = pos;
-        ch.ntok = 1;
-        ch.expert = my_e;
-        a.tk_chunks[pos] = ch;
-        if (lane == 0) *a.tk_nchunks = k;
-    }
-    return r;
-}
 
 template <typename TA, int BG, int BD, int GS>
 __global__ void __launch_bounds__(kVecWarps * 32, 1) vec_layer_kernel(const VecArgs a, const VecCfg c) {
@@ -338,11 +219,10 @@ __global__ void __launch_bounds__(kVecWarps * 32, 1) vec_layer_kernel(const VecA
     int &s_abort = *reinterpret_cast<int *>(smem + c.off_flag);
     uint8_t *ring = smem + c.off_ring + (size_t)warp * c.nq * c.sub;
     uint64_t *bar = reinterpret_cast<uint64_t *>(smem + c.off_bar) + warp * kVecMaxStages;
-    uint64_t *xbar = reinterpret_cast<uint64_t *>(smem + c.off_xbar);  // [0] x pieces, [1] h pieces
+    uint64_t *xbar = reinterpret_cast<uint64_t *>(smem + c.off_xbar);  // x pieces
     uint8_t *xq = smem + c.off_xq;                               // x pieces [groups][2 GS]
     float2 *xs = reinterpret_cast<float2 *>(smem + c.off_xs);  // [groups]
-    uint8_t *hq = smem + c.off_hq;                               // h pieces [R][groups][2 GS]
-    float2 *hs = reinterpret_cast<float2 *>(smem + c.off_hs);  // [R][segments]
+    uint8_t *hq = smem + c.off_hq;  // per-warp scratch: one K chunk of h's pieces and factors
     const uint8_t *zero = smem + c.off_zero;                     // 2 GS zero bytes (B of idle lanes)
     float *pa = reinterpret_cast<float *>(smem + c.off_pa);      // [unit j][K chunk][64]
     float *pb = reinterpret_cast<float *>(smem + c.off_pb);      // [pair j][chunk][K chunk][32]
@@ -353,15 +233,12 @@ __global__ void __launch_bounds__(kVecWarps * 32, 1) vec_layer_kernel(const VecA
 
     if (lane == 0) {
         for (int q = 0; q < nq; ++q) mbar_init(&bar[q], 1);
-        if (warp == 0) {
-            mbar_init(&xbar[0], 1);
-            mbar_init(&xbar[1], 1);
-        }
+        if (warp == 0) mbar_init(&xbar[0], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     for (int i = threadIdx.x; i < GS / 8; i += blockDim.x)
         reinterpret_cast<uint4 *>(smem + c.off_zero)[i] = make_uint4(0u, 0u, 0u, 0u);
-    for (int i = threadIdx.x; i < R; i += blockDim.x) route_ch[i] = -1;
+    for (int i = threadIdx.x; i < 32; i += blockDim.x) route_ch[i] = -1;
     if (threadIdx.x == 0) s_abort = 0;
     __syncthreads();
 
@@ -379,7 +256,18 @@ __global__ void __launch_bounds__(kVecWarps * 32, 1) vec_layer_kernel(const VecA
     int nch, cslot = 0, croute = 0;  // lane ch holds chunk ch's (slot, route, weight)
     float cw = 1.0f;
     if (a.tk_scores) {
-        const TopkRegs tk = block_topk(a, reinterpret_cast<TkEntry *>(smem + c.off_tk));
+        // warp 0 selects (fused_topk; block 0's also writes the routing and
+        // the dispatch), the block reads its result from shared memory
+        TkShare *tks = reinterpret_cast<TkShare *>(smem + c.off_tk);
+        if (warp == 0) {
+            const TopkRegs r = fused_topk(a, true);
+            tks[lane] = TkShare{r.pos, r.slot, r.w, 0};
+        }
+        __syncthreads();
+        TopkRegs tk;
+        tk.pos = tks[lane].pos;
+        tk.slot = tks[lane].slot;
+        tk.w = tks[lane].w;
         nch = a.tk_k;
         for (int j = 0; j < nch; ++j) {
             const int pj = __shfl_sync(kFull, tk.pos, j);
@@ -424,38 +312,77 @@ __global__ void __launch_bounds__(kVecWarps * 32, 1) vec_layer_kernel(const VecA
     const int myB = nitB > warp ? (nitB - warp + W - 1) / W : 0;
     const int total = myA + myB;
     const uint64_t pol = evict_first_policy();
-    // this warp's n-th item (gate/up items warp, warp + W, ..., then down
-    // items) into ring sub-slots from pos: c.qa sub-slots for a gate/up item,
-    // c.qb for a down item
-    auto issue = [&](int pos, int n, bool reuse) {
-        int ch, p, cc;
-        bool down = n >= myA;
-        if (!down) {
-            const int i = warp + n * W, j = i / PA.nck;
-            cc = i - j * PA.nck;
-            const int u = b + j * G;
-            ch = u / PA.pairs;
-            p = u - ch * PA.pairs;
+    // The gate/up units of this block, one per lane: lane j holds unit
+    // b + j * G as (chunk, pair).
+    int uch = 0, upr = 0;
+    if (lane < nuA) {
+        const int u = b + lane * G;
+        uch = u / PA.pairs;
+        upr = u - uch * PA.pairs;
+    }
+    // Item cursor over this warp's items -- gate/up items warp, warp + W, ...
+    // of the block's list (unit j = i / nck, K chunk cc), then its down items
+    // (pair j = i / perB, chunk ch, K chunk cc) -- advanced without division.
+    struct Cur {
+        int n, j, ch, cc;
+    };
+    auto cur_start = [&](Cur &q) {
+        q.n = 0;
+        if (myA > 0) {
+            q.j = warp / PA.nck;
+            q.cc = warp - q.j * PA.nck;
+            q.ch = 0;
         } else {
-            const int i = warp + (n - myA) * W, j = i / perB, r2 = i - j * perB;
-            ch = r2 / PB.nck;
-            cc = r2 - ch * PB.nck;
-            p = b + j * G;
+            q.j = warp / perB;
+            const int r2 = warp - q.j * perB;
+            q.ch = r2 / PB.nck;
+            q.cc = r2 - q.ch * PB.nck;
         }
+    };
+    auto cur_next = [&](Cur &q) {
+        ++q.n;
+        if (q.n < myA) {
+            q.cc += W;
+            while (q.cc >= PA.nck) {
+                q.cc -= PA.nck;
+                ++q.j;
+            }
+        } else if (q.n == myA) {  // first down item
+            q.j = warp / perB;
+            const int r2 = warp - q.j * perB;
+            q.ch = r2 / PB.nck;
+            q.cc = r2 - q.ch * PB.nck;
+        } else {
+            q.cc += W;
+            while (q.cc >= PB.nck) {
+                q.cc -= PB.nck;
+                if (++q.ch == nch) {
+                    q.ch = 0;
+                    ++q.j;
+                }
+            }
+        }
+    };
+    // the item at cursor q into ring sub-slots from pos: c.qa sub-slots for a
+    // gate/up item, c.qb for a down item
+    auto issue = [&](int pos, const Cur &q, bool reuse) {
+        const bool down = q.n >= myA;
+        const int ch = down ? q.ch : __shfl_sync(kFull, uch, q.j);
+        const int p = down ? b + q.j * G : __shfl_sync(kFull, upr, q.j);
         const int slot = __shfl_sync(kFull, cslot, ch);
         if (lane == 0) {
             uint8_t *dst = ring + (size_t)pos * c.sub;
             if (reuse) fence_proxy_async();  // the ring's earlier contents were read by generic loads
             if (!down) {
                 mbar_expect_tx(&bar[pos], static_cast<uint32_t>(2 * PA.blk));
-                const size_t off = ((size_t)p * PA.nck + cc) * (size_t)PA.blk;
+                const size_t off = ((size_t)p * PA.nck + q.cc) * (size_t)PA.blk;
                 bulk_g2s_hint(dst, a.q0.tiles + (size_t)slot * a.q0.tile_slot_stride + off,
                               static_cast<uint32_t>(PA.blk), &bar[pos], pol);
                 bulk_g2s_hint(dst + PA.blk, a.q1.tiles + (size_t)slot * a.q1.tile_slot_stride + off,
                               static_cast<uint32_t>(PA.blk), &bar[pos], pol);
             } else {
                 mbar_expect_tx(&bar[pos], static_cast<uint32_t>(PB.blk));
-                const size_t off = ((size_t)p * PB.nck + cc) * (size_t)PB.blk;
+                const size_t off = ((size_t)p * PB.nck + q.cc) * (size_t)PB.blk;
                 bulk_g2s_hint(dst, a.q2.tiles + (size_t)slot * a.q2.tile_slot_stride + off,
                               static_cast<uint32_t>(PB.blk), &bar[pos], pol);
             }
@@ -465,10 +392,13 @@ __global__ void __launch_bounds__(kVecWarps * 32, 1) vec_layer_kernel(const VecA
     int issued = 0, consumed = 0, ip = 0, cp = 0, used = 0;
     uint32_t par = 0;
     auto qof = [&](int n) { return n < myA ? c.qa : c.qb; };
+    Cur ci;  // issue cursor
+    cur_start(ci);
     auto try_issue = [&]() {
         while (issued < total && used + qof(issued) <= nq) {
             const int q = qof(issued);
-            issue(ip, issued, consumed > 0);
+            issue(ip, ci, consumed > 0);
+            cur_next(ci);
             ip += q;
             if (ip == nq) ip = 0;
             used += q;
@@ -501,25 +431,6 @@ __global__ void __launch_bounds__(kVecWarps * 32, 1) vec_layer_kernel(const VecA
             ++consumed;
         }
     };
-    // thread 0 waits (bounded) until *ctr reaches want; false: gave up
-    auto grid_wait = [&](const uint32_t *ctr, uint32_t want) {
-        if (threadIdx.x == 0 && !s_abort && ld_acquire_u32(ctr) < want) {
-            const long long t0 = clock64();
-            uint32_t sl = 32;
-            while (ld_acquire_u32(ctr) < want) {
-                __nanosleep(sl);
-                if (sl < 256) sl <<= 1;
-                if (clock64() - t0 > kWaitLimitCycles) {
-                    set_error(a.err, -4);
-                    s_abort = 1;
-                    break;
-                }
-            }
-        }
-        __syncthreads();
-        return s_abort == 0;
-    };
-
     // ---- x's pieces: from the router (bulk copy above) or converted here
     if (a.x_ready) {
         if (!mbar_wait(&xbar[0], 0)) {
@@ -533,8 +444,48 @@ __global__ void __launch_bounds__(kVecWarps * 32, 1) vec_layer_kernel(const VecA
     __syncthreads();  // x pieces and the route map are complete
 
     // ============================== gate/up items
-    for (int n = 0; n < myA && !aborted; ++n) {
-        const int i = warp + n * W, j = i / PA.nck, cc = i - j * PA.nck;
+    // A unit of this block, once all its items are done: K chunks in order,
+    // SwiGLU, and h's int8 pieces (one scale per 32-row segment) into global
+    // scratch, then a release increment of the grid-wide count of finished
+    // units.
+    const int ml = lane >> 4, rl = lane & 15;  // lane = row of the 32-row pair
+    auto finish_unit = [&](int j) {
+        const int ch = __shfl_sync(kFull, uch, j), p = __shfl_sync(kFull, upr, j);
+        const int route = __shfl_sync(kFull, croute, ch);
+        const float *pp = pa + (size_t)j * PA.nck * 64 + ml * 16 + rl;
+        float ga = 0.0f, ua = 0.0f;
+        for (int cc = 0; cc < PA.nck; ++cc) {
+            ga += pp[cc * 64];
+            ua += pp[cc * 64 + 32];
+        }
+        const float hv = swiglu_h<TA>(ga, ua, a.limit, a.swiglu_mode);
+        float amax = fabsf(hv), sum = hv;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, o));
+            sum += __shfl_xor_sync(kFull, sum, o);
+        }
+        int S = 0;
+        if (amax > 0.0f) S = min(13 - (static_cast<int>((__float_as_uint(amax) >> 23) & 0xffu) - 127), 126);
+        const int xi = __float2int_rn(hv * __uint_as_float(static_cast<uint32_t>(S + 127) << 23));
+        const int hi = (xi + 128) >> 8, lo = xi - (hi << 8);
+        const int ngd = PB.ngroups, gd = (32 * p) / GS, e = (32 * p) % GS + lane;
+        uint8_t *gq = a.hq + ((size_t)route * ngd + gd) * (2 * GS);
+        gq[piece_offset<BD>(e, 0)] = static_cast<uint8_t>(hi & 0xff);
+        gq[piece_offset<BD>(e, 1)] = static_cast<uint8_t>(lo & 0xff);
+        if (lane == 0) a.hs[(size_t)route * nseg + p] = make_float2(sum, exp2i(-(S + 8 - BD)));
+        __syncwarp();
+        // cumulative release: the warp's stores above precede the count of
+        // finished units of h's K chunk (route, 32 p / CK) of the down GEMV
+        if (lane == 0)
+            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.hready + (size_t)route * PB.nck +
+                                                                         (32 * p) / (8 * GS))
+                         : "memory");
+    };
+    Cur cu;  // consume cursor
+    cur_start(cu);
+    for (int n = 0; n < myA && !aborted; ++n, cur_next(cu)) {
+        const int j = cu.j, cc = cu.cc;
         if (!wait_next()) {
             set_error(a.err, -4);
             aborted = true;
@@ -563,77 +514,75 @@ __global__ void __launch_bounds__(kVecWarps * 32, 1) vec_layer_kernel(const VecA
     }
     if (aborted) s_abort = 1;
     __syncthreads();
+    if (!s_abort)
+        for (int j = warp; j < nuA; j += W) finish_unit(j);
 
-    // ---- gate/up units of this block: K chunks in order, SwiGLU, h's int8
-    // pieces (one scale per 32-row segment) into global scratch
-    const int ml = lane >> 4, rl = lane & 15;  // lane = row of the 32-row pair
-    if (!s_abort) {
-        for (int j = warp; j < nuA; j += W) {
-            const int u = b + j * G, ch = u / PA.pairs, p = u - ch * PA.pairs;
-            const int route = __shfl_sync(kFull, croute, ch);
-            const float *pp = pa + (size_t)j * PA.nck * 64 + ml * 16 + rl;
-            float ga = 0.0f, ua = 0.0f;
-            for (int cc = 0; cc < PA.nck; ++cc) {
-                ga += pp[cc * 64];
-                ua += pp[cc * 64 + 32];
-            }
-            const float hv = swiglu_h<TA>(ga, ua, a.limit, a.swiglu_mode);
-            float amax = fabsf(hv), sum = hv;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, o));
-                sum += __shfl_xor_sync(kFull, sum, o);
-            }
-            int S = 0;
-            if (amax > 0.0f) S = min(13 - (static_cast<int>((__float_as_uint(amax) >> 23) & 0xffu) - 127), 126);
-            const int xi = __float2int_rn(hv * __uint_as_float(static_cast<uint32_t>(S + 127) << 23));
-            const int hi = (xi + 128) >> 8, lo = xi - (hi << 8);
-            const int ngd = PB.ngroups, gd = (32 * p) / GS, e = (32 * p) % GS + lane;
-            uint8_t *gq = a.hq + ((size_t)route * ngd + gd) * (2 * GS);
-            gq[piece_offset<BD>(e, 0)] = static_cast<uint8_t>(hi & 0xff);
-            gq[piece_offset<BD>(e, 1)] = static_cast<uint8_t>(lo & 0xff);
-            if (lane == 0) a.hs[(size_t)route * nseg + p] = make_float2(sum, exp2i(-(S + 8 - BD)));
-            asm volatile("fence.proxy.async.global;" ::: "memory");  // read back by bulk copies
-            __threadfence();
-            __syncwarp();
-            if (lane == 0) atomicAdd(a.hready, 1u);
-        }
-    }
-
-    // ============================== every unit done (bounded wait), h pieces in
-    const bool hok = grid_wait(a.hready, static_cast<uint32_t>(nunits));
-    pdl_trigger();  // every block of this grid is resident
-    if (!hok) {
+    // Every block has started (all passed the launch wait): dependents may
+    // launch without taking an SM this grid still needs.
+    pdl_trigger();
+    if (s_abort) {
         drain();
         return;
     }
-    if (npB > 0) {
-        const uint32_t hq_bytes = static_cast<uint32_t>(R * PB.ngroups * 2 * GS);
-        const uint32_t hs_bytes = static_cast<uint32_t>((R * nseg * 8 + 15) & ~15);  // padded on both sides
-        if (threadIdx.x == 0) {
-            asm volatile("fence.proxy.async.global;" ::: "memory");  // generic writes of other blocks -> async reads
-            mbar_expect_tx(&xbar[1], hq_bytes + hs_bytes);
-            bulk_g2s(hq, a.hq, hq_bytes, &xbar[1]);
-            bulk_g2s(hs, a.hs, hs_bytes, &xbar[1]);
-        }
-        if (!mbar_wait(&xbar[1], 0)) {
-            set_error(a.err, -4);
-            aborted = true;
-        }
-    }
 
     // ============================== down items
-    for (int n = 0; n < myB && !aborted; ++n) {
-        const int i = warp + n * W, j = i / perB, r2 = i - j * perB, ch = r2 / PB.nck, cc = r2 - ch * PB.nck;
+    // Item (pair, chunk ch, K chunk cc) needs h's K chunk cc of its route:
+    // the CK / 32 gate/up units of that chunk (count hready[route][cc]).
+    // Lane 0 waits for them (bounded), then the warp loads the chunk's int8
+    // pieces and (sum, factor) into its own scratch.
+    const int upc = PB.nck > 0 ? PA.pairs / PB.nck : 1;  // gate/up units per down K chunk
+    uint8_t *wq = hq + (size_t)warp * (8 * 2 * GS + 8 * NSEG_D * 8);  // [8 groups][2 GS]
+    float2 *wxs = reinterpret_cast<float2 *>(wq + 8 * 2 * GS);         // [8 groups][NSEG_D]
+    for (int n = 0; n < myB && !aborted; ++n, cur_next(cu)) {
+        const int j = cu.j, ch = cu.ch, cc = cu.cc;
         const int route = __shfl_sync(kFull, croute, ch);
+        const uint32_t *ctr = a.hready + (size_t)route * PB.nck + cc;
+        bool ok = true;
+        if (ld_acquire_u32(ctr) < static_cast<uint32_t>(upc)) {
+            const long long t0 = clock64();
+            uint32_t sl = 32;
+            while (ld_acquire_u32(ctr) < static_cast<uint32_t>(upc)) {
+                __nanosleep(sl);
+                if (sl < 256) sl <<= 1;
+                if (clock64() - t0 > kWaitLimitCycles) {
+                    ok = false;
+                    break;
+                }
+            }
+        }
+        if (!__all_sync(kFull, ok)) {
+            set_error(a.err, -4);
+            aborted = true;
+            break;
+        }
+        {
+            // 16-byte pieces of the chunk (8 groups) and its 8 * NSEG_D factors
+            const uint4 *sq = reinterpret_cast<const uint4 *>(a.hq + ((size_t)route * PB.ngroups + cc * 8) * (2 * GS));
+            const float4 *ss = reinterpret_cast<const float4 *>(a.hs + (size_t)route * nseg + cc * 8 * NSEG_D);
+            constexpr int NQ = 8 * 2 * GS / 16, NS = 8 * NSEG_D / 2;
+            uint4 v[(NQ + 31) / 32];
+            float4 f[(NS + 31) / 32];
+#pragma unroll
+            for (int q = 0; q < (NQ + 31) / 32; ++q)
+                if (lane + 32 * q < NQ) v[q] = __ldcg(sq + lane + 32 * q);
+#pragma unroll
+            for (int q = 0; q < (NS + 31) / 32; ++q)
+                if (lane + 32 * q < NS) f[q] = __ldcg(ss + lane + 32 * q);
+#pragma unroll
+            for (int q = 0; q < (NQ + 31) / 32; ++q)
+                if (lane + 32 * q < NQ) reinterpret_cast<uint4 *>(wq)[lane + 32 * q] = v[q];
+#pragma unroll
+            for (int q = 0; q < (NS + 31) / 32; ++q)
+                if (lane + 32 * q < NS) reinterpret_cast<float4 *>(wxs)[lane + 32 * q] = f[q];
+        }
+        __syncwarp();
         if (!wait_next()) {
             set_error(a.err, -4);
             aborted = true;
             break;
         }
         float dacc[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};
-        vec_item<TA, BD, GS, 2, NSEG_D>(ring + (size_t)cp * c.sub, hq + (size_t)route * PB.ngroups * (2 * GS),
-                                        hs + (size_t)route * nseg, zero, cc, dacc);
+        vec_item<TA, BD, GS, 2, NSEG_D>(ring + (size_t)cp * c.sub, wq, wxs, zero, 0, dacc);
         advance();
 #pragma unroll
         for (int m = 0; m < 2; ++m)
@@ -769,6 +718,7 @@ bool vec_layer_config(int hidden, int inter, int bits_g, int gs_g, int bits_d, i
     c.grid = vec_sm_count();
     const int G = c.grid;
     const int u_max = (routes * c.ga.pairs + G - 1) / G, p_max = (c.dn.pairs + G - 1) / G;
+    if (u_max > 32) return false;  // a block's gate/up units sit one per lane
     // ring sub-slots: a gate/up item (gate + up block) takes qa of them, a
     // down item qb; both at most 2, so items never straddle the ring's end
     c.sub = al128(static_cast<int>(c.ga.blk < c.dn.blk ? c.ga.blk : c.dn.blk));
@@ -784,11 +734,11 @@ bool vec_layer_config(int hidden, int inter, int bits_g, int gs_g, int bits_d, i
     c.off_zero = al128(c.off_xbar + 16);
     c.off_rch = al128(c.off_zero + 2 * gs);
     c.off_tk = al128(c.off_rch + 32 * 4);
-    c.off_xs = al128(c.off_tk + (kVecWarps * 16 + 16) * 16);  // lists + winners
+    c.off_xs = al128(c.off_tk + 32 * 16);  // top-k result per lane
     c.off_xq = al128(c.off_xs + c.ga.ngroups * 8 + 16);
-    c.off_hs = al128(c.off_xq + c.ga.ngroups * 2 * gs);
-    c.off_hq = al128(c.off_hs + routes * (inter / 32) * 8 + 16);
-    c.off_pa = al128(c.off_hq + routes * c.dn.ngroups * 2 * gs);
+    // per-warp scratch of one K chunk of h: 8 groups of pieces, 8 * gs / 32 factors
+    c.off_hq = al128(c.off_xq + c.ga.ngroups * 2 * gs);
+    c.off_pa = al128(c.off_hq + kVecWarps * (8 * 2 * gs + 8 * (gs / 32) * 8));
     c.off_pb = al128(c.off_pa + u_max * c.ga.nck * 64 * 4);
     c.off_ring = al128(c.off_pb + p_max * routes * c.dn.nck * 32 * 4);
     const long room = (long)kVecSmem - c.off_ring;
