@@ -41,15 +41,18 @@
 //   down:    per route y = T(sum), T(T(y) * T(w)), summed in route order in
 //            fp32, then the shared expert's row and the residual
 //            (combine_finish, arena.py:619-624).
-// Between the phases each block waits (bounded) until every unit is done,
-// then bulk-copies the h pieces.  The kernel needs all its blocks resident
-// (one per SM; the grid is the SM count).  Routing: a single token's top-k
-// runs in one warp (fused_topk) from the router's scores, or the chunk table is
-// read; x's int8 pieces come from the router (or are converted here).
-// The sums run in a fixed order, so results repeat bit for bit.
+// A finished gate/up unit adds one to the count of its h chunk (route, down K
+// chunk); a down item waits (bounded) only for the count of the chunk it
+// reads, so the down phase starts chunk by chunk, not behind a grid-wide
+// barrier, and the next item's chunk is loaded while the current one
+// computes.  The kernel needs all its blocks resident (one per SM; the grid
+// is the SM count).  Routing: a single token's top-k runs block-wide
+// (block_topk) from the router's scores, or the chunk table is read; x's
+// int8 pieces come from the router (or are converted here).  The sums run in
+// a fixed order, so results repeat bit for bit.
 //
-// Every wait is bounded (mbar_wait, the grid-wide counter); on a timeout the
-// kernel flags LMOE_ECUDA, drains the copies it issued (bounded) and stops.
+// Every wait is bounded (mbar_wait, the h counts); on a timeout the kernel
+// flags LMOE_ECUDA, drains the copies it issued (bounded) and stops.
 #include <cstdlib>
 #include <cstring>
 
@@ -200,13 +203,140 @@ __device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t *p) {
     return v;
 }
 
-// The routing of one lane (chunk pos, arena slot, weight), shared by the
-// warp that ran the top-k with the rest of the block.
-struct TkShare {
-    int32_t pos, slot;
+// Single-token top-k of the block from the router's (score, biased score)
+// (arena.py:501-506), with the winners, selection order and weights of the
+// router's own finisher (fused_topk).  Experts are ordered by (key desc, id
+// asc), a strict order.  Thread tid holds experts tid and tid + 256 (E <= 512).
+//  1. Each warp ranks its own experts among themselves with shuffles.  An
+//     expert that k others of its warp beat cannot win, so only local ranks
+//     below k go on, into shared memory at [warp][local rank].
+//  2. One thread per candidate counts the candidates that beat it; a count
+//     below k is its place in the selection order.  Every expert that beats a
+//     winner is itself a winner, hence a candidate, so the count is exact for
+//     the winners and at least k for the rest.
+//  3. Thread j < k takes the j-th winner: weight = score / (fp32 sum of the
+//     winners' scores in selection order + 1e-20) * scaling; its chunk in the
+//     dispatch is the rank of its id among the winners' ids.  Block 0 writes
+//     the routing and the dispatch.
+// Lane ch < k of every warp returns chunk ch's (arena slot, route, weight).
+struct TkCand {
+    uint32_t key;
+    int32_t id, slot;
+    float score;
+};
+struct TkChunk {
+    int32_t slot, route;
     float w;
     int32_t pad;
 };
+constexpr int kTkBytes = (kVecWarps * 16 + 16) * 16 + 16 * 16;  // candidates, winners, chunks
+
+template <class A>
+__device__ __forceinline__ void block_topk(const A &a, uint8_t *tks, int &cslot, int &croute, float &cw) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int E = a.tk_E, k = a.tk_k;
+    TkCand *cand = reinterpret_cast<TkCand *>(tks);        // [warps][k]
+    TkCand *win = cand + kVecWarps * 16;                   // [k], selection order
+    TkChunk *chk = reinterpret_cast<TkChunk *>(win + 16);  // [k], dispatch order
+    uint32_t mk[2];
+    float ms[2];
+    int msl[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const int e = tid + 256 * i;
+        mk[i] = 0u;
+        ms[i] = 0.0f;
+        msl[i] = e;
+        if (e < E) {
+            const float2 v = __ldcg(a.tk_scores + e);
+            ms[i] = v.x;
+            mk[i] = topk_key(v.y);
+            if (a.tk_expert_slot) msl[i] = __ldg(a.tk_expert_slot + e);
+        }
+    }
+    // 1. ranks within the warp: set i2 of the warp holds experts warp * 32 + src + 256 * i2
+    int lr0 = 0, lr1 = 0;
+    const bool two = E > 256;
+    for (int i2 = 0; i2 < (two ? 2 : 1); ++i2) {
+        const uint32_t kv = i2 ? mk[1] : mk[0];
+#pragma unroll 8
+        for (int src = 0; src < 32; ++src) {
+            const uint32_t ok = __shfl_sync(kFull, kv, src);
+            const int oi = src + 256 * i2;
+            lr0 += (ok > mk[0]) || (ok == mk[0] && oi < lane);
+            if (two) lr1 += (ok > mk[1]) || (ok == mk[1] && oi < lane + 256);
+        }
+    }
+    if (lane < k) cand[warp * k + lane] = TkCand{0u, 0x7fffffff, 0, 0.0f};
+    if (tid < k) {
+        win[tid] = TkCand{0u, 0x7fffffff, 0, 0.0f};
+        chk[tid] = TkChunk{0, tid, 0.0f, 0};
+    }
+    __syncwarp();
+    if (mk[0] != 0u && lr0 < k) cand[warp * k + lr0] = TkCand{mk[0], tid, msl[0], ms[0]};
+    if (two && mk[1] != 0u && lr1 < k) cand[warp * k + lr1] = TkCand{mk[1], tid + 256, msl[1], ms[1]};
+    __syncthreads();
+    // 2. ranks among the candidates
+    const int nc = static_cast<int>(blockDim.x >> 5) * k;
+    if (tid < nc) {
+        const TkCand me = cand[tid];
+        if (me.key != 0u) {
+            int rank = 0;
+#pragma unroll 4
+            for (int o = 0; o < nc; ++o) {
+                const TkCand q = cand[o];
+                rank += (q.key > me.key) || (q.key == me.key && q.id < me.id);
+            }
+            if (rank < k) win[rank] = me;
+        }
+    }
+    __syncthreads();
+    // 3. weights and the dispatch
+    if (tid < k) {
+        const TkCand me = win[tid];
+        float ssum = 0.0f;  // fp32, in selection order
+        int pos = 0;        // rank of this winner's id among the winners' ids
+        for (int j = 0; j < k; ++j) {
+            const TkCand q = win[j];
+            ssum += q.score;
+            pos += q.id < me.id;
+        }
+        float wv = a.tk_norm ? me.score / (ssum + 1e-20f) : me.score;
+        wv *= a.tk_scaling;
+        int slot = 0;
+        if (me.id < 0 || me.id >= E) {
+            set_error(a.err, -3);
+        } else {
+            slot = me.slot;
+            if (slot < 0 || slot >= a.n_slots) {
+                set_error(a.err, -3);
+                slot = 0;
+            }
+        }
+        chk[pos] = TkChunk{slot, tid, wv, 0};
+        if (blockIdx.x == 0) {
+            a.tk_idx[tid] = me.id;
+            a.tk_w[tid] = wv;
+            if (a.tk_idx_user) a.tk_idx_user[tid] = me.id;
+            if (a.tk_w_user) a.tk_w_user[tid] = wv;
+            a.tk_sorted[pos] = tid;
+            Chunk ch;
+            ch.slot = slot;
+            ch.route_start = pos;
+            ch.ntok = 1;
+            ch.expert = me.id;
+            a.tk_chunks[pos] = ch;
+            if (tid == 0) *a.tk_nchunks = k;
+        }
+    }
+    __syncthreads();
+    if (lane < k) {
+        const TkChunk q = chk[lane];
+        cslot = q.slot;
+        croute = q.route;
+        cw = q.w;
+    }
+}
 
 template <typename TA, int BG, int BD, int GS>
 __global__ void __launch_bounds__(kVecWarps * 32, 1) vec_layer_kernel(const VecArgs a, const VecCfg c) {
@@ -242,6 +372,29 @@ __global__ void __launch_bounds__(kVecWarps * 32, 1) vec_layer_kernel(const VecA
     if (threadIdx.x == 0) s_abort = 0;
     __syncthreads();
 
+    // ---- this block's units and this warp's items, for nch chunks.  With
+    // the top-k fused here the chunk count is k before the routing exists,
+    // so the plan is made while the preceding kernel still runs.
+    int nch = 0, nuA = 0, npB = 0, perB = 0, myA = 0, myB = 0, total = 0;
+    int uch = 0, upr = 0;  // lane j: the block's gate/up unit b + j * G as (chunk, pair)
+    auto plan = [&](int n) {
+        nch = n;
+        const int nunits = nch * PA.pairs;
+        nuA = b < nunits ? (nunits - b + G - 1) / G : 0;  // gate/up units b, b + G, ...
+        npB = b < PB.pairs ? (PB.pairs - b + G - 1) / G : 0;  // down pairs b, b + G, ...
+        perB = nch * PB.nck;
+        const int nitA = nuA * PA.nck, nitB = npB * perB;
+        myA = nitA > warp ? (nitA - warp + W - 1) / W : 0;
+        myB = nitB > warp ? (nitB - warp + W - 1) / W : 0;
+        total = myA + myB;
+        if (lane < nuA) {
+            const int u = b + lane * G;
+            uch = u / PA.pairs;
+            upr = u - uch * PA.pairs;
+        }
+    };
+    if (a.tk_scores) plan(a.tk_k);
+
     // The routing and x's pieces come from the preceding kernel.  Dependent
     // launches are released only after the grid-wide wait below: until then
     // every block of this grid must be able to become resident.
@@ -253,38 +406,17 @@ __global__ void __launch_bounds__(kVecWarps * 32, 1) vec_layer_kernel(const VecA
         bulk_g2s(xq, a.xq, xq_bytes, &xbar[0]);
         bulk_g2s(xs, a.xs, xs_bytes, &xbar[0]);
     }
-    int nch, cslot = 0, croute = 0;  // lane ch holds chunk ch's (slot, route, weight)
+    int cslot = 0, croute = 0;  // lane ch holds chunk ch's (slot, route, weight)
     float cw = 1.0f;
     if (a.tk_scores) {
-        // warp 0 selects (fused_topk; block 0's also writes the routing and
-        // the dispatch), the block reads its result from shared memory
-        TkShare *tks = reinterpret_cast<TkShare *>(smem + c.off_tk);
-        if (warp == 0) {
-            const TopkRegs r = fused_topk(a, true);
-            tks[lane] = TkShare{r.pos, r.slot, r.w, 0};
-        }
-        __syncthreads();
-        TopkRegs tk;
-        tk.pos = tks[lane].pos;
-        tk.slot = tks[lane].slot;
-        tk.w = tks[lane].w;
-        nch = a.tk_k;
-        for (int j = 0; j < nch; ++j) {
-            const int pj = __shfl_sync(kFull, tk.pos, j);
-            const int sj = __shfl_sync(kFull, tk.slot, j);
-            const float wj = __shfl_sync(kFull, tk.w, j);
-            if (lane == pj) {
-                cslot = sj;
-                croute = j;
-                cw = wj;
-            }
-        }
+        block_topk(a, smem + c.off_tk, cslot, croute, cw);
     } else {
-        nch = __ldcg(a.n_chunks);
-        if (nch < 0 || nch > a.max_chunks || nch > 32 || nch > R) {
+        int n = __ldcg(a.n_chunks);
+        if (n < 0 || n > a.max_chunks || n > 32 || n > R) {
             set_error(a.err, -3);
-            nch = nch < 0 ? 0 : min(min(a.max_chunks, 32), R);
+            n = n < 0 ? 0 : min(min(a.max_chunks, 32), R);
         }
+        plan(n);
         if (lane < nch) {
             const int4 ck = __ldcg(reinterpret_cast<const int4 *>(a.chunks) + lane);  // {slot, start, ntok, expert}
             cslot = ck.x;
@@ -302,24 +434,7 @@ __global__ void __launch_bounds__(kVecWarps * 32, 1) vec_layer_kernel(const VecA
     }
     if (warp == 0 && lane < nch) route_ch[croute] = lane;
 
-    // ---- this block's units and this warp's items
-    const int nunits = nch * PA.pairs;
-    const int nuA = b < nunits ? (nunits - b + G - 1) / G : 0;  // gate/up units b, b + G, ...
-    const int npB = b < PB.pairs ? (PB.pairs - b + G - 1) / G : 0;  // down pairs b, b + G, ...
-    const int perB = nch * PB.nck;
-    const int nitA = nuA * PA.nck, nitB = npB * perB;
-    const int myA = nitA > warp ? (nitA - warp + W - 1) / W : 0;
-    const int myB = nitB > warp ? (nitB - warp + W - 1) / W : 0;
-    const int total = myA + myB;
     const uint64_t pol = evict_first_policy();
-    // The gate/up units of this block, one per lane: lane j holds unit
-    // b + j * G as (chunk, pair).
-    int uch = 0, upr = 0;
-    if (lane < nuA) {
-        const int u = b + lane * G;
-        uch = u / PA.pairs;
-        upr = u - uch * PA.pairs;
-    }
     // Item cursor over this warp's items -- gate/up items warp, warp + W, ...
     // of the block's list (unit j = i / nck, K chunk cc), then its down items
     // (pair j = i / perB, chunk ch, K chunk cc) -- advanced without division.
@@ -527,55 +642,73 @@ __global__ void __launch_bounds__(kVecWarps * 32, 1) vec_layer_kernel(const VecA
 
     // ============================== down items
     // Item (pair, chunk ch, K chunk cc) needs h's K chunk cc of its route:
-    // the CK / 32 gate/up units of that chunk (count hready[route][cc]).
-    // Lane 0 waits for them (bounded), then the warp loads the chunk's int8
-    // pieces and (sum, factor) into its own scratch.
+    // the CK / 32 gate/up units of that chunk (count hready[route][cc]).  The
+    // warp waits for them (bounded), loads the chunk's int8 pieces and (sum,
+    // factor) pairs into registers, and stores them into its own scratch.
+    // The next item's chunk is loaded while this item computes when its
+    // units are already done.
     const int upc = PB.nck > 0 ? PA.pairs / PB.nck : 1;  // gate/up units per down K chunk
     uint8_t *wq = hq + (size_t)warp * (8 * 2 * GS + 8 * NSEG_D * 8);  // [8 groups][2 GS]
     float2 *wxs = reinterpret_cast<float2 *>(wq + 8 * 2 * GS);         // [8 groups][NSEG_D]
+    constexpr int NQ = 8 * 2 * GS / 16, NS = 8 * NSEG_D / 2;  // 16-byte pieces and factor pairs of a chunk
+    constexpr int VQ = (NQ + 31) / 32, VS = (NS + 31) / 32;
+    uint4 hv[VQ];
+    float4 hf[VS];
+    auto h_ctr = [&](const Cur &q) {
+        return a.hready + (size_t)__shfl_sync(kFull, croute, q.ch) * PB.nck + q.cc;
+    };
+    auto h_load = [&](const Cur &q) {
+        const int route = __shfl_sync(kFull, croute, q.ch);
+        const uint4 *sq = reinterpret_cast<const uint4 *>(a.hq + ((size_t)route * PB.ngroups + q.cc * 8) * (2 * GS));
+        const float4 *ss = reinterpret_cast<const float4 *>(a.hs + (size_t)route * nseg + q.cc * 8 * NSEG_D);
+#pragma unroll
+        for (int i = 0; i < VQ; ++i)
+            if (lane + 32 * i < NQ) hv[i] = __ldcg(sq + lane + 32 * i);
+#pragma unroll
+        for (int i = 0; i < VS; ++i)
+            if (lane + 32 * i < NS) hf[i] = __ldcg(ss + lane + 32 * i);
+    };
+    bool have = false;  // hv / hf hold the chunk of the item at cu
     for (int n = 0; n < myB && !aborted; ++n, cur_next(cu)) {
         const int j = cu.j, ch = cu.ch, cc = cu.cc;
-        const int route = __shfl_sync(kFull, croute, ch);
-        const uint32_t *ctr = a.hready + (size_t)route * PB.nck + cc;
-        bool ok = true;
-        if (ld_acquire_u32(ctr) < static_cast<uint32_t>(upc)) {
-            const long long t0 = clock64();
-            uint32_t sl = 32;
-            while (ld_acquire_u32(ctr) < static_cast<uint32_t>(upc)) {
-                __nanosleep(sl);
-                if (sl < 256) sl <<= 1;
-                if (clock64() - t0 > kWaitLimitCycles) {
-                    ok = false;
-                    break;
+        if (!have) {
+            const uint32_t *ctr = h_ctr(cu);
+            bool ok = true;
+            if (ld_acquire_u32(ctr) < static_cast<uint32_t>(upc)) {
+                const long long t0 = clock64();
+                uint32_t sl = 32;
+                while (ld_acquire_u32(ctr) < static_cast<uint32_t>(upc)) {
+                    __nanosleep(sl);
+                    if (sl < 256) sl <<= 1;
+                    if (clock64() - t0 > kWaitLimitCycles) {
+                        ok = false;
+                        break;
+                    }
                 }
             }
+            if (!__all_sync(kFull, ok)) {
+                set_error(a.err, -4);
+                aborted = true;
+                break;
+            }
+            h_load(cu);
         }
-        if (!__all_sync(kFull, ok)) {
-            set_error(a.err, -4);
-            aborted = true;
-            break;
-        }
-        {
-            // 16-byte pieces of the chunk (8 groups) and its 8 * NSEG_D factors
-            const uint4 *sq = reinterpret_cast<const uint4 *>(a.hq + ((size_t)route * PB.ngroups + cc * 8) * (2 * GS));
-            const float4 *ss = reinterpret_cast<const float4 *>(a.hs + (size_t)route * nseg + cc * 8 * NSEG_D);
-            constexpr int NQ = 8 * 2 * GS / 16, NS = 8 * NSEG_D / 2;
-            uint4 v[(NQ + 31) / 32];
-            float4 f[(NS + 31) / 32];
 #pragma unroll
-            for (int q = 0; q < (NQ + 31) / 32; ++q)
-                if (lane + 32 * q < NQ) v[q] = __ldcg(sq + lane + 32 * q);
+        for (int i = 0; i < VQ; ++i)
+            if (lane + 32 * i < NQ) reinterpret_cast<uint4 *>(wq)[lane + 32 * i] = hv[i];
 #pragma unroll
-            for (int q = 0; q < (NS + 31) / 32; ++q)
-                if (lane + 32 * q < NS) f[q] = __ldcg(ss + lane + 32 * q);
-#pragma unroll
-            for (int q = 0; q < (NQ + 31) / 32; ++q)
-                if (lane + 32 * q < NQ) reinterpret_cast<uint4 *>(wq)[lane + 32 * q] = v[q];
-#pragma unroll
-            for (int q = 0; q < (NS + 31) / 32; ++q)
-                if (lane + 32 * q < NS) reinterpret_cast<float4 *>(wxs)[lane + 32 * q] = f[q];
-        }
+        for (int i = 0; i < VS; ++i)
+            if (lane + 32 * i < NS) reinterpret_cast<float4 *>(wxs)[lane + 32 * i] = hf[i];
         __syncwarp();
+        have = false;
+        if (n + 1 < myB) {  // every lane acquires the count itself before loading
+            Cur cn = cu;
+            cur_next(cn);
+            if (__all_sync(kFull, ld_acquire_u32(h_ctr(cn)) >= static_cast<uint32_t>(upc))) {
+                h_load(cn);
+                have = true;
+            }
+        }
         if (!wait_next()) {
             set_error(a.err, -4);
             aborted = true;
@@ -734,7 +867,7 @@ bool vec_layer_config(int hidden, int inter, int bits_g, int gs_g, int bits_d, i
     c.off_zero = al128(c.off_xbar + 16);
     c.off_rch = al128(c.off_zero + 2 * gs);
     c.off_tk = al128(c.off_rch + 32 * 4);
-    c.off_xs = al128(c.off_tk + 32 * 16);  // top-k result per lane
+    c.off_xs = al128(c.off_tk + kTkBytes);  // top-k candidates, winners and chunks
     c.off_xq = al128(c.off_xs + c.ga.ngroups * 8 + 16);
     // per-warp scratch of one K chunk of h: 8 groups of pieces, 8 * gs / 32 factors
     c.off_hq = al128(c.off_xq + c.ga.ngroups * 2 * gs);
