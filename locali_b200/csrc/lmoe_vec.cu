@@ -433,6 +433,8 @@ __global__ void __launch_bounds__(kVecWarps * 32, 1) vec_layer_kernel(const VecA
         }
     }
     if (warp == 0 && lane < nch) route_ch[croute] = lane;
+    // the residual rows of this warp's first combine pair, loaded early
+    const uint16_t rv_pre = (a.residual && a.out && warp < npB) ? a.residual[32 * (b + warp * G) + lane] : 0;
 
     const uint64_t pol = evict_first_policy();
     // Item cursor over this warp's items -- gate/up items warp, warp + W, ...
@@ -739,39 +741,36 @@ __global__ void __launch_bounds__(kVecWarps * 32, 1) vec_layer_kernel(const VecA
     }
     __syncthreads();
 
-    // ---- down pairs of this block: per route y in K order, y * w, the
+    // ---- down pairs of this block: per (pair, chunk) y in K order and the
+    // route's row T(T(y) * T(w)), spread over the warps; then per pair the
     // combine in route order, the shared expert's row and the residual
-    for (int j = warp; j < npB; j += W) {
-        const int p = b + j * G, row = 32 * p + lane;
-        auto yrow = [&](int ch) {
-            const float *pp = pb + ((size_t)j * R + ch) * PB.nck * 32 + ml * 16 + rl;
-            float y = 0.0f;
-            for (int cc = 0; cc < PB.nck; ++cc) y += pp[cc * 32];
-            return y;
-        };
-        if (a.yw)  // per-route rows of the routes computed
-            for (int ch = 0; ch < nch; ++ch) {
-                const int r = __shfl_sync(kFull, croute, ch);
-                const float wv = Act<TA>::round(__shfl_sync(kFull, cw, ch));
-                a.yw[(size_t)r * hidden + row] = Act<TA>::from_f(Act<TA>::round(yrow(ch)) * wv);
-            }
-        if (a.out) {
+    // (combine_finish).  A pair's row of chunk ch replaces its K chunk 0
+    // partial in shared memory.
+    for (int q = warp; q < npB * nch; q += W) {
+        const int j = q / nch, ch = q - j * nch;
+        const int row = 32 * (b + j * G) + lane;
+        float *pp = pb + ((size_t)j * R + ch) * PB.nck * 32 + ml * 16 + rl;
+        float y = 0.0f;
+        for (int cc = 0; cc < PB.nck; ++cc) y += pp[cc * 32];
+        const float v = Act<TA>::round(Act<TA>::round(y) * Act<TA>::round(__shfl_sync(kFull, cw, ch)));
+        if (a.yw) a.yw[(size_t)__shfl_sync(kFull, croute, ch) * hidden + row] = Act<TA>::from_f(v);
+        pp[0] = v;
+    }
+    __syncthreads();
+    if (a.out)
+        for (int j = warp; j < npB; j += W) {
+            const int row = 32 * (b + j * G) + lane;
+            const float *yv = pb + (size_t)j * R * PB.nck * 32 + lane;  // + ch * nck * 32: chunk ch's row
             float sacc = 0.0f;
             for (int r = 0; r < a.top_k && r < R; ++r) {
                 const int ch = route_ch[r];
-                const float wv = Act<TA>::round(__shfl_sync(kFull, cw, ch < 0 ? 0 : ch));
-                if (ch >= 0) sacc += Act<TA>::round(Act<TA>::round(yrow(ch)) * wv);
+                if (ch >= 0) sacc += yv[(size_t)ch * PB.nck * 32];
             }
             const bool sh = a.shared_base > 0 && a.shared_base < R && route_ch[a.shared_base] >= 0;
-            uint16_t sv = 0;
-            if (sh) {
-                const int ch = route_ch[a.shared_base];
-                sv = Act<TA>::from_f(Act<TA>::round(yrow(ch)) * Act<TA>::round(__shfl_sync(kFull, cw, ch)));
-            }
-            const uint16_t rv = a.residual ? a.residual[row] : 0;
+            const uint16_t sv = sh ? Act<TA>::from_f(yv[(size_t)route_ch[a.shared_base] * PB.nck * 32]) : 0;
+            const uint16_t rv = !a.residual ? 0 : (j == warp ? rv_pre : a.residual[row]);
             a.out[row] = Act<TA>::from_f(combine_finish<TA>(sacc, sh, sv, a.residual != nullptr, rv));
         }
-    }
 }
 
 int g_vec_sms = 0;
