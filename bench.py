@@ -776,7 +776,10 @@ def run_decode_main(args, world, rank, dev, name):
     K, W = args.steps, args.warmup
     r = measure_decode(cfg, kerns, K, W, dev, world, rank, args.kernel_steps, args.path)
     traffic = None
-    prof = ROOT / "profiles" / f"gateup_{cfg.name}_traffic.json"
+    # ncu DRAM bytes of the roofline kernel (one launch), when a capture of
+    # it for this config is committed
+    kname = "vec_layer" if r["roofline"]["kernel"].startswith("vec_layer") else "gateup"
+    prof = ROOT / "profiles" / f"{kname}_{cfg.name}_traffic.json"
     if prof.exists():
         try:
             traffic = json.loads(prof.read_text()).get("dram_bytes_per_launch")
