@@ -553,6 +553,7 @@ __device__ __forceinline__ void convert_group_rt(int bits, int gs, const uint16_
 // computes; a grid-wide counter of converted h groups (bounded wait) starts
 // the down products.
 constexpr int kVecWarps = 8;      // warps per block, each with its own copy ring
+constexpr int kVecBlockWarps = kVecWarps + 1;  // and one warp that finishes the gate/up units
 constexpr int kVecMaxStages = 8;  // ring sub-slots per warp
 struct VecPhase {                  // geometry of one projection's stream format
     int32_t nck, pairs, RB, fm_c, tS, tB, TB, ngroups;

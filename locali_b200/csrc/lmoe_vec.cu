@@ -37,22 +37,23 @@
 // block finishes its units in K order:
 //   gate/up: clamped SwiGLU (dsv4_arena.py:223-235) into h, and h's 32 rows
 //            as int8 pieces with one scale per 32-row segment (written to
-//            global scratch; a grid-wide count of finished units follows);
+//            global scratch, then counted);
 //   down:    per route y = T(sum), T(T(y) * T(w)), summed in route order in
 //            fp32, then the shared expert's row and the residual
 //            (combine_finish, arena.py:619-624).
-// A finished gate/up unit adds one to the count of its h chunk (route, down K
-// chunk); a down item waits (bounded) only for the count of the chunk it
-// reads, so the down phase starts chunk by chunk, not behind a grid-wide
-// barrier, and the next item's chunk is loaded while the current one
-// computes.  The kernel needs all its blocks resident (one per SM; the grid
-// is the SM count).  Routing: a single token's top-k runs block-wide
+// A ninth warp (the finisher) finishes each gate/up unit as soon as its
+// items are done and adds one to the count of the unit's h chunk (route,
+// down K chunk); a down item waits (bounded) only for the count of the chunk
+// it reads, so the first chunks are ready while later units still compute,
+// and the next item's chunk is loaded while the current one computes.  The
+// kernel needs all its blocks resident (one per SM; the grid is the SM
+// count).  Routing: a single token's top-k runs block-wide
 // (block_topk) from the router's scores, or the chunk table is read; x's
 // int8 pieces come from the router (or are converted here).  The sums run in
 // a fixed order, so results repeat bit for bit.
 //
-// Every wait is bounded (mbar_wait, the h counts); on a timeout the kernel
-// flags LMOE_ECUDA, drains the copies it issued (bounded) and stops.
+// Every wait is bounded (mbar_wait, the unit and h counts); on a timeout the
+// kernel flags LMOE_ECUDA, drains the copies it issued (bounded) and stops.
 #include <cstdlib>
 #include <cstring>
 
@@ -138,6 +139,7 @@ __device__ __forceinline__ void vec_item(const uint8_t *sb, const uint8_t *xrow,
             for (int jj = 0; jj < NJ; ++jj) bf[jj] = lds<uint2>(bp + (prov ? jj * 16 : 0));
         }
         float X = 0.0f, P[NM][2];
+        uint4 qa[NM], qb[NM];  // 16 bytes of rows g and g + 8: word pairs wp, wp + 1
 #pragma unroll
         for (int sg = 0; sg < NSEG; ++sg) {
             const float2 xg = xsr[(cc * 8 + gi) * NSEG + sg];
@@ -149,10 +151,25 @@ __device__ __forceinline__ void vec_item(const uint8_t *sb, const uint8_t *xrow,
                 const int byte = gi * WPG * 4 + wp * 8;  // word pair's offset in the row
                 const int off = (((byte >> 4) ^ cfx) << 4) + (byte & 15);
                 uint2 wa[NM], wb[NM];
+                if constexpr (WPG >= 4) {  // a group row is whole 16-byte chunks: one load per two word pairs
+                    if ((wp & 1) == 0) {
 #pragma unroll
-                for (int m = 0; m < NM; ++m) {
-                    wa[m] = lds<uint2>(rg + m * VT::TB + off);
-                    wb[m] = lds<uint2>(rg + m * VT::TB + 8 * VT::RB + off);
+                        for (int m = 0; m < NM; ++m) {
+                            qa[m] = lds<uint4>(rg + m * VT::TB + off);
+                            qb[m] = lds<uint4>(rg + m * VT::TB + 8 * VT::RB + off);
+                        }
+                    }
+#pragma unroll
+                    for (int m = 0; m < NM; ++m) {
+                        wa[m] = (wp & 1) ? make_uint2(qa[m].z, qa[m].w) : make_uint2(qa[m].x, qa[m].y);
+                        wb[m] = (wp & 1) ? make_uint2(qb[m].z, qb[m].w) : make_uint2(qb[m].x, qb[m].y);
+                    }
+                } else {
+#pragma unroll
+                    for (int m = 0; m < NM; ++m) {
+                        wa[m] = lds<uint2>(rg + m * VT::TB + off);
+                        wb[m] = lds<uint2>(rg + m * VT::TB + 8 * VT::RB + off);
+                    }
                 }
 #pragma unroll
                 for (int p2 = 0; p2 < NC; ++p2) {
@@ -206,7 +223,7 @@ __device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t *p) {
 // Single-token top-k of the block from the router's (score, biased score)
 // (arena.py:501-506), with the winners, selection order and weights of the
 // router's own finisher (fused_topk).  Experts are ordered by (key desc, id
-// asc), a strict order.  Thread tid holds experts tid and tid + 256 (E <= 512).
+// asc), a strict order.  Thread tid holds experts tid, tid + NT, ... (NT threads, E <= 512).
 //  1. Each warp ranks its own experts among themselves with shuffles.  An
 //     expert that k others of its warp beat cannot win, so only local ranks
 //     below k go on, into shared memory at [warp][local rank].
@@ -229,21 +246,22 @@ struct TkChunk {
     float w;
     int32_t pad;
 };
-constexpr int kTkBytes = (kVecWarps * 16 + 16) * 16 + 16 * 16;  // candidates, winners, chunks
+constexpr int kTkBytes = (kVecBlockWarps * 16 + 16) * 16 + 16 * 16;  // candidates, winners, chunks
 
 template <class A>
 __device__ __forceinline__ void block_topk(const A &a, uint8_t *tks, int &cslot, int &croute, float &cw) {
+    constexpr int NT = kVecBlockWarps * 32, PER = (512 + NT - 1) / NT;  // experts per thread (E <= 512)
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int E = a.tk_E, k = a.tk_k;
     TkCand *cand = reinterpret_cast<TkCand *>(tks);        // [warps][k]
-    TkCand *win = cand + kVecWarps * 16;                   // [k], selection order
+    TkCand *win = cand + kVecBlockWarps * 16;                   // [k], selection order
     TkChunk *chk = reinterpret_cast<TkChunk *>(win + 16);  // [k], dispatch order
-    uint32_t mk[2];
-    float ms[2];
-    int msl[2];
+    uint32_t mk[PER];
+    float ms[PER];
+    int msl[PER];
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-        const int e = tid + 256 * i;
+    for (int i = 0; i < PER; ++i) {
+        const int e = tid + NT * i;
         mk[i] = 0u;
         ms[i] = 0.0f;
         msl[i] = e;
@@ -254,17 +272,20 @@ __device__ __forceinline__ void block_topk(const A &a, uint8_t *tks, int &cslot,
             if (a.tk_expert_slot) msl[i] = __ldg(a.tk_expert_slot + e);
         }
     }
-    // 1. ranks within the warp: set i2 of the warp holds experts warp * 32 + src + 256 * i2
-    int lr0 = 0, lr1 = 0;
-    const bool two = E > 256;
-    for (int i2 = 0; i2 < (two ? 2 : 1); ++i2) {
-        const uint32_t kv = i2 ? mk[1] : mk[0];
+    // 1. ranks within the warp: set i2 of the warp holds experts warp * 32 + src + NT * i2
+    int lr[PER];
+#pragma unroll
+    for (int i = 0; i < PER; ++i) lr[i] = 0;
+#pragma unroll
+    for (int i2 = 0; i2 < PER; ++i2) {
+        if (NT * i2 >= E) break;
 #pragma unroll 8
         for (int src = 0; src < 32; ++src) {
-            const uint32_t ok = __shfl_sync(kFull, kv, src);
-            const int oi = src + 256 * i2;
-            lr0 += (ok > mk[0]) || (ok == mk[0] && oi < lane);
-            if (two) lr1 += (ok > mk[1]) || (ok == mk[1] && oi < lane + 256);
+            const uint32_t ok = __shfl_sync(kFull, mk[i2], src);
+            const int oi = src + NT * i2;
+#pragma unroll
+            for (int i = 0; i < PER; ++i)
+                if (NT * i < E) lr[i] += (ok > mk[i]) || (ok == mk[i] && oi < lane + NT * i);
         }
     }
     if (lane < k) cand[warp * k + lane] = TkCand{0u, 0x7fffffff, 0, 0.0f};
@@ -273,8 +294,9 @@ __device__ __forceinline__ void block_topk(const A &a, uint8_t *tks, int &cslot,
         chk[tid] = TkChunk{0, tid, 0.0f, 0};
     }
     __syncwarp();
-    if (mk[0] != 0u && lr0 < k) cand[warp * k + lr0] = TkCand{mk[0], tid, msl[0], ms[0]};
-    if (two && mk[1] != 0u && lr1 < k) cand[warp * k + lr1] = TkCand{mk[1], tid + 256, msl[1], ms[1]};
+#pragma unroll
+    for (int i = 0; i < PER; ++i)
+        if (mk[i] != 0u && lr[i] < k) cand[warp * k + lr[i]] = TkCand{mk[i], tid + NT * i, msl[i], ms[i]};
     __syncthreads();
     // 2. ranks among the candidates
     const int nc = static_cast<int>(blockDim.x >> 5) * k;
@@ -339,14 +361,18 @@ __device__ __forceinline__ void block_topk(const A &a, uint8_t *tks, int &cslot,
 }
 
 template <typename TA, int BG, int BD, int GS>
-__global__ void __launch_bounds__(kVecWarps * 32, 1) vec_layer_kernel(const VecArgs a, const VecCfg c) {
+__global__ void __launch_bounds__(kVecBlockWarps * 32, 1) vec_layer_kernel(const VecArgs a, const VecCfg c) {
     constexpr int NSEG_D = GS / 32;  // h segments (32 rows, one gate/up unit each) per down group
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
-    const int b = static_cast<int>(blockIdx.x), G = static_cast<int>(gridDim.x), W = static_cast<int>(blockDim.x >> 5);
+    // warps 0 .. W - 1 stream and compute items; warp W (the finisher)
+    // finishes the block's gate/up units as their items complete
+    constexpr int W = kVecWarps;
+    const int b = static_cast<int>(blockIdx.x), G = static_cast<int>(gridDim.x);
+    const bool finisher = warp == W;
     const int nq = c.nq, R = a.routes;
     extern __shared__ __align__(1024) uint8_t smem[];
-    int &s_abort = *reinterpret_cast<int *>(smem + c.off_flag);
+    volatile int &s_abort = *reinterpret_cast<volatile int *>(smem + c.off_flag);
     uint8_t *ring = smem + c.off_ring + (size_t)warp * c.nq * c.sub;
     uint64_t *bar = reinterpret_cast<uint64_t *>(smem + c.off_bar) + warp * kVecMaxStages;
     uint64_t *xbar = reinterpret_cast<uint64_t *>(smem + c.off_xbar);  // x pieces
@@ -357,18 +383,22 @@ __global__ void __launch_bounds__(kVecWarps * 32, 1) vec_layer_kernel(const VecA
     float *pa = reinterpret_cast<float *>(smem + c.off_pa);      // [unit j][K chunk][64]
     float *pb = reinterpret_cast<float *>(smem + c.off_pb);      // [pair j][chunk][K chunk][32]
     int *route_ch = reinterpret_cast<int *>(smem + c.off_rch);   // [R]: chunk of each route (-1: none)
+    int *ucnt = route_ch + 32;                                   // [unit j]: its items done
     const VecPhase &PA = c.ga, &PB = c.dn;
     const int inter = a.q0.rows, hidden = a.q2.rows;
     const int nseg = inter / 32;  // h segments per route
 
-    if (lane == 0) {
+    if (lane == 0 && !finisher) {
         for (int q = 0; q < nq; ++q) mbar_init(&bar[q], 1);
         if (warp == 0) mbar_init(&xbar[0], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     for (int i = threadIdx.x; i < GS / 8; i += blockDim.x)
         reinterpret_cast<uint4 *>(smem + c.off_zero)[i] = make_uint4(0u, 0u, 0u, 0u);
-    for (int i = threadIdx.x; i < 32; i += blockDim.x) route_ch[i] = -1;
+    for (int i = threadIdx.x; i < 32; i += blockDim.x) {
+        route_ch[i] = -1;
+        ucnt[i] = 0;
+    }
     if (threadIdx.x == 0) s_abort = 0;
     __syncthreads();
 
@@ -384,8 +414,8 @@ __global__ void __launch_bounds__(kVecWarps * 32, 1) vec_layer_kernel(const VecA
         npB = b < PB.pairs ? (PB.pairs - b + G - 1) / G : 0;  // down pairs b, b + G, ...
         perB = nch * PB.nck;
         const int nitA = nuA * PA.nck, nitB = npB * perB;
-        myA = nitA > warp ? (nitA - warp + W - 1) / W : 0;
-        myB = nitB > warp ? (nitB - warp + W - 1) / W : 0;
+        myA = !finisher && nitA > warp ? (nitA - warp + W - 1) / W : 0;
+        myB = !finisher && nitB > warp ? (nitB - warp + W - 1) / W : 0;
         total = myA + myB;
         if (lane < nuA) {
             const int u = b + lane * G;
@@ -554,17 +584,17 @@ __global__ void __launch_bounds__(kVecWarps * 32, 1) vec_layer_kernel(const VecA
             set_error(a.err, -4);
             aborted = true;
         }
-    } else {
+    } else if (!finisher) {
         for (int gi = warp; gi < PA.ngroups; gi += W)
             convert_group<TA, BG, GS>(a.x + (size_t)gi * GS, xq + (size_t)gi * (2 * GS), xs + gi, true);
     }
     __syncthreads();  // x pieces and the route map are complete
 
     // ============================== gate/up items
-    // A unit of this block, once all its items are done: K chunks in order,
-    // SwiGLU, and h's int8 pieces (one scale per 32-row segment) into global
-    // scratch, then a release increment of the grid-wide count of finished
-    // units.
+    // A unit of this block, once all its items are done (finisher warp): K
+    // chunks in order, SwiGLU, and h's int8 pieces (one scale per 32-row
+    // segment) into global scratch, then a release increment of the count of
+    // finished units of its h chunk.
     const int ml = lane >> 4, rl = lane & 15;  // lane = row of the 32-row pair
     auto finish_unit = [&](int j) {
         const int ch = __shfl_sync(kFull, uch, j), p = __shfl_sync(kFull, upr, j);
@@ -628,19 +658,41 @@ __global__ void __launch_bounds__(kVecWarps * 32, 1) vec_layer_kernel(const VecA
                 pp[m * 16 + g + 8] = racc[m][1];
             }
         }
+        __syncwarp();
+        if (lane == 0) {  // the partial sums above precede the count
+            __threadfence_block();
+            atomicAdd(&ucnt[j], 1);
+        }
     }
     if (aborted) s_abort = 1;
-    __syncthreads();
-    if (!s_abort)
-        for (int j = warp; j < nuA; j += W) finish_unit(j);
-
-    // Every block has started (all passed the launch wait): dependents may
-    // launch without taking an SM this grid still needs.
-    pdl_trigger();
-    if (s_abort) {
-        drain();
-        return;
+    if (finisher) {
+        // units in the order the warps complete them (every warp takes its
+        // items unit by unit); each wait is bounded and ends when a compute
+        // warp gives up
+        for (int j = 0; j < nuA; ++j) {
+            bool ok = true;
+            if (*reinterpret_cast<volatile int *>(ucnt + j) < PA.nck) {
+                const long long t0 = clock64();
+                while (*reinterpret_cast<volatile int *>(ucnt + j) < PA.nck) {
+                    if (s_abort || clock64() - t0 > kWaitLimitCycles) {
+                        ok = false;
+                        break;
+                    }
+                    __nanosleep(20);
+                }
+            }
+            if (!__all_sync(kFull, ok)) {
+                if (!s_abort) set_error(a.err, -4);
+                s_abort = 1;
+                break;
+            }
+            __threadfence_block();
+            finish_unit(j);
+        }
     }
+    // Every block has passed its launch wait (the routing above follows it):
+    // dependents may launch without taking an SM this grid still needs.
+    pdl_trigger();
 
     // ============================== down items
     // Item (pair, chunk ch, K chunk cc) needs h's K chunk cc of its route:
@@ -682,7 +734,7 @@ __global__ void __launch_bounds__(kVecWarps * 32, 1) vec_layer_kernel(const VecA
                 while (ld_acquire_u32(ctr) < static_cast<uint32_t>(upc)) {
                     __nanosleep(sl);
                     if (sl < 256) sl <<= 1;
-                    if (clock64() - t0 > kWaitLimitCycles) {
+                    if (s_abort || clock64() - t0 > kWaitLimitCycles) {
                         ok = false;
                         break;
                     }
@@ -736,17 +788,18 @@ __global__ void __launch_bounds__(kVecWarps * 32, 1) vec_layer_kernel(const VecA
         }
     }
     if (aborted) {
+        s_abort = 1;
         drain();
-        return;
     }
     __syncthreads();
+    if (s_abort) return;
 
     // ---- down pairs of this block: per (pair, chunk) y in K order and the
     // route's row T(T(y) * T(w)), spread over the warps; then per pair the
     // combine in route order, the shared expert's row and the residual
     // (combine_finish).  A pair's row of chunk ch replaces its K chunk 0
     // partial in shared memory.
-    for (int q = warp; q < npB * nch; q += W) {
+    for (int q = warp; q < npB * nch; q += kVecBlockWarps) {
         const int j = q / nch, ch = q - j * nch;
         const int row = 32 * (b + j * G) + lane;
         float *pp = pb + ((size_t)j * R + ch) * PB.nck * 32 + ml * 16 + rl;
@@ -758,7 +811,7 @@ __global__ void __launch_bounds__(kVecWarps * 32, 1) vec_layer_kernel(const VecA
     }
     __syncthreads();
     if (a.out)
-        for (int j = warp; j < npB; j += W) {
+        for (int j = warp; j < npB; j += kVecBlockWarps) {
             const int row = 32 * (b + j * G) + lane;
             const float *yv = pb + (size_t)j * R * PB.nck * 32 + lane;  // + ch * nck * 32: chunk ch's row
             float sacc = 0.0f;
@@ -815,7 +868,7 @@ cudaError_t launch_vec_t(const VecArgs &a, const VecCfg &c, cudaStream_t st) {
         if (e != cudaSuccess) return e;
         configured = c.smem;
     }
-    return launch_pdl(kern, dim3(static_cast<unsigned>(c.grid)), dim3(c.warps * 32), c.smem, st, a, c);
+    return launch_pdl(kern, dim3(static_cast<unsigned>(c.grid)), dim3(kVecBlockWarps * 32), c.smem, st, a, c);
 }
 
 // (gate/up bits, down bits) pairs compiled, for group sizes 32, 64, 128
@@ -865,7 +918,7 @@ bool vec_layer_config(int hidden, int inter, int bits_g, int gs_g, int bits_d, i
     c.off_xbar = c.off_flag + 16;
     c.off_zero = al128(c.off_xbar + 16);
     c.off_rch = al128(c.off_zero + 2 * gs);
-    c.off_tk = al128(c.off_rch + 32 * 4);
+    c.off_tk = al128(c.off_rch + 64 * 4);  // route -> chunk, unit item counts
     c.off_xs = al128(c.off_tk + kTkBytes);  // top-k candidates, winners and chunks
     c.off_xq = al128(c.off_xs + c.ga.ngroups * 8 + 16);
     // per-warp scratch of one K chunk of h: 8 groups of pieces, 8 * gs / 32 factors
