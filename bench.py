@@ -385,7 +385,8 @@ def measure_decode(cfg, kerns, K, W, dev, world, rank, kernel_steps, path):
     del graph
     value = world * T * K / (ms / 1e3)
 
-    # ---- per-kernel timing pass (events on the launching stream)
+    # ---- per-kernel timing pass (events on the launching stream, at the
+    # kernel boundaries of the same launches the graph replays)
     nk = kernel_steps
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(nk)]
     for e4 in ev:
@@ -399,7 +400,7 @@ def measure_decode(cfg, kerns, K, W, dev, world, rank, kernel_steps, path):
         for s in range(c0, min(nk, c0 + chunk)):
             i = W + (s % K)
             ev[s][0].record()
-            kerns[i % n_layers].staged(xs[i], outs[i], ev[s][1], ev[s][2], idx=idx_buf[s])
+            kerns[i % n_layers].timed(xs[i], outs[i], ev[s][1], ev[s][2], idx=idx_buf[s])
             ev[s][3].record()
     torch.cuda.synchronize()
     for k in kerns:

@@ -179,6 +179,19 @@ int lmoe_moe_layer_staged(const lmoe_layer *layer, const void *x, int32_t tokens
 #define LMOE_PREFILL_MIN_ROUTES 256
 #define LMOE_PREFILL_ROUTES_PER_4_EXPERTS 7
 
+/* lmoe_moe_layer with two caller-owned CUDA events (either may be NULL)
+ * recorded at kernel boundaries only, for timing the kernels of exactly the
+ * launches lmoe_moe_layer makes: ev_router after the routing kernel,
+ * ev_experts after the first expert kernel (for one token over the pre-tiled
+ * copy, the single-token layer kernel, which also selects the top-k).  Unlike
+ * lmoe_moe_layer_staged, ev_router does not mark the routing as complete:
+ * idx/w are written by the layer's later kernels.  No counterpart in the
+ * reference (a timing hook). */
+int lmoe_moe_layer_timed(const lmoe_layer *layer, const void *x, int32_t tokens,
+                         void *out, int32_t *idx, float *w, void *workspace,
+                         size_t ws_bytes, void *stream, void *ev_router,
+                         void *ev_experts);
+
 /* lmoe_moe_layer_staged on an explicit path (LMOE_PATH_*); LMOE_EUNSUPPORTED
  * when the layer's geometry does not allow the requested path. */
 int lmoe_moe_layer_path(const lmoe_layer *layer, const void *x, int32_t tokens,

@@ -112,6 +112,8 @@ _SIGS = {
                                _VP, _VP, _VP], ctypes.c_int),
     "lmoe_moe_layer_path": ([ctypes.POINTER(Layer), _VP, ctypes.c_int32, _VP, _VP, _VP, _VP, ctypes.c_size_t,
                              _VP, ctypes.c_int32, _VP, _VP], ctypes.c_int),
+    "lmoe_moe_layer_timed": ([ctypes.POINTER(Layer), _VP, ctypes.c_int32, _VP, _VP, _VP, _VP, ctypes.c_size_t,
+                              _VP, _VP, _VP], ctypes.c_int),
     "lmoe_workspace_size_path": ([ctypes.POINTER(Layer), ctypes.c_int32, ctypes.c_int32], ctypes.c_size_t),
     "lmoe_moe_layer_static": ([ctypes.POINTER(Layer), _VP, ctypes.c_int32, _VP, _VP, _VP, _VP], ctypes.c_int),
     "lmoe_static_workspace_bytes": ([], ctypes.c_size_t),

@@ -932,7 +932,8 @@ int lmoe_route(const lmoe_router *router, int32_t hidden, int32_t dtype, const v
 // sum; residual (may be NULL, may alias out) is added last.
 static int layer_entry(const lmoe_layer *layer, const void *x, int32_t tokens, const int32_t *hash_idx, void *out,
                        int32_t *idx, float *w, void *workspace, size_t ws_bytes, void *stream, int32_t path,
-                       void *ev_routed, void *ev_gateup, int32_t shared_slot = -1, const void *residual = nullptr) {
+                       void *ev_routed, void *ev_gateup, int32_t shared_slot = -1, const void *residual = nullptr,
+                       bool events_only = false) {
     int rc = check_layer(layer);
     if (rc) return rc;
     if (tokens < 0 || (tokens > 0 && (!x || !out || !workspace))) return LMOE_EINVAL;
@@ -947,8 +948,9 @@ static int layer_entry(const lmoe_layer *layer, const void *x, int32_t tokens, c
     if (residual && !aligned16(residual)) return LMOE_EINVAL;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     // the routing is only complete after gate/up when the top-k is fused:
-    // a caller that waits on ev_routed gets the separate finisher
-    const bool fused = !ev_routed && topk_fusable(layer, tokens, hash_idx, shared_slot >= 0, pf);
+    // a caller that waits on ev_routed gets the separate finisher (unless the
+    // events only mark launch boundaries for timing)
+    const bool fused = (!ev_routed || events_only) && topk_fusable(layer, tokens, hash_idx, shared_slot >= 0, pf);
     bool x_pieces = false;
     rc = route_impl(layer->router, layer->experts.hidden, layer->experts.dtype, layer, L, x, tokens, idx, w,
                     workspace, st, hash_idx, fused, shared ? tokens * layer->router.top_k : 0, &x_pieces);
@@ -982,6 +984,12 @@ int lmoe_moe_layer_path(const lmoe_layer *layer, const void *x, int32_t tokens, 
                         void *ev_gateup) {
     return layer_entry(layer, x, tokens, nullptr, out, idx, w, workspace, ws_bytes, stream, path, ev_routed,
                        ev_gateup);
+}
+
+int lmoe_moe_layer_timed(const lmoe_layer *layer, const void *x, int32_t tokens, void *out, int32_t *idx, float *w,
+                         void *workspace, size_t ws_bytes, void *stream, void *ev_router, void *ev_experts) {
+    return layer_entry(layer, x, tokens, nullptr, out, idx, w, workspace, ws_bytes, stream, LMOE_PATH_AUTO, ev_router,
+                       ev_experts, -1, nullptr, true);
 }
 
 int lmoe_moe_layer_host(const lmoe_layer *layer, const void *x_host, int32_t tokens, void *out_host,

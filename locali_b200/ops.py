@@ -369,6 +369,21 @@ class MoEKernel:
                                          _event(ev_routed), _event(ev_gateup)), "lmoe_moe_layer_staged")
         return out
 
+    def timed(self, x: torch.Tensor, out: torch.Tensor, ev_router: torch.cuda.Event,
+              ev_experts: torch.cuda.Event, idx: torch.Tensor | None = None) -> torch.Tensor:
+        """The launches of ``__call__`` (AUTO path) with CUDA events at kernel
+        boundaries: after the routing kernel and after the first expert
+        kernel (``lmoe_moe_layer_timed``).  Unlike :meth:`staged`, the routing
+        is not complete at ``ev_router`` when the top-k runs in the expert
+        kernel, so the timed launches are exactly the untimed ones."""
+        flat = self._x(x)
+        T = flat.shape[0]
+        self.ws.ensure(self.workspace_bytes(T))
+        check(lmoe().lmoe_moe_layer_timed(ctypes.byref(self.desc), flat.data_ptr(), T, out.data_ptr(), _ptr(idx),
+                                          None, self.ws.ptr(), self.ws.nbytes, _stream(), _event(ev_router),
+                                          _event(ev_experts)), "lmoe_moe_layer_timed")
+        return out
+
     def route(self, x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
         return route(self._x(x), self.router, self.ws)
 

@@ -67,6 +67,32 @@ def test_fused_topk_matches_finisher(built, scoring, E, k, norm, perm):
             assert set(t2np(idx_f)[0].tolist()) == set(ridx[0].tolist())
 
 
+def test_timed_entry_keeps_the_fused_launches(built):
+    """lmoe_moe_layer_timed records its events at kernel boundaries without
+    switching to the separate finisher: same output and routing as the plain
+    call, and as the staged entry that does switch."""
+    cfg = synth.config("c1", n_experts=256, top_k=6, inter=1024)
+    layer, r, slot, kern = _kern(cfg, seed=21, slot_perm=True)
+    for s in range(3):
+        x = synth.make_tokens(cfg, 1, seed=70 + s, device="cuda")
+        idx_p = torch.full((1, 6), -7, dtype=torch.int32, device="cuda")
+        out_p = kern(x, idx=idx_p).clone()
+        out_t = torch.empty_like(out_p)
+        idx_t = torch.full((1, 6), -7, dtype=torch.int32, device="cuda")
+        e1, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        kern.timed(x, out_t, e1, e2, idx=idx_t)
+        out_s = torch.empty_like(out_p)
+        kern.staged(x, out_s, torch.cuda.Event(), torch.cuda.Event())
+        torch.cuda.synchronize()
+        kern.ws.check()
+        assert torch.equal(out_t, out_p)
+        assert torch.equal(out_s, out_p)
+        assert torch.equal(idx_t, idx_p)
+        assert e0.elapsed_time(e1) >= 0.0 and e1.elapsed_time(e2) > 0.0
+
+
 def test_fused_topk_host_and_static_entries(built):
     """The pinned-host and static entries take the fused path too."""
     cfg = synth.config("c1", n_experts=64, inter=1024)
