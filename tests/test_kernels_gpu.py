@@ -12,7 +12,7 @@ import numpy as np
 import pytest
 import torch
 
-from locali_b200 import ops, synth
+from locali_b200 import _lib, ops, synth
 from oracle import moe_oracle as O
 from oracle.bridge import layer_np, qproj_np, t2np
 
@@ -169,6 +169,47 @@ def test_layer_tiled_matches_oracle(built, name, T):
     again = kern_t(x)
     torch.cuda.synchronize()
     assert torch.equal(again, out_t)
+
+
+@pytest.mark.parametrize("bg,bd,gs,dtype", [
+    (2, 4, 64, torch.bfloat16),
+    (2, 2, 128, torch.float16),
+    (4, 4, 32, torch.float16),
+    (4, 4, 128, torch.bfloat16),
+    (8, 8, 64, torch.bfloat16),
+])
+def test_single_token_geometries(built, bg, bd, gs, dtype):
+    """One token over the pre-tiled copy (the single-token layer kernel where
+    its shared-memory plan fits, else the stream GEMVs) at the bit widths and
+    group sizes it is built for, bf16 and f16: within the layer bar of the
+    oracle and of the row-major path, and repeatable bit for bit."""
+    cfg = synth.config("c1", hidden=2048, n_experts=64, inter=1024, bits_gate=bg, bits_up=bg, bits_down=bd,
+                       group_size=gs)
+    layer = synth.make_layer(cfg, seed=bg * 10 + bd + gs, device="cuda", dtype=dtype)
+    kern = ops.MoEKernel(layer.router, layer.experts, layer.expert_slot, cfg.swiglu_limit, "fused")
+    try:  # the row-major GEMVs do not plan every geometry the tiled path runs
+        kern.workspace_bytes(1)
+    except _lib.LmoeError:
+        kern = None
+    layer.experts.pack_tiles()
+    kern_t = ops.MoEKernel(layer.router, layer.experts, layer.expert_slot, cfg.swiglu_limit, "fused")
+    for s in range(2):
+        x = synth.make_tokens(cfg, 1, seed=90 + s, device="cuda", dtype=dtype)
+        out = kern(x).clone() if kern is not None else None
+        idx = torch.empty((1, cfg.top_k), dtype=torch.int32, device="cuda")
+        out_t = kern_t(x, idx=idx).clone()
+        again = kern_t(x)
+        torch.cuda.synchronize()
+        kern_t.ws.check()
+        act = "f16" if dtype == torch.float16 else "bf16"
+        ref = O.moe_layer(t2np(x), layer_np(layer, dtype=act), acc=np.float32)
+        ok = ~ref["ties"]
+        assert np.array_equal(t2np(idx)[ok], ref["idx"][ok])
+        if ok.all():
+            assert O.rel_l2(t2np(out_t), ref["out"]) < 4e-3
+        if out is not None:
+            assert O.rel_l2(t2np(out_t), t2np(out)) < 4e-3
+        assert torch.equal(again, out_t)
 
 
 @pytest.mark.parametrize("T", [1, 5])
